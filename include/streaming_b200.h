@@ -1,0 +1,174 @@
+/*
+ * streaming_b200.h -- C ABI of the B200 streaming-step runtime.
+ *
+ * This is the drop-in boundary for the reference's per-event hot path,
+ * Stream::Runtime (reference include/Runtime.hpp:7-46, src/cuda/Runtime.cu:164-665).
+ * The reference has no FFI: its C++ Runtime::Impl drives CUDA directly. Here the
+ * C++ Runtime (include/Runtime.hpp in this repo) and any other host language call
+ * these functions instead; every argument is a plain pointer, size or struct.
+ *
+ * Conventions
+ *   - Every function returns ST_OK (0) or a negative ST_ERR_* code; the message
+ *     is then available from st_last_error(handle) (or st_last_error(NULL) for
+ *     a failed st_create). The reference raised std::runtime_error for the same
+ *     conditions (src/cuda/Resources.cuh:9-20, src/cuda/Runtime.cu:178-194, 399-425).
+ *   - One outstanding command per runtime, one submitting thread; not thread
+ *     safe (reference docs/transport.md:14).
+ *   - After a device-side error (ST_ERR_DEVICE_TIMEOUT, ST_ERR_CUDA) the runtime
+ *     only accepts st_destroy.
+ */
+#ifndef STREAMING_B200_H
+#define STREAMING_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ST_ABI_VERSION 1
+
+enum st_status {
+  ST_OK = 0,
+  ST_ERR_INVALID = -1,         /* bad argument, option or model dimension */
+  ST_ERR_UNSUPPORTED = -2,     /* valid in the reference but not provided (cuBLAS backends) */
+  ST_ERR_CUDA = -3,            /* a CUDA runtime call failed */
+  ST_ERR_STOPPED = -4,         /* persistent worker stopped or never started */
+  ST_ERR_EXHAUSTED = -5,       /* mailbox sequence exhausted (last ID reserved for STOP) */
+  ST_ERR_WORKER_EXITED = -6,   /* persistent worker left: max_events or idle budget */
+  ST_ERR_DEVICE_TIMEOUT = -7,  /* a bounded device-side wait gave up */
+  ST_ERR_HOST_TIMEOUT = -8,    /* the host gave up waiting for a completion */
+  ST_ERR_STATE = -9            /* call out of order (e.g. step before st_start) */
+};
+
+/* reference include/Runtime.hpp:7 (Backend). Values match the enum order there. */
+enum st_backend {
+  ST_BACKEND_CUDA = 0,         /* per-phase kernel sequence */
+  ST_BACKEND_GRAPH = 1,        /* the same sequence captured once as a CUDA graph */
+  ST_BACKEND_CUBLAS = 2,       /* rejected: cuBLAS comparator is not provided */
+  ST_BACKEND_CUBLAS_GRAPH = 3, /* rejected */
+  ST_BACKEND_FUSED = 4,        /* one cooperative launch per step */
+  ST_BACKEND_PERSISTENT = 5    /* one resident kernel driven by a mapped host mailbox */
+};
+
+/* Storage precision. 1 is the reference "mixed" mode (fp16 storage,
+ * reference reference/model.py:3-5); 2 is the bf16 variant. Accumulation,
+ * norms and softmax are fp32 in every mode. */
+enum st_mode { ST_MODE_FP32 = 0, ST_MODE_FP16 = 1, ST_MODE_BF16 = 2 };
+
+/* reference include/Model.hpp:12-18 (ModelConfig) + numeric mode + stream count. */
+typedef struct {
+  int layers, width, heads, ffn, window, features;
+  float epsilon;
+  int mode;    /* st_mode */
+  int streams; /* independent streams advanced together by one step; 1 = reference */
+} st_model_desc;
+
+/* reference include/Runtime.hpp:8-19 (RuntimeOptions), same field meaning.
+ * blocks: CTAs in every launch; 0 selects one CTA per SM. vector_matvec and
+ * fused_attention are accepted for compatibility: the kernels here always use
+ * 16-byte weight loads and split-window attention. */
+typedef struct {
+  int backend;                /* st_backend */
+  int blocks;
+  int backoff;                /* device nanosleep / host yield while polling */
+  int mapped;                 /* mapped pinned staging for CUDA/GRAPH backends */
+  int vector_matvec;
+  int fused_attention;
+  uint64_t max_events;        /* persistent: exit after this many RUNs (0 = unbounded) */
+  uint64_t initial_sequence;  /* persistent: first mailbox sequence number */
+  double idle_seconds;        /* persistent: idle budget, (0, 3600] */
+  int device;                 /* CUDA device ordinal */
+} st_options;
+
+typedef struct st_runtime st_runtime;
+
+/* Fills *options with the reference defaults (backend GRAPH, blocks 1,
+ * idle 30 s; reference include/Runtime.hpp:8-19). */
+void st_default_options(st_options* options);
+
+/* Replaces the reference Runtime::Impl constructor's validation and allocation
+ * (reference src/cuda/Runtime.cu:169-271). Allocates all device state, zeroed;
+ * weights follow with st_set_tensor, then st_start. */
+int st_create(const st_model_desc* model, const st_options* options, st_runtime** out);
+
+/* Uploads one checkpoint tensor, float32 values already representable in the
+ * storage type (reference src/cuda/Runtime.cu:231-256 upload). Names as in the
+ * manifest: "input", "final_norm", "score", "layers.<l>.<norm1|norm2|q|k|v|out|gate|up|down>".
+ * count must equal the tensor's element count. */
+int st_set_tensor(st_runtime* rt, const char* name, const float* data, size_t count);
+
+/* Checks that every tensor is present, warms up, captures the graph (GRAPH) or
+ * starts the resident worker (PERSISTENT) (reference src/cuda/Runtime.cu:263-291). */
+int st_start(st_runtime* rt);
+
+/* One event -> one score (reference Runtime::step, src/cuda/Runtime.cu:430-455).
+ * input: features floats in host memory. For streams > 1 use st_step_batch. */
+int st_step(st_runtime* rt, const float* input, float* score);
+
+/* All streams advance by one event: inputs [streams][features], scores [streams],
+ * both host memory. New; the reference runs one stream per runtime. */
+int st_step_batch(st_runtime* rt, const float* inputs, float* scores);
+
+/* Zero every stream's K/V/hidden and position (reference Runtime::reset,
+ * src/cuda/Runtime.cu:457-464). */
+int st_reset(st_runtime* rt);
+
+/* Zero one stream's state only (new; needed once several streams share a step). */
+int st_reset_stream(st_runtime* rt, int stream);
+
+/* STOP the resident worker and join it; idempotent (reference Runtime::stop,
+ * src/cuda/Runtime.cu:466-474). No-op for the other backends. */
+int st_stop(st_runtime* rt);
+
+/* Copy stream `stream`'s state to host: position, keys and values
+ * [layers][heads][window][head_dim] widened to float, hidden [layers][width]
+ * (reference Runtime::snapshot, src/cuda/Runtime.cu:548-568). Any output
+ * pointer may be NULL. */
+int st_snapshot(st_runtime* rt, int stream, uint64_t* position, float* keys,
+                float* values, float* hidden);
+
+/* Replace stream `stream`'s state: position, keys, values ([layers][heads]
+ * [window][head_dim] floats, rounded to the storage type) and hidden
+ * ([layers][width]). New: the reference can only read state. Used for sampled
+ * checking of long runs by state hand-off and for testing far positions. */
+int st_load_state(st_runtime* rt, int stream, uint64_t position, const float* keys,
+                  const float* values, const float* hidden);
+
+/* Device-only timing over a preloaded host trace of `count` events
+ * ([count][streams][features]): resets, then steps every event on the device
+ * and reports microseconds per step from CUDA events (reference
+ * Runtime::deviceTrace, src/cuda/Runtime.cu:596-630). scores ([count][streams])
+ * may be NULL. Stops a PERSISTENT worker first, as the reference does. */
+int st_device_trace(st_runtime* rt, const float* inputs, size_t count, float* scores,
+                    double* us_per_step);
+
+/* Same, but `inputs` is a device pointer already resident in HBM and no score is
+ * copied back; *kernel_launches receives the number of kernels launched. */
+int st_device_trace_resident(st_runtime* rt, const float* device_inputs, size_t count,
+                             double* us_per_step, uint64_t* kernel_launches);
+
+/* JSON description of the runtime: options, grid, kernel resources, layout
+ * (reference Runtime::info, src/cuda/Runtime.cu:570-594). Writes at most
+ * capacity bytes including the terminator; *needed gets the full length. */
+int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed);
+
+/* JSON device probe (reference deviceProbe/probe(), src/cuda/Runtime.cu:134-161). */
+int st_probe(int device, char* json, size_t capacity, size_t* needed);
+
+/* Kernels launched by this runtime since creation (for launch-count reporting). */
+uint64_t st_kernel_launches(const st_runtime* rt);
+
+const char* st_last_error(const st_runtime* rt);
+
+/* Stops the worker, synchronizes and frees everything (reference
+ * src/cuda/Runtime.cu:294-299). NULL is ignored. */
+void st_destroy(st_runtime* rt);
+
+int st_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

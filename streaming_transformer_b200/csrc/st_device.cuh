@@ -1,0 +1,630 @@
+// st_device.cuh -- device side of the B200 streaming step (sm_100a).
+//
+// One event per stream flows through input projection, per layer
+// [RMSNorm, QKV + RoPE + ring insert, split-window attention, out-projection +
+// residual, RMSNorm, gate/up + SwiGLU, down-projection + residual], final
+// RMSNorm and a 1-row score head (reference src/cuda/Primitives.cuh:137-278,
+// src/cpu/Cpu.cpp:59-141). Cast points and op order follow the reference; see
+// each phase below.
+//
+// Work split: every phase spreads its rows over all CTAs (contiguous row
+// ranges, so a CTA's weight slice is one contiguous span of HBM) and each CTA
+// streams its span with 16-byte non-temporal loads, many in flight per thread.
+// Phases are separated by a grid barrier (fused / persistent kernels) or a
+// kernel boundary (per-op and graph backends). Six phases per layer replace the
+// reference's 17 stages: RoPE and ring insert run in the QKV epilogue, SwiGLU in
+// the gate/up epilogue, residuals in the projection epilogues, and RMSNorm is
+// recomputed redundantly by every CTA from the 2-4 KB residual vector.
+//
+// Coherence: weights are the only data read through the non-coherent path
+// (they never change while a kernel runs). Activations, ring slots, partials
+// and positions are written by other CTAs inside the same kernel, so they are
+// read with ld.global.cg (L2 only); the event input may be mapped host memory
+// rewritten between steps and is read with ld.global.cv.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace st {
+
+constexpr int kThreads = 512;               // threads per CTA in every kernel
+constexpr int kWarps = kThreads / 32;
+constexpr int kRowTile = 64;                // GEMV rows per shared-memory tile
+constexpr int kMaxCols = 4096;              // max(width, ffn, features)
+constexpr int kMaxBlocksPerRow = kMaxCols / 4 / 32;  // fp32: 16-byte vectors / 32 lanes
+constexpr int kAttChunk = 32;               // ring slots per attention work item
+constexpr int kMaxLayers = 16;
+constexpr int kUnroll = 8;                  // 16-byte loads in flight per lane
+
+enum ErrorCode : int { kOk = 0, kBarrierTimeout = 1, kAborted = 2 };
+enum Command : int { kRun = 1, kReset = 2, kStop = 3, kPing = 4 };
+
+struct LayerPtrs {
+  const void* norm1;
+  const void* norm2;
+  const void* qkv;     // [3d, d]: q rows, then k rows, then v rows
+  const void* out;     // [d, d]
+  const void* gateup;  // [2F, d]: row 2i = gate_i, row 2i+1 = up_i
+  const void* down;    // [d, F]
+};
+
+// Everything a step needs; passed by value to every kernel.
+struct StepArgs {
+  int layers, width, heads, ffn, window, features, head_dim, streams;
+  float epsilon;
+  int nchunks_max;                    // ceil(window / kAttChunk)
+  const void* input_w;                // [d, features]
+  const void* final_norm;             // [d]
+  const void* score_w;                // [1, d]
+  LayerPtrs layer[kMaxLayers];
+  const float* rope_freq;             // [head_dim / 2]: 10000^(-i/head_dim), host powf
+  void* keys;                         // [S][L][H][W][hd] storage type
+  void* values;
+  float* hidden;                      // [S][L][d]
+  unsigned long long* position;       // [S]
+  const float* input;                 // [S][features] (device or mapped host)
+  float* x;                           // [S][d] residual after each layer
+  float* x2;                          // [S][d] residual after attention
+  float* q;                           // [S][d] rotated, cast query
+  float* part;                        // [S][H][nchunks_max][hd + 2] attention partials
+  float* act;                         // [S][F] SwiGLU output
+  float* score;                       // [S]
+  unsigned long long* bar_counter;    // grid barrier arrivals (monotonic)
+  int* error;                         // first error code, 0 = none (device memory)
+  int* host_error;                    // mapped host mirror of the error word (may be null)
+  unsigned long long bar_timeout_ns;  // bound on any single barrier wait
+};
+
+// ---------------------------------------------------------------- storage types
+template <typename T> struct Storage;
+template <> struct Storage<float> {
+  static constexpr int kVec = 4;
+  __device__ static float load(const float* p, size_t i) { return p[i]; }
+  __device__ static float load_cg(const float* p, size_t i) { return __ldcg(p + i); }
+  __device__ static float round(float v) { return v; }
+  __device__ static void store(float* p, size_t i, float v) { p[i] = v; }
+  __device__ static void unpack(const uint4& u, float* f) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  }
+};
+template <> struct Storage<__half> {
+  static constexpr int kVec = 8;
+  __device__ static float load(const __half* p, size_t i) { return __half2float(p[i]); }
+  __device__ static float load_cg(const __half* p, size_t i) { return __half2float(__ldcg(p + i)); }
+  __device__ static float round(float v) { return __half2float(__float2half_rn(v)); }
+  __device__ static void store(__half* p, size_t i, float v) { p[i] = __float2half_rn(v); }
+  __device__ static void unpack(const uint4& u, float* f) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[k]);
+      float2 t = __half22float2(h);
+      f[2 * k] = t.x; f[2 * k + 1] = t.y;
+    }
+  }
+};
+template <> struct Storage<__nv_bfloat16> {
+  static constexpr int kVec = 8;
+  __device__ static float load(const __nv_bfloat16* p, size_t i) { return __bfloat162float(p[i]); }
+  __device__ static float load_cg(const __nv_bfloat16* p, size_t i) { return __bfloat162float(__ldcg(p + i)); }
+  __device__ static float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+  __device__ static void store(__nv_bfloat16* p, size_t i, float v) { p[i] = __float2bfloat16_rn(v); }
+  __device__ static void unpack(const uint4& u, float* f) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      f[2 * k] = __uint_as_float(w[k] << 16);
+      f[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    }
+  }
+};
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  // Weights are read once per step: skip L1, default L2 policy.
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
+__device__ __forceinline__ unsigned long long ld_cg_u64(const unsigned long long* p) { return __ldcg(p); }
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ int ld_volatile_int(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ void set_error(const StepArgs& a, int code) {
+  if (atomicCAS(a.error, 0, code) == 0 && a.host_error) {
+    *reinterpret_cast<volatile int*>(a.host_error) = code;
+    __threadfence_system();
+  }
+}
+
+// Grid barrier on a monotonically increasing arrival counter. Every CTA keeps
+// the same local epoch count; `base` is the counter value when the launch
+// started. Returns false (and records the error) when the wait exceeds the
+// bound or another CTA already failed; callers then leave the kernel.
+struct GridSync {
+  unsigned long long base;
+  unsigned long long epoch;
+  __device__ bool sync(const StepArgs& a, unsigned long long timeout_ns) {
+    __syncthreads();
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+      epoch += 1;
+      const unsigned long long target = base + epoch * gridDim.x;
+      red_release_gpu_add(a.bar_counter, 1ull);
+      int good = 1;
+      unsigned long long start = 0;
+      unsigned int polls = 0;
+      while (ld_acquire_gpu(a.bar_counter) < target) {
+        if ((++polls & 63u) == 0) {
+          if (ld_volatile_int(a.error) != 0) { good = 0; break; }
+          const unsigned long long now = globaltimer();
+          if (start == 0) start = now;
+          else if (now - start > timeout_ns) { set_error(a, kBarrierTimeout); good = 0; break; }
+        }
+      }
+      ok = good;
+    }
+    __syncthreads();
+    return ok != 0;
+  }
+};
+
+// ---------------------------------------------------------------- shared scratch
+struct alignas(16) Smem {
+  float xs[kMaxCols];                        // GEMV input vector (one stream)
+  float red[kRowTile * kMaxBlocksPerRow];    // per-(row, 32-vector block) partials
+  float rowsum[kRowTile];
+  float warp_scratch[kWarps];
+  float scalar[4];
+};
+
+__device__ __forceinline__ float block_sum(float v, Smem& sm) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) sm.warp_scratch[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (warp == 0) {
+    t = lane < kWarps ? sm.warp_scratch[lane] : 0.f;
+    t = warp_sum(t);
+    if (lane == 0) sm.scalar[0] = t;
+  }
+  __syncthreads();
+  return sm.scalar[0];
+}
+
+// RMSNorm of a residual vector into sm.xs, cast to storage precision
+// (reference src/cpu/Cpu.cpp:43-57: scale = 1/sqrt(mean(x^2)+eps), out = x*scale*g).
+template <typename T>
+__device__ void norm_to_smem(const float* x, const T* gain, int width, float eps, Smem& sm) {
+  float s = 0.f;
+  for (int i = threadIdx.x; i < width; i += kThreads) {
+    const float v = ld_cg(x + i);
+    sm.xs[i] = v;
+    s += v * v;
+  }
+  const float total = block_sum(s, sm);
+  const float scale = 1.0f / sqrtf(total / (float)width + eps);
+  for (int i = threadIdx.x; i < width; i += kThreads)
+    sm.xs[i] = Storage<T>::round(sm.xs[i] * scale * Storage<T>::load(gain, i));
+  __syncthreads();
+}
+
+template <typename T>
+__device__ __forceinline__ float dot_vec(const uint4& w, const float* x) {
+  constexpr int V = Storage<T>::kVec;
+  float f[V];
+  Storage<T>::unpack(w, f);
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < V; k += 4) {
+    const float4 xv = *reinterpret_cast<const float4*>(x + k);
+    acc = fmaf(f[k], xv.x, acc);
+    acc = fmaf(f[k + 1], xv.y, acc);
+    acc = fmaf(f[k + 2], xv.z, acc);
+    acc = fmaf(f[k + 3], xv.w, acc);
+  }
+  return acc;
+}
+
+// rowsum[i] = sum_c W[row0 + i, c] * xs[c] for i < nrows (nrows <= kRowTile),
+// fp32 accumulation in a fixed order (bit-stable run to run). All threads call.
+template <typename T>
+__device__ void gemv_tile(const T* __restrict__ W, int row0, int nrows, int cols, Smem& sm) {
+  constexpr int V = Storage<T>::kVec;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const T* base = W + (size_t)row0 * cols;
+  const bool vec_ok = (cols % V) == 0;
+  const int vpr = cols / V;
+  if (vec_ok && (vpr & 31) == 0) {
+    // 32 consecutive 16-byte vectors of one row per warp block.
+    const int bpr = vpr >> 5;
+    const int nblk = nrows * bpr;
+    for (int b0 = warp; b0 < nblk; b0 += kWarps * kUnroll) {
+      uint4 w[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int blk = b0 + u * kWarps;
+        if (blk < nblk) {
+          const int r = blk / bpr, cb = blk - r * bpr;
+          w[u] = ld_stream(base + (size_t)r * cols + (size_t)((cb << 5) + lane) * V);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int blk = b0 + u * kWarps;
+        if (blk < nblk) {
+          const int r = blk / bpr, cb = blk - r * bpr;
+          float acc = dot_vec<T>(w[u], sm.xs + ((cb << 5) + lane) * V);
+          acc = warp_sum(acc);
+          if (lane == 0) sm.red[blk] = acc;
+          (void)r;
+        }
+      }
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < nrows; r += kThreads) {
+      float s = 0.f;
+      for (int k = 0; k < bpr; ++k) s += sm.red[r * bpr + k];
+      sm.rowsum[r] = s;
+    }
+  } else if (vec_ok && (32 % vpr) == 0) {
+    // Short rows: 32 / vpr rows per warp, one vector per lane.
+    const int rpw = 32 / vpr;
+    const int sub = lane / vpr, c = lane - sub * vpr;
+    for (int r0 = warp * rpw; r0 < nrows; r0 += kWarps * rpw) {
+      const int r = r0 + sub;
+      float acc = 0.f;
+      if (r < nrows) acc = dot_vec<T>(ld_stream(base + (size_t)r * cols + (size_t)c * V), sm.xs + c * V);
+      for (int o = vpr >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (c == 0 && r < nrows) sm.rowsum[r] = acc;
+    }
+  } else if (vec_ok) {
+    for (int r = warp; r < nrows; r += kWarps) {
+      float acc = 0.f;
+      for (int c = lane; c < vpr; c += 32)
+        acc += dot_vec<T>(ld_stream(base + (size_t)r * cols + (size_t)c * V), sm.xs + c * V);
+      acc = warp_sum(acc);
+      if (lane == 0) sm.rowsum[r] = acc;
+    }
+  } else {
+    // Unaligned rows: scalar loads.
+    for (int r = warp; r < nrows; r += kWarps) {
+      float acc = 0.f;
+      for (int c = lane; c < cols; c += 32) acc = fmaf(Storage<T>::load(base, (size_t)r * cols + c), sm.xs[c], acc);
+      acc = warp_sum(acc);
+      if (lane == 0) sm.rowsum[r] = acc;
+    }
+  }
+  __syncthreads();
+}
+
+// Contiguous share [lo, hi) of `units` for this CTA.
+__device__ __forceinline__ void cta_range(int units, int& lo, int& hi) {
+  lo = (int)(((long long)units * blockIdx.x) / gridDim.x);
+  hi = (int)(((long long)units * (blockIdx.x + 1)) / gridDim.x);
+}
+
+// Runs gemv over this CTA's rows [lo*unit, hi*unit) in tiles and calls
+// epi(row, sum) for each row (all threads participate; epi is called by the
+// thread that owns the row within the tile, possibly in pairs).
+template <typename T, typename Epi>
+__device__ void cta_gemv(const T* W, int rows, int cols, int unit, Smem& sm, Epi epi) {
+  int lo, hi;
+  cta_range(rows / unit, lo, hi);
+  const int r_begin = lo * unit, r_end = hi * unit;
+  for (int r0 = r_begin; r0 < r_end; r0 += kRowTile) {
+    const int n = min(kRowTile, r_end - r0);
+    gemv_tile<T>(W, r0, n, cols, sm);
+    epi(r0, n);
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------- phases
+__device__ __forceinline__ unsigned long long stream_position(const StepArgs& a, int s) {
+  return ld_cg_u64(a.position + s);
+}
+
+// x = cast(W_in * input) (reference src/cpu/Cpu.cpp:65).
+template <typename T>
+__device__ void phase_input(const StepArgs& a, const float* input, Smem& sm) {
+  for (int s = 0; s < a.streams; ++s) {
+    for (int i = threadIdx.x; i < a.features; i += kThreads) sm.xs[i] = __ldcv(input + (size_t)s * a.features + i);
+    __syncthreads();
+    float* x = a.x + (size_t)s * a.width;
+    cta_gemv<T>((const T*)a.input_w, a.width, a.features, 1, sm, [&](int r0, int n) {
+      for (int i = threadIdx.x; i < n; i += kThreads) x[r0 + i] = Storage<T>::round(sm.rowsum[i]);
+    });
+  }
+}
+
+// norm1 -> q,k,v = cast(W z) -> RoPE on adjacent pairs, cast -> k,v into ring
+// slot t % W (reference src/cpu/Cpu.cpp:69-96, Primitives.cuh:144-166).
+template <typename T>
+__device__ void phase_qkv(const StepArgs& a, int l, Smem& sm) {
+  const int d = a.width, hd = a.head_dim, H = a.heads, W = a.window;
+  const LayerPtrs& w = a.layer[l];
+  for (int s = 0; s < a.streams; ++s) {
+    const unsigned long long t = stream_position(a, s);
+    const int slot = (int)(t % (unsigned long long)W);
+    norm_to_smem<T>(a.x + (size_t)s * d, (const T*)w.norm1, d, a.epsilon, sm);
+    T* keys = (T*)a.keys + (((size_t)s * a.layers + l) * H) * (size_t)W * hd;
+    T* values = (T*)a.values + (((size_t)s * a.layers + l) * H) * (size_t)W * hd;
+    float* q = a.q + (size_t)s * d;
+    const float tf = (float)t;
+    cta_gemv<T>((const T*)w.qkv, 3 * d, d, 2, sm, [&](int r0, int n) {
+      for (int p = threadIdx.x; p < n / 2; p += kThreads) {
+        const int row = r0 + 2 * p;
+        const int which = row / d, within = row - which * d;
+        const int head = within / hd, dim = within - head * hd;
+        float v0 = Storage<T>::round(sm.rowsum[2 * p]);
+        float v1 = Storage<T>::round(sm.rowsum[2 * p + 1]);
+        if (which < 2) {
+          const float angle = tf * a.rope_freq[dim >> 1];
+          const float co = cosf(angle), si = sinf(angle);
+          const float r0v = v0 * co - v1 * si;
+          const float r1v = v0 * si + v1 * co;
+          v0 = Storage<T>::round(r0v);
+          v1 = Storage<T>::round(r1v);
+        }
+        if (which == 0) {
+          q[within] = v0;
+          q[within + 1] = v1;
+        } else {
+          T* ring = which == 1 ? keys : values;
+          const size_t at = ((size_t)head * W + slot) * hd + dim;
+          Storage<T>::store(ring, at, v0);
+          Storage<T>::store(ring, at + 1, v1);
+        }
+      }
+    });
+  }
+}
+
+// One (stream, head, chunk of <= 32 ring slots) work item per warp: logits
+// q.K/sqrt(hd), chunk max, exp, sum and sum p*V -> partial (m, l, acc[hd]).
+// Physical ring slots [0, valid) are the retained history; softmax does not
+// depend on their order (reference src/cpu/Cpu.cpp:97-110).
+template <typename T, int DPL>
+__device__ void attention_item(const StepArgs& a, int l, int s, int h, int c, int valid) {
+  const int lane = threadIdx.x & 31;
+  const int hd = a.head_dim, W = a.window, H = a.heads;
+  const int j0 = c * kAttChunk;
+  const int nj = min(kAttChunk, valid - j0);
+  const size_t head_base = ((((size_t)s * a.layers + l) * H + h) * (size_t)W) * hd;
+  const T* K = (const T*)a.keys + head_base;
+  const T* Vv = (const T*)a.values + head_base;
+  const float* q = a.q + (size_t)s * a.width + (size_t)h * hd;
+  float score = -INFINITY;
+  if (lane < nj) {
+    const T* krow = K + (size_t)(j0 + lane) * hd;
+    float dot = 0.f;
+    for (int i = 0; i < hd; ++i) dot = fmaf(ld_cg(q + i), Storage<T>::load_cg(krow, i), dot);
+    score = dot / sqrtf((float)hd);
+  }
+  const float m = warp_max(score);
+  const float p = lane < nj ? expf(score - m) : 0.f;
+  const float lsum = warp_sum(p);
+  float acc[DPL];
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) acc[k] = 0.f;
+  for (int j = 0; j < nj; ++j) {
+    const float pj = __shfl_sync(0xffffffffu, p, j);
+    const T* vrow = Vv + (size_t)(j0 + j) * hd;
+#pragma unroll
+    for (int k = 0; k < DPL; ++k) {
+      const int dd = lane + 32 * k;
+      if (dd < hd) acc[k] = fmaf(pj, Storage<T>::load_cg(vrow, dd), acc[k]);
+    }
+  }
+  float* out = a.part + ((((size_t)s * H + h) * a.nchunks_max + c) * (size_t)(hd + 2));
+  if (lane == 0) { out[0] = m; out[1] = lsum; }
+#pragma unroll
+  for (int k = 0; k < DPL; ++k) {
+    const int dd = lane + 32 * k;
+    if (dd < hd) out[2 + dd] = acc[k];
+  }
+}
+
+template <typename T>
+__device__ void phase_attention(const StepArgs& a, int l) {
+  const int warp = threadIdx.x >> 5;
+  const int gw = blockIdx.x * kWarps + warp, nw = gridDim.x * kWarps;
+  const int H = a.heads, C = a.nchunks_max;
+  const int items = a.streams * H * C;
+  const int dpl = (a.head_dim + 31) / 32;
+  for (int it = gw; it < items; it += nw) {
+    const int s = it / (H * C), rem = it - s * H * C;
+    const int h = rem / C, c = rem - h * C;
+    const unsigned long long t = stream_position(a, s);
+    const int valid = t + 1 < (unsigned long long)a.window ? (int)(t + 1) : a.window;
+    if (c * kAttChunk >= valid) continue;
+    if (dpl <= 1) attention_item<T, 1>(a, l, s, h, c, valid);
+    else if (dpl <= 2) attention_item<T, 2>(a, l, s, h, c, valid);
+    else if (dpl <= 4) attention_item<T, 4>(a, l, s, h, c, valid);
+    else if (dpl <= 8) attention_item<T, 8>(a, l, s, h, c, valid);
+    else attention_item<T, 32>(a, l, s, h, c, valid);
+  }
+}
+
+// Merge the chunk partials of one stream into sm.xs = cast(attention) (all threads).
+template <typename T>
+__device__ void merge_attention(const StepArgs& a, int s, Smem& sm) {
+  const int hd = a.head_dim, H = a.heads, C = a.nchunks_max;
+  const unsigned long long t = stream_position(a, s);
+  const int valid = t + 1 < (unsigned long long)a.window ? (int)(t + 1) : a.window;
+  const int nc = (valid + kAttChunk - 1) / kAttChunk;
+  const float* part = a.part + (size_t)s * H * C * (hd + 2);
+  for (int e = threadIdx.x; e < a.width; e += kThreads) {
+    const int h = e / hd, dd = e - h * hd;
+    const float* ph = part + (size_t)h * C * (hd + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nc; ++c) M = fmaxf(M, ld_cg(ph + (size_t)c * (hd + 2)));
+    float L = 0.f, acc = 0.f;
+    for (int c = 0; c < nc; ++c) {
+      const float* pc = ph + (size_t)c * (hd + 2);
+      const float scale = expf(ld_cg(pc) - M);
+      L = fmaf(ld_cg(pc + 1), scale, L);
+      acc = fmaf(ld_cg(pc + 2 + dd), scale, acc);
+    }
+    sm.xs[e] = Storage<T>::round(acc / L);
+  }
+  __syncthreads();
+}
+
+// attention -> cast(W_out a) -> x2 = cast(x + out) (reference src/cpu/Cpu.cpp:111-118).
+template <typename T>
+__device__ void phase_out(const StepArgs& a, int l, Smem& sm) {
+  const int d = a.width;
+  for (int s = 0; s < a.streams; ++s) {
+    merge_attention<T>(a, s, sm);
+    const float* x = a.x + (size_t)s * d;
+    float* x2 = a.x2 + (size_t)s * d;
+    cta_gemv<T>((const T*)a.layer[l].out, d, d, 1, sm, [&](int r0, int n) {
+      for (int i = threadIdx.x; i < n; i += kThreads)
+        x2[r0 + i] = Storage<T>::round(ld_cg(x + r0 + i) + Storage<T>::round(sm.rowsum[i]));
+    });
+  }
+}
+
+// norm2 -> gate, up = cast(W z) -> act = cast(silu(gate) * up)
+// (reference src/cpu/Cpu.cpp:120-126).
+template <typename T>
+__device__ void phase_ffn_in(const StepArgs& a, int l, Smem& sm) {
+  const int d = a.width, F = a.ffn;
+  const LayerPtrs& w = a.layer[l];
+  for (int s = 0; s < a.streams; ++s) {
+    norm_to_smem<T>(a.x2 + (size_t)s * d, (const T*)w.norm2, d, a.epsilon, sm);
+    float* act = a.act + (size_t)s * F;
+    cta_gemv<T>((const T*)w.gateup, 2 * F, d, 2, sm, [&](int r0, int n) {
+      for (int p = threadIdx.x; p < n / 2; p += kThreads) {
+        const float g = Storage<T>::round(sm.rowsum[2 * p]);
+        const float u = Storage<T>::round(sm.rowsum[2 * p + 1]);
+        act[(r0 >> 1) + p] = Storage<T>::round((g / (1.0f + expf(-g))) * u);
+      }
+    });
+  }
+}
+
+// act -> cast(W_down act) -> x = cast(x2 + down); hidden[l] = x
+// (reference src/cpu/Cpu.cpp:128-134).
+template <typename T>
+__device__ void phase_ffn_out(const StepArgs& a, int l, Smem& sm) {
+  const int d = a.width, F = a.ffn;
+  for (int s = 0; s < a.streams; ++s) {
+    const float* act = a.act + (size_t)s * F;
+    for (int i = threadIdx.x; i < F; i += kThreads) sm.xs[i] = ld_cg(act + i);
+    __syncthreads();
+    const float* x2 = a.x2 + (size_t)s * d;
+    float* x = a.x + (size_t)s * d;
+    float* hidden = a.hidden + ((size_t)s * a.layers + l) * d;
+    cta_gemv<T>((const T*)a.layer[l].down, d, F, 1, sm, [&](int r0, int n) {
+      for (int i = threadIdx.x; i < n; i += kThreads) {
+        const float v = Storage<T>::round(ld_cg(x2 + r0 + i) + Storage<T>::round(sm.rowsum[i]));
+        x[r0 + i] = v;
+        hidden[r0 + i] = v;
+      }
+    });
+  }
+}
+
+// Final norm and score head without a cast, then position++ (CTA 0 only;
+// reference src/cpu/Cpu.cpp:136-140, Primitives.cuh:270-276).
+template <typename T>
+__device__ void phase_final(const StepArgs& a, Smem& sm) {
+  if (blockIdx.x != 0) return;
+  for (int s = 0; s < a.streams; ++s) {
+    norm_to_smem<T>(a.x + (size_t)s * a.width, (const T*)a.final_norm, a.width, a.epsilon, sm);
+    // one row: block-wide dot product
+    float acc = 0.f;
+    for (int i = threadIdx.x; i < a.width; i += kThreads)
+      acc = fmaf(Storage<T>::load((const T*)a.score_w, i), sm.xs[i], acc);
+    const float total = block_sum(acc, sm);
+    if (threadIdx.x == 0) a.score[s] = total;
+    __syncthreads();
+  }
+  for (int s = threadIdx.x; s < a.streams; s += kThreads) a.position[s] = ld_cg_u64(a.position + s) + 1;
+}
+
+// Zero K/V/hidden and position for streams [s0, s1) (reference
+// src/cuda/Primitives.cuh:280-292), grid-stride over all CTAs.
+template <typename T>
+__device__ void reset_streams(const StepArgs& a, int s0, int s1) {
+  const size_t per_stream = (size_t)a.layers * a.width * a.window;
+  const size_t begin = (size_t)s0 * per_stream, end = (size_t)s1 * per_stream;
+  const size_t stride = (size_t)gridDim.x * kThreads;
+  for (size_t i = begin + (size_t)blockIdx.x * kThreads + threadIdx.x; i < end; i += stride) {
+    Storage<T>::store((T*)a.keys, i, 0.f);
+    Storage<T>::store((T*)a.values, i, 0.f);
+  }
+  const size_t hb = (size_t)s0 * a.layers * a.width, he = (size_t)s1 * a.layers * a.width;
+  for (size_t i = hb + (size_t)blockIdx.x * kThreads + threadIdx.x; i < he; i += stride) a.hidden[i] = 0.f;
+  if (blockIdx.x == 0)
+    for (int s = s0 + threadIdx.x; s < s1; s += kThreads) a.position[s] = 0ull;
+}
+
+// One full step across the grid, barriers between phases. Returns false if a
+// barrier gave up (the error word is set).
+template <typename T>
+__device__ bool forward(const StepArgs& a, const float* input, GridSync& gs, Smem& sm) {
+  phase_input<T>(a, input, sm);
+  if (!gs.sync(a, a.bar_timeout_ns)) return false;
+  for (int l = 0; l < a.layers; ++l) {
+    phase_qkv<T>(a, l, sm);
+    if (!gs.sync(a, a.bar_timeout_ns)) return false;
+    phase_attention<T>(a, l);
+    if (!gs.sync(a, a.bar_timeout_ns)) return false;
+    phase_out<T>(a, l, sm);
+    if (!gs.sync(a, a.bar_timeout_ns)) return false;
+    phase_ffn_in<T>(a, l, sm);
+    if (!gs.sync(a, a.bar_timeout_ns)) return false;
+    phase_ffn_out<T>(a, l, sm);
+    if (!gs.sync(a, a.bar_timeout_ns)) return false;
+  }
+  phase_final<T>(a, sm);
+  return true;
+}
+
+// Number of grid barriers forward() executes.
+__host__ __device__ inline int forward_barriers(int layers) { return 1 + 5 * layers; }
+
+}  // namespace st

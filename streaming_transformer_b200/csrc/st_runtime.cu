@@ -1,0 +1,963 @@
+// st_runtime.cu -- host runtime behind the C ABI (include/streaming_b200.h).
+//
+// Owns every device and pinned buffer of one runtime and drives the kernels of
+// st_kernels.cuh for the five backends. It takes the place of the reference's
+// Runtime::Impl (reference src/cuda/Runtime.cu:164-665) behind a plain C ABI.
+//
+// Device layout (one runtime, S streams):
+//   weights slab   every tensor 256-byte aligned, in storage precision; per
+//                  layer q/k/v are fused into one [3d, d] matrix and gate/up are
+//                  interleaved row by row into [2F, d] so each CTA's row range
+//                  is one contiguous span and pairs (RoPE, SwiGLU) stay together
+//   state          K, V [S][L][H][W][hd] storage precision; hidden [S][L][d]
+//                  fp32; position u64 [S]
+//   scratch        fp32 activations, attention partials, barrier counter,
+//                  error word, RoPE frequency table
+//   mapped pinned  mailbox (request/completion/exited on separate 64-byte
+//                  lines), input [S][features], scores [S]
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <limits>
+#include <map>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/streaming_b200.h"
+#include "st_kernels.cuh"
+
+using namespace st;
+
+namespace {
+
+thread_local std::string g_create_error;
+
+struct TensorSlot {
+  size_t offset;      // bytes into the weights slab (region start)
+  int rows, cols;     // logical tensor shape (1-D tensors: rows = 1)
+  int row_step;       // destination row = row * row_step + row_offset
+  int row_offset;
+  int index;          // presence flag index
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Exact widening of binary16 / bfloat16 bit patterns for snapshots.
+float half_bits_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const uint32_t exp = (h >> 10) & 0x1fu, man = h & 0x3ffu;
+  uint32_t bits;
+  if (exp == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {  // subnormal: value = man * 2^-24
+      float v = (float)man * (1.0f / 16777216.0f);
+      std::memcpy(&bits, &v, 4);
+      bits |= sign;
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7f800000u | (man << 13);
+  } else {
+    bits = sign | ((exp + 112u) << 23) | (man << 13);
+  }
+  float out;
+  std::memcpy(&out, &bits, 4);
+  return out;
+}
+float bf16_bits_to_float(uint16_t h) {
+  uint32_t bits = (uint32_t)h << 16;
+  float out;
+  std::memcpy(&out, &bits, 4);
+  return out;
+}
+
+template <typename T>
+__global__ void k_convert(const float* src, T* dst, int rows, int cols, int row_step, int row_offset) {
+  const size_t n = (size_t)rows * cols;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / cols, c = i - r * cols;
+    Storage<T>::store(dst, ((size_t)r * row_step + row_offset) * cols + c, src[i]);
+  }
+}
+
+}  // namespace
+
+struct st_runtime {
+  st_model_desc desc{};
+  st_options opt{};
+  int device = 0;
+  int sms = 0;
+  int grid = 1;
+  int legal_blocks = 1;
+  size_t elem = 4;
+  cudaStream_t stream = nullptr;
+  cudaStream_t aux = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
+
+  char* weights = nullptr;
+  size_t weights_bytes = 0;
+  std::map<std::string, TensorSlot> slots;
+  std::vector<char> have;
+
+  char* state = nullptr;
+  size_t state_bytes = 0;
+  char* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  size_t kv_bytes_per_tensor = 0;
+
+  Mailbox* mb_h = nullptr;
+  Mailbox* mb_d = nullptr;
+  float* in_h = nullptr;
+  float* in_d = nullptr;   // device alias of in_h
+  float* out_h = nullptr;
+  float* out_d = nullptr;  // device alias of out_h
+  float* dev_input = nullptr;
+  float* dev_score = nullptr;
+  Control* control = nullptr;
+
+  StepArgs args{};
+  unsigned long long bar_base = 0;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t graph_exec = nullptr;
+
+  bool started = false;
+  bool running = false;  // persistent worker resident
+  bool failed = false;
+  uint64_t sequence = 0;
+  uint64_t launches = 0;
+  std::string error;
+
+  int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    error = buf;
+    if (code == ST_ERR_CUDA || code == ST_ERR_DEVICE_TIMEOUT) failed = true;
+    return code;
+  }
+  int cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return ST_OK;
+    return fail(ST_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  }
+};
+
+#define ST_TRY(expr)                                  \
+  do {                                                \
+    int _st = (expr);                                 \
+    if (_st != ST_OK) return _st;                     \
+  } while (0)
+#define ST_CUDA(rt, expr) ST_TRY((rt)->cuda((expr), #expr))
+
+namespace {
+
+int forward_barrier_count(const st_runtime* rt) { return forward_barriers(rt->desc.layers); }
+
+template <typename T>
+struct Kernels {
+  static const void* persistent() { return (const void*)k_persistent<T>; }
+  static const void* fused() { return (const void*)k_fused<T>; }
+  static const void* trace() { return (const void*)k_trace<T>; }
+};
+
+const void* persistent_fn(const st_runtime* rt) {
+  switch (rt->desc.mode) {
+    case ST_MODE_FP16: return Kernels<__half>::persistent();
+    case ST_MODE_BF16: return Kernels<__nv_bfloat16>::persistent();
+    default: return Kernels<float>::persistent();
+  }
+}
+
+template <typename T>
+int launch_sequence_t(st_runtime* rt, const StepArgs& a) {
+  const dim3 g(rt->grid), b(kThreads);
+  cudaStream_t s = rt->stream;
+  k_input<T><<<g, b, 0, s>>>(a);
+  for (int l = 0; l < rt->desc.layers; ++l) {
+    k_qkv<T><<<g, b, 0, s>>>(a, l);
+    k_attention<T><<<g, b, 0, s>>>(a, l);
+    k_out<T><<<g, b, 0, s>>>(a, l);
+    k_ffn_in<T><<<g, b, 0, s>>>(a, l);
+    k_ffn_out<T><<<g, b, 0, s>>>(a, l);
+  }
+  k_final<T><<<dim3(1), b, 0, s>>>(a);
+  rt->launches += 2 + 5ull * rt->desc.layers;
+  return rt->cuda(cudaGetLastError(), "per-op launch");
+}
+
+int launch_sequence(st_runtime* rt, const StepArgs& a) {
+  switch (rt->desc.mode) {
+    case ST_MODE_FP16: return launch_sequence_t<__half>(rt, a);
+    case ST_MODE_BF16: return launch_sequence_t<__nv_bfloat16>(rt, a);
+    default: return launch_sequence_t<float>(rt, a);
+  }
+}
+
+template <typename T>
+int launch_reset_t(st_runtime* rt, int s0, int s1) {
+  k_reset<T><<<rt->grid, kThreads, 0, rt->stream>>>(rt->args, s0, s1);
+  rt->launches += 1;
+  return rt->cuda(cudaGetLastError(), "reset launch");
+}
+
+int launch_reset(st_runtime* rt, int s0, int s1) {
+  switch (rt->desc.mode) {
+    case ST_MODE_FP16: return launch_reset_t<__half>(rt, s0, s1);
+    case ST_MODE_BF16: return launch_reset_t<__nv_bfloat16>(rt, s0, s1);
+    default: return launch_reset_t<float>(rt, s0, s1);
+  }
+}
+
+int launch_cooperative(st_runtime* rt, const void* fn, void** params) {
+  cudaError_t e = cudaLaunchCooperativeKernel(fn, dim3(rt->grid), dim3(kThreads), params, 0, rt->stream);
+  rt->launches += 1;
+  return rt->cuda(e, "cooperative launch");
+}
+
+template <typename T>
+int launch_fused_t(st_runtime* rt, StepArgs a) {
+  unsigned long long base = rt->bar_base;
+  void* params[] = {&a, &base};
+  ST_TRY(launch_cooperative(rt, (const void*)k_fused<T>, params));
+  rt->bar_base += (unsigned long long)forward_barrier_count(rt) * rt->grid;
+  return ST_OK;
+}
+
+int launch_fused(st_runtime* rt, const StepArgs& a) {
+  switch (rt->desc.mode) {
+    case ST_MODE_FP16: return launch_fused_t<__half>(rt, a);
+    case ST_MODE_BF16: return launch_fused_t<__nv_bfloat16>(rt, a);
+    default: return launch_fused_t<float>(rt, a);
+  }
+}
+
+template <typename T>
+int launch_trace_t(st_runtime* rt, StepArgs a, const float* inputs, unsigned long long count, float* scores) {
+  unsigned long long base = rt->bar_base;
+  void* params[] = {&a, &inputs, &count, &scores, &base};
+  ST_TRY(launch_cooperative(rt, (const void*)k_trace<T>, params));
+  rt->bar_base += count * (unsigned long long)(forward_barrier_count(rt) + 1) * rt->grid;
+  return ST_OK;
+}
+
+int launch_trace(st_runtime* rt, const StepArgs& a, const float* inputs, unsigned long long count, float* scores) {
+  switch (rt->desc.mode) {
+    case ST_MODE_FP16: return launch_trace_t<__half>(rt, a, inputs, count, scores);
+    case ST_MODE_BF16: return launch_trace_t<__nv_bfloat16>(rt, a, inputs, count, scores);
+    default: return launch_trace_t<float>(rt, a, inputs, count, scores);
+  }
+}
+
+// Host-side check of the error word mirrored into mapped memory.
+int check_device_error(st_runtime* rt) {
+  const int e = __atomic_load_n(&rt->mb_h->error, __ATOMIC_ACQUIRE);
+  if (e == kBarrierTimeout) return rt->fail(ST_ERR_DEVICE_TIMEOUT, "device grid barrier wait exceeded its bound");
+  if (e != 0) return rt->fail(ST_ERR_DEVICE_TIMEOUT, "device error code %d", e);
+  return ST_OK;
+}
+
+// Load every kernel of this mode before a resident worker starts: lazy module
+// loading of a cold kernel can synchronize the context, which would wait for a
+// worker that is itself waiting for the host (reference src/cuda/Runtime.cu:288-290).
+template <typename T>
+int preload_t(st_runtime* rt) {
+  const void* fns[] = {(const void*)k_input<T>, (const void*)k_qkv<T>, (const void*)k_attention<T>,
+                       (const void*)k_out<T>, (const void*)k_ffn_in<T>, (const void*)k_ffn_out<T>,
+                       (const void*)k_final<T>, (const void*)k_reset<T>, (const void*)k_fused<T>,
+                       (const void*)k_trace<T>, (const void*)k_persistent<T>, (const void*)k_convert<T>};
+  for (const void* f : fns) {
+    cudaFuncAttributes fa{};
+    ST_CUDA(rt, cudaFuncGetAttributes(&fa, f));
+  }
+  return ST_OK;
+}
+
+int preload(st_runtime* rt) {
+  switch (rt->desc.mode) {
+    case ST_MODE_FP16: return preload_t<__half>(rt);
+    case ST_MODE_BF16: return preload_t<__nv_bfloat16>(rt);
+    default: return preload_t<float>(rt);
+  }
+}
+
+int start_persistent(st_runtime* rt) {
+  ST_CUDA(rt, cudaMemsetAsync(rt->control, 0, sizeof(Control), rt->stream));
+  std::memset((void*)rt->mb_h, 0, sizeof(Mailbox));
+  rt->sequence = rt->opt.initial_sequence;
+  __atomic_store_n(&rt->mb_h->request, rt->sequence, __ATOMIC_RELEASE);
+  __atomic_store_n(&rt->mb_h->completion, rt->sequence, __ATOMIC_RELEASE);
+  PersistArgs p{};
+  p.mailbox = rt->mb_d;
+  p.max_events = rt->opt.max_events;
+  p.initial_sequence = rt->opt.initial_sequence;
+  p.idle_ns = (unsigned long long)(rt->opt.idle_seconds * 1e9);
+  p.dispatch_timeout_ns = p.idle_ns + 10ull * 1000000000ull;
+  p.control = rt->control;
+  p.backoff = rt->opt.backoff;
+  StepArgs a = rt->args;
+  a.input = rt->in_d;
+  a.score = rt->out_d;
+  unsigned long long base = rt->bar_base;
+  void* params[] = {&a, &p, &base};
+  ST_TRY(launch_cooperative(rt, persistent_fn(rt), params));
+  rt->running = true;
+  return ST_OK;
+}
+
+// After the resident worker has left: join it and restart barrier accounting.
+int join_persistent(st_runtime* rt) {
+  rt->running = false;
+  ST_CUDA(rt, cudaStreamSynchronize(rt->stream));
+  ST_CUDA(rt, cudaMemsetAsync(rt->args.bar_counter, 0, sizeof(unsigned long long), rt->stream));
+  ST_CUDA(rt, cudaStreamSynchronize(rt->stream));
+  rt->bar_base = 0;
+  return check_device_error(rt);
+}
+
+// reference src/cuda/Runtime.cu:398-428
+int command(st_runtime* rt, int cmd, int arg) {
+  if (!rt->running) return rt->fail(ST_ERR_STOPPED, "Persistent runtime is stopped");
+  const uint64_t maximum = std::numeric_limits<uint64_t>::max();
+  if (rt->sequence == maximum || (rt->sequence == maximum - 1 && cmd != kStop))
+    return rt->fail(ST_ERR_EXHAUSTED, "Sequence exhausted; create a new runtime before wraparound");
+  if (__atomic_load_n(&rt->mb_h->exited, __ATOMIC_ACQUIRE)) {
+    int st = join_persistent(rt);
+    if (st != ST_OK) return st;
+    return rt->fail(ST_ERR_WORKER_EXITED, "Persistent worker exited: finite-event or idle budget reached");
+  }
+  rt->mb_h->command = cmd;
+  rt->mb_h->arg = arg;
+  // Input and command are written before the request is published.
+  __atomic_store_n(&rt->mb_h->request, ++rt->sequence, __ATOMIC_RELEASE);
+  const auto start = std::chrono::steady_clock::now();
+  uint64_t polls = 0;
+  while (__atomic_load_n(&rt->mb_h->completion, __ATOMIC_ACQUIRE) != rt->sequence) {
+    if (rt->opt.backoff) std::this_thread::yield();
+    if ((++polls & 0xffff) == 0) {
+      if (__atomic_load_n(&rt->mb_h->exited, __ATOMIC_ACQUIRE) || cudaStreamQuery(rt->stream) != cudaErrorNotReady) {
+        int st = join_persistent(rt);
+        if (st != ST_OK) return st;
+        return rt->fail(ST_ERR_WORKER_EXITED, "Persistent worker exited before completion");
+      }
+      const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count();
+      if (waited > rt->opt.idle_seconds + 30)
+        return rt->fail(ST_ERR_HOST_TIMEOUT, "Persistent response timeout");
+    }
+  }
+  return ST_OK;
+}
+
+int validate_desc(const st_model_desc* m) {
+  // reference src/runtime/Model.cpp:22-29 plus the stream count and mode.
+  if (m->layers < 1 || m->layers > 16 || m->width < 1 || m->width > 1024 || m->heads < 1 ||
+      m->width % m->heads || (m->width / m->heads) % 2 || m->ffn < 1 || m->ffn > 4096 ||
+      m->window < 1 || m->window > 4096 || m->features < 1 || m->features > 1024 ||
+      !std::isfinite(m->epsilon) || m->epsilon <= 0)
+    return 0;
+  if (m->mode < ST_MODE_FP32 || m->mode > ST_MODE_BF16) return 0;
+  if (m->streams < 1) return 0;
+  return 1;
+}
+
+int graph_capture(st_runtime* rt) {
+  ST_CUDA(rt, cudaStreamBeginCapture(rt->stream, cudaStreamCaptureModeThreadLocal));
+  const uint64_t before = rt->launches;
+  int st = launch_sequence(rt, rt->args);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(rt->stream, &g);
+  if (st != ST_OK) return st;
+  ST_TRY(rt->cuda(e, "cudaStreamEndCapture"));
+  rt->graph = g;
+  ST_CUDA(rt, cudaGraphInstantiate(&rt->graph_exec, g, 0));
+  rt->launches = before;  // captured launches are counted when the graph runs
+  return ST_OK;
+}
+
+int run_step_nonpersistent(st_runtime* rt) {
+  const size_t in_bytes = (size_t)rt->desc.streams * rt->desc.features * sizeof(float);
+  const size_t out_bytes = (size_t)rt->desc.streams * sizeof(float);
+  if (!rt->opt.mapped)
+    ST_CUDA(rt, cudaMemcpyAsync(rt->dev_input, rt->in_h, in_bytes, cudaMemcpyHostToDevice, rt->stream));
+  if (rt->opt.backend == ST_BACKEND_GRAPH) {
+    ST_CUDA(rt, cudaGraphLaunch(rt->graph_exec, rt->stream));
+    rt->launches += 2 + 5ull * rt->desc.layers;
+  } else if (rt->opt.backend == ST_BACKEND_FUSED) {
+    ST_TRY(launch_fused(rt, rt->args));
+  } else {
+    ST_TRY(launch_sequence(rt, rt->args));
+  }
+  if (!rt->opt.mapped)
+    ST_CUDA(rt, cudaMemcpyAsync(rt->out_h, rt->dev_score, out_bytes, cudaMemcpyDeviceToHost, rt->stream));
+  ST_CUDA(rt, cudaStreamSynchronize(rt->stream));
+  return check_device_error(rt);
+}
+
+std::string json_escape(const std::string& s) {
+  std::string o;
+  for (char c : s) {
+    if (c == '"' || c == '\\') { o += '\\'; o += c; }
+    else if ((unsigned char)c < 0x20) { char b[8]; snprintf(b, sizeof b, "\\u%04x", c); o += b; }
+    else o += c;
+  }
+  return o;
+}
+
+int copy_json(const std::string& s, char* json, size_t capacity, size_t* needed) {
+  if (needed) *needed = s.size() + 1;
+  if (json && capacity) {
+    const size_t n = std::min(capacity - 1, s.size());
+    std::memcpy(json, s.data(), n);
+    json[n] = '\0';
+  }
+  return ST_OK;
+}
+
+std::string probe_json(int device, int* status) {
+  *status = ST_OK;
+  cudaDeviceProp p{};
+  int driver = 0, runtime = 0;
+  if (cudaGetDeviceProperties(&p, device) != cudaSuccess || cudaDriverGetVersion(&driver) != cudaSuccess ||
+      cudaRuntimeGetVersion(&runtime) != cudaSuccess) {
+    *status = ST_ERR_CUDA;
+    return "{}";
+  }
+  auto attr = [&](cudaDeviceAttr a) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, a, device);
+    return v;
+  };
+  char bus[32] = {0};
+  cudaDeviceGetPCIBusId(bus, sizeof bus, device);
+  std::ostringstream o;
+  o << "{\"gpu\":\"" << json_escape(p.name) << "\",\"device\":" << device << ",\"compute_major\":" << p.major
+    << ",\"compute_minor\":" << p.minor << ",\"sm_count\":" << p.multiProcessorCount
+    << ",\"registers_per_sm\":" << p.regsPerMultiprocessor << ",\"shared_bytes_per_sm\":" << p.sharedMemPerMultiprocessor
+    << ",\"shared_bytes_per_block\":" << p.sharedMemPerBlock << ",\"global_bytes\":" << p.totalGlobalMem
+    << ",\"l2_bytes\":" << p.l2CacheSize << ",\"pci_bus\":\"" << bus << "\""
+    << ",\"clock_khz\":" << attr(cudaDevAttrClockRate) << ",\"memory_clock_khz\":" << attr(cudaDevAttrMemoryClockRate)
+    << ",\"driver_version\":" << driver << ",\"runtime_version\":" << runtime
+    << ",\"nvcc\":" << (__CUDACC_VER_MAJOR__ * 1000 + __CUDACC_VER_MINOR__ * 10 + __CUDACC_VER_BUILD__)
+    << ",\"build_cuda_architectures\":\"100a\""
+    << ",\"kernel_timeout\":" << attr(cudaDevAttrKernelExecTimeout)
+    << ",\"cooperative_launch\":" << attr(cudaDevAttrCooperativeLaunch)
+    << ",\"can_map_host\":" << attr(cudaDevAttrCanMapHostMemory)
+    << ",\"unified_addressing\":" << attr(cudaDevAttrUnifiedAddressing)
+    << ",\"host_native_atomic_supported\":" << attr(cudaDevAttrHostNativeAtomicSupported)
+    << ",\"cpu_logical_count\":" << std::thread::hardware_concurrency() << ",\"os\":\"Linux\"}";
+  return o.str();
+}
+
+}  // namespace
+
+extern "C" {
+
+int st_abi_version(void) { return ST_ABI_VERSION; }
+
+void st_default_options(st_options* o) {
+  if (!o) return;
+  std::memset(o, 0, sizeof *o);
+  o->backend = ST_BACKEND_GRAPH;
+  o->blocks = 1;
+  o->idle_seconds = 30;
+}
+
+const char* st_last_error(const st_runtime* rt) { return rt ? rt->error.c_str() : g_create_error.c_str(); }
+
+uint64_t st_kernel_launches(const st_runtime* rt) { return rt ? rt->launches : 0; }
+
+int st_create(const st_model_desc* model, const st_options* options, st_runtime** out) {
+  if (!model || !options || !out) { g_create_error = "null argument"; return ST_ERR_INVALID; }
+  *out = nullptr;
+  if (!validate_desc(model)) { g_create_error = "Invalid or unsupported model dimensions"; return ST_ERR_INVALID; }
+  const st_options& o = *options;
+  if (o.backend < ST_BACKEND_CUDA || o.backend > ST_BACKEND_PERSISTENT) { g_create_error = "Unknown backend"; return ST_ERR_INVALID; }
+  if (o.backend == ST_BACKEND_CUBLAS || o.backend == ST_BACKEND_CUBLAS_GRAPH) {
+    g_create_error = "cuBLAS backends are not provided by the B200 runtime";
+    return ST_ERR_UNSUPPORTED;
+  }
+  // reference src/cuda/Runtime.cu:178-183
+  if (o.blocks < 0 || !(o.idle_seconds > 0) || o.idle_seconds > 3600) {
+    g_create_error = "Invalid blocks or idle budget";
+    return ST_ERR_INVALID;
+  }
+  if (o.initial_sequence >= std::numeric_limits<uint64_t>::max() - 1) {
+    g_create_error = "Initial sequence must leave room for RUN and STOP";
+    return ST_ERR_INVALID;
+  }
+  auto* rt = new st_runtime();
+  rt->desc = *model;
+  rt->opt = o;
+  rt->device = o.device;
+  auto bail = [&](int code) {
+    g_create_error = rt->error;
+    st_destroy(rt);
+    return code;
+  };
+  if (rt->cuda(cudaSetDevice(rt->device), "cudaSetDevice") != ST_OK) return bail(ST_ERR_CUDA);
+  cudaDeviceProp prop{};
+  if (rt->cuda(cudaGetDeviceProperties(&prop, rt->device), "cudaGetDeviceProperties") != ST_OK) return bail(ST_ERR_CUDA);
+  if (prop.major != 10) {
+    rt->fail(ST_ERR_UNSUPPORTED, "This build targets sm_100a (B200); device is compute %d.%d", prop.major, prop.minor);
+    return bail(ST_ERR_UNSUPPORTED);
+  }
+  int can_map = 0, uva = 0, coop = 0;
+  cudaDeviceGetAttribute(&can_map, cudaDevAttrCanMapHostMemory, rt->device);
+  cudaDeviceGetAttribute(&uva, cudaDevAttrUnifiedAddressing, rt->device);
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, rt->device);
+  if (!can_map || !uva) {
+    rt->fail(ST_ERR_UNSUPPORTED, "Mapped communication requires mapped host memory and UVA");
+    return bail(ST_ERR_UNSUPPORTED);
+  }
+  rt->sms = prop.multiProcessorCount;
+  const st_model_desc& m = rt->desc;
+  rt->elem = m.mode == ST_MODE_FP32 ? 4 : 2;
+  // Cooperative capacity from the compiled kernels (reference src/cuda/Runtime.cu:306-314).
+  int per_sm = 0, per_sm_fused = 0, per_sm_trace = 0;
+  const void* fk = m.mode == ST_MODE_FP16 ? Kernels<__half>::fused() : m.mode == ST_MODE_BF16 ? Kernels<__nv_bfloat16>::fused() : Kernels<float>::fused();
+  const void* tk = m.mode == ST_MODE_FP16 ? Kernels<__half>::trace() : m.mode == ST_MODE_BF16 ? Kernels<__nv_bfloat16>::trace() : Kernels<float>::trace();
+  if (rt->cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, persistent_fn(rt), kThreads, 0), "occupancy") != ST_OK ||
+      rt->cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_fused, fk, kThreads, 0), "occupancy") != ST_OK ||
+      rt->cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_trace, tk, kThreads, 0), "occupancy") != ST_OK)
+    return bail(ST_ERR_CUDA);
+  rt->legal_blocks = coop ? std::min(per_sm, std::min(per_sm_fused, per_sm_trace)) * rt->sms : 1;
+  rt->grid = o.blocks == 0 ? rt->sms : o.blocks;
+  const bool cooperative = o.backend == ST_BACKEND_FUSED || o.backend == ST_BACKEND_PERSISTENT;
+  if (cooperative && rt->grid > rt->legal_blocks) {
+    rt->fail(ST_ERR_INVALID, "Requested cooperative grid exceeds actual occupancy limit %d", rt->legal_blocks);
+    return bail(ST_ERR_INVALID);
+  }
+  if (rt->cuda(cudaStreamCreateWithFlags(&rt->stream, cudaStreamNonBlocking), "stream") != ST_OK ||
+      rt->cuda(cudaStreamCreateWithFlags(&rt->aux, cudaStreamNonBlocking), "stream") != ST_OK ||
+      rt->cuda(cudaEventCreate(&rt->ev_start), "event") != ST_OK ||
+      rt->cuda(cudaEventCreate(&rt->ev_stop), "event") != ST_OK)
+    return bail(ST_ERR_CUDA);
+
+  // ---- weights slab layout
+  const int d = m.width, F = m.ffn, L = m.layers, hd = m.width / m.heads;
+  size_t off = 0;
+  int index = 0;
+  auto region = [&](size_t rows, size_t cols) {
+    const size_t at = off;
+    off = align_up(off + rows * cols * rt->elem, 256);
+    return at;
+  };
+  auto slot = [&](const std::string& name, size_t at, int rows, int cols, int step, int roff) {
+    rt->slots[name] = TensorSlot{at, rows, cols, step, roff, index++};
+  };
+  slot("input", region(d, m.features), d, m.features, 1, 0);
+  slot("final_norm", region(1, d), 1, d, 1, 0);
+  slot("score", region(1, d), 1, d, 1, 0);
+  std::vector<size_t> qkv_at(L), gu_at(L), out_at(L), down_at(L), n1_at(L), n2_at(L);
+  for (int l = 0; l < L; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    n1_at[l] = region(1, d);
+    n2_at[l] = region(1, d);
+    qkv_at[l] = region(3 * (size_t)d, d);
+    out_at[l] = region(d, d);
+    gu_at[l] = region(2 * (size_t)F, d);
+    down_at[l] = region(d, F);
+    slot(p + "norm1", n1_at[l], 1, d, 1, 0);
+    slot(p + "norm2", n2_at[l], 1, d, 1, 0);
+    slot(p + "q", qkv_at[l], d, d, 1, 0);
+    slot(p + "k", qkv_at[l], d, d, 1, d);
+    slot(p + "v", qkv_at[l], d, d, 1, 2 * d);
+    slot(p + "out", out_at[l], d, d, 1, 0);
+    slot(p + "gate", gu_at[l], F, d, 2, 0);
+    slot(p + "up", gu_at[l], F, d, 2, 1);
+    slot(p + "down", down_at[l], d, F, 1, 0);
+  }
+  rt->have.assign(index, 0);
+  rt->weights_bytes = off;
+  if (rt->cuda(cudaMalloc(&rt->weights, off), "cudaMalloc weights") != ST_OK) return bail(ST_ERR_CUDA);
+
+  // ---- state
+  const size_t S = m.streams;
+  rt->kv_bytes_per_tensor = S * L * (size_t)d * m.window * rt->elem;
+  const size_t kv_at = 0;
+  size_t so = align_up(rt->kv_bytes_per_tensor, 256) * 2;
+  const size_t hidden_at = so;
+  so = align_up(so + S * L * d * sizeof(float), 256);
+  const size_t pos_at = so;
+  so = align_up(so + S * sizeof(unsigned long long), 256);
+  rt->state_bytes = so;
+  if (rt->cuda(cudaMalloc(&rt->state, so), "cudaMalloc state") != ST_OK) return bail(ST_ERR_CUDA);
+  if (rt->cuda(cudaMemset(rt->state, 0, so), "cudaMemset state") != ST_OK) return bail(ST_ERR_CUDA);
+
+  // ---- scratch
+  const int nch = (m.window + kAttChunk - 1) / kAttChunk;
+  size_t co = 0;
+  auto take = [&](size_t bytes) { const size_t at = co; co = align_up(co + bytes, 256); return at; };
+  const size_t x_at = take(S * d * 4), x2_at = take(S * d * 4), q_at = take(S * d * 4);
+  const size_t part_at = take(S * m.heads * (size_t)nch * (hd + 2) * 4);
+  const size_t act_at = take(S * F * 4), score_at = take(S * 4), input_at = take(S * m.features * 4);
+  const size_t bar_at = take(sizeof(unsigned long long)), err_at = take(sizeof(int));
+  const size_t rope_at = take((hd / 2) * sizeof(float)), ctl_at = take(sizeof(Control));
+  rt->scratch_bytes = co;
+  if (rt->cuda(cudaMalloc(&rt->scratch, co), "cudaMalloc scratch") != ST_OK) return bail(ST_ERR_CUDA);
+  if (rt->cuda(cudaMemset(rt->scratch, 0, co), "cudaMemset scratch") != ST_OK) return bail(ST_ERR_CUDA);
+  std::vector<float> freq(hd / 2);
+  for (int i = 0; i < hd; i += 2) freq[i / 2] = powf(10000.0f, -(float)i / (float)hd);
+  if (rt->cuda(cudaMemcpy(rt->scratch + rope_at, freq.data(), freq.size() * 4, cudaMemcpyHostToDevice), "rope table") != ST_OK)
+    return bail(ST_ERR_CUDA);
+
+  // ---- mapped pinned memory
+  void* hp = nullptr;
+  if (rt->cuda(cudaHostAlloc(&hp, sizeof(Mailbox), cudaHostAllocMapped), "cudaHostAlloc mailbox") != ST_OK) return bail(ST_ERR_CUDA);
+  rt->mb_h = (Mailbox*)hp;
+  std::memset(hp, 0, sizeof(Mailbox));
+  if (rt->cuda(cudaHostGetDevicePointer((void**)&rt->mb_d, hp, 0), "mailbox alias") != ST_OK) return bail(ST_ERR_CUDA);
+  if (rt->cuda(cudaHostAlloc(&hp, S * m.features * 4, cudaHostAllocMapped), "cudaHostAlloc input") != ST_OK) return bail(ST_ERR_CUDA);
+  rt->in_h = (float*)hp;
+  std::memset(hp, 0, S * m.features * 4);
+  if (rt->cuda(cudaHostGetDevicePointer((void**)&rt->in_d, hp, 0), "input alias") != ST_OK) return bail(ST_ERR_CUDA);
+  if (rt->cuda(cudaHostAlloc(&hp, S * 4, cudaHostAllocMapped), "cudaHostAlloc output") != ST_OK) return bail(ST_ERR_CUDA);
+  rt->out_h = (float*)hp;
+  std::memset(hp, 0, S * 4);
+  if (rt->cuda(cudaHostGetDevicePointer((void**)&rt->out_d, hp, 0), "output alias") != ST_OK) return bail(ST_ERR_CUDA);
+
+  // ---- step arguments
+  StepArgs& a = rt->args;
+  a.layers = L; a.width = d; a.heads = m.heads; a.ffn = F; a.window = m.window; a.features = m.features;
+  a.head_dim = hd; a.streams = (int)S; a.epsilon = m.epsilon; a.nchunks_max = nch;
+  a.input_w = rt->weights + rt->slots["input"].offset;
+  a.final_norm = rt->weights + rt->slots["final_norm"].offset;
+  a.score_w = rt->weights + rt->slots["score"].offset;
+  for (int l = 0; l < L; ++l) {
+    a.layer[l].norm1 = rt->weights + n1_at[l];
+    a.layer[l].norm2 = rt->weights + n2_at[l];
+    a.layer[l].qkv = rt->weights + qkv_at[l];
+    a.layer[l].out = rt->weights + out_at[l];
+    a.layer[l].gateup = rt->weights + gu_at[l];
+    a.layer[l].down = rt->weights + down_at[l];
+  }
+  a.rope_freq = (const float*)(rt->scratch + rope_at);
+  a.keys = rt->state + kv_at;
+  a.values = rt->state + kv_at + align_up(rt->kv_bytes_per_tensor, 256);
+  a.hidden = (float*)(rt->state + hidden_at);
+  a.position = (unsigned long long*)(rt->state + pos_at);
+  rt->dev_input = (float*)(rt->scratch + input_at);
+  rt->dev_score = (float*)(rt->scratch + score_at);
+  a.input = o.mapped ? rt->in_d : rt->dev_input;
+  a.score = o.mapped ? rt->out_d : rt->dev_score;
+  a.x = (float*)(rt->scratch + x_at);
+  a.x2 = (float*)(rt->scratch + x2_at);
+  a.q = (float*)(rt->scratch + q_at);
+  a.part = (float*)(rt->scratch + part_at);
+  a.act = (float*)(rt->scratch + act_at);
+  a.bar_counter = (unsigned long long*)(rt->scratch + bar_at);
+  a.error = (int*)(rt->scratch + err_at);
+  a.host_error = &rt->mb_d->error;
+  a.bar_timeout_ns = 2ull * 1000000000ull;
+  rt->control = (Control*)(rt->scratch + ctl_at);
+  *out = rt;
+  return ST_OK;
+}
+
+int st_set_tensor(st_runtime* rt, const char* name, const float* data, size_t count) {
+  if (!rt || !name || !data) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (rt->started) return rt->fail(ST_ERR_STATE, "tensors are fixed once the runtime has started");
+  auto it = rt->slots.find(name);
+  if (it == rt->slots.end()) return rt->fail(ST_ERR_INVALID, "Unknown tensor %s", name);
+  const TensorSlot& s = it->second;
+  if (count != (size_t)s.rows * s.cols) return rt->fail(ST_ERR_INVALID, "Shape mismatch: %s", name);
+  float* tmp = nullptr;
+  ST_CUDA(rt, cudaMalloc(&tmp, count * sizeof(float)));
+  int st = rt->cuda(cudaMemcpy(tmp, data, count * sizeof(float), cudaMemcpyHostToDevice), "tensor upload");
+  if (st == ST_OK) {
+    const int blocks = (int)std::min<size_t>((count + 255) / 256, 4096);
+    void* dst = rt->weights + s.offset;
+    if (rt->desc.mode == ST_MODE_FP16) k_convert<__half><<<blocks, 256, 0, rt->stream>>>(tmp, (__half*)dst, s.rows, s.cols, s.row_step, s.row_offset);
+    else if (rt->desc.mode == ST_MODE_BF16) k_convert<__nv_bfloat16><<<blocks, 256, 0, rt->stream>>>(tmp, (__nv_bfloat16*)dst, s.rows, s.cols, s.row_step, s.row_offset);
+    else k_convert<float><<<blocks, 256, 0, rt->stream>>>(tmp, (float*)dst, s.rows, s.cols, s.row_step, s.row_offset);
+    st = rt->cuda(cudaGetLastError(), "convert launch");
+    if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "convert");
+  }
+  cudaFree(tmp);
+  if (st == ST_OK) rt->have[s.index] = 1;
+  return st;
+}
+
+int st_start(st_runtime* rt) {
+  if (!rt) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (rt->started) return rt->fail(ST_ERR_STATE, "runtime already started");
+  for (const auto& kv : rt->slots)
+    if (!rt->have[kv.second.index]) return rt->fail(ST_ERR_INVALID, "Missing tensor %s", kv.first.c_str());
+  ST_CUDA(rt, cudaSetDevice(rt->device));
+  ST_TRY(preload(rt));
+  // Warm every kernel once (lazy module loading), then restore the initial state.
+  if (rt->opt.backend != ST_BACKEND_PERSISTENT) {
+    ST_TRY(launch_sequence(rt, rt->args));
+    if (rt->opt.backend == ST_BACKEND_FUSED) ST_TRY(launch_fused(rt, rt->args));
+  }
+  ST_TRY(launch_reset(rt, 0, rt->desc.streams));
+  ST_CUDA(rt, cudaStreamSynchronize(rt->stream));
+  ST_TRY(check_device_error(rt));
+  if (rt->opt.backend == ST_BACKEND_GRAPH) ST_TRY(graph_capture(rt));
+  rt->started = true;
+  if (rt->opt.backend == ST_BACKEND_PERSISTENT) ST_TRY(start_persistent(rt));
+  return ST_OK;
+}
+
+static int step_common(st_runtime* rt, const float* inputs, float* scores) {
+  if (!rt || !inputs || !scores) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
+  const size_t n = (size_t)rt->desc.streams * rt->desc.features;
+  if (rt->opt.backend == ST_BACKEND_PERSISTENT) {
+    if (!rt->running) return rt->fail(ST_ERR_STOPPED, "Persistent runtime is stopped");
+    std::memcpy(rt->in_h, inputs, n * sizeof(float));
+    ST_TRY(command(rt, kRun, -1));
+  } else {
+    std::memcpy(rt->in_h, inputs, n * sizeof(float));
+    ST_TRY(run_step_nonpersistent(rt));
+  }
+  std::memcpy(scores, rt->out_h, (size_t)rt->desc.streams * sizeof(float));
+  return ST_OK;
+}
+
+int st_step(st_runtime* rt, const float* input, float* score) {
+  if (rt && rt->desc.streams != 1) return rt->fail(ST_ERR_INVALID, "st_step needs streams == 1; use st_step_batch");
+  return step_common(rt, input, score);
+}
+
+int st_step_batch(st_runtime* rt, const float* inputs, float* scores) { return step_common(rt, inputs, scores); }
+
+int st_reset_stream(st_runtime* rt, int stream) {
+  if (!rt) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
+  if (stream < -1 || stream >= rt->desc.streams) return rt->fail(ST_ERR_INVALID, "stream index out of range");
+  if (rt->opt.backend == ST_BACKEND_PERSISTENT) return command(rt, kReset, stream);
+  const int s0 = stream < 0 ? 0 : stream, s1 = stream < 0 ? rt->desc.streams : stream + 1;
+  ST_TRY(launch_reset(rt, s0, s1));
+  ST_CUDA(rt, cudaStreamSynchronize(rt->stream));
+  return check_device_error(rt);
+}
+
+int st_reset(st_runtime* rt) { return st_reset_stream(rt, -1); }
+
+int st_stop(st_runtime* rt) {
+  if (!rt) return ST_ERR_INVALID;
+  if (rt->running) {
+    if (!__atomic_load_n(&rt->mb_h->exited, __ATOMIC_ACQUIRE)) {
+      int st = command(rt, kStop, -1);
+      if (st != ST_OK && st != ST_ERR_WORKER_EXITED) return st;
+    }
+    if (rt->running) ST_TRY(join_persistent(rt));
+  }
+  return ST_OK;
+}
+
+int st_snapshot(st_runtime* rt, int stream, uint64_t* position, float* keys, float* values, float* hidden) {
+  if (!rt) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (stream < 0 || stream >= rt->desc.streams) return rt->fail(ST_ERR_INVALID, "stream index out of range");
+  const st_model_desc& m = rt->desc;
+  const size_t cache = (size_t)m.layers * m.width * m.window;
+  cudaStream_t s = rt->aux;
+  if (position) {
+    unsigned long long p = 0;
+    ST_CUDA(rt, cudaMemcpyAsync(&p, rt->args.position + stream, sizeof p, cudaMemcpyDeviceToHost, s));
+    ST_CUDA(rt, cudaStreamSynchronize(s));
+    *position = p;
+  }
+  auto download = [&](const void* base, float* dst) -> int {
+    if (!dst) return ST_OK;
+    const char* src = (const char*)base + (size_t)stream * cache * rt->elem;
+    if (m.mode == ST_MODE_FP32) {
+      ST_CUDA(rt, cudaMemcpyAsync(dst, src, cache * 4, cudaMemcpyDeviceToHost, s));
+      ST_CUDA(rt, cudaStreamSynchronize(s));
+      return ST_OK;
+    }
+    std::vector<uint16_t> raw(cache);
+    ST_CUDA(rt, cudaMemcpyAsync(raw.data(), src, cache * 2, cudaMemcpyDeviceToHost, s));
+    ST_CUDA(rt, cudaStreamSynchronize(s));
+    for (size_t i = 0; i < cache; ++i)
+      dst[i] = m.mode == ST_MODE_FP16 ? half_bits_to_float(raw[i]) : bf16_bits_to_float(raw[i]);
+    return ST_OK;
+  };
+  ST_TRY(download(rt->args.keys, keys));
+  ST_TRY(download(rt->args.values, values));
+  if (hidden) {
+    const size_t n = (size_t)m.layers * m.width;
+    ST_CUDA(rt, cudaMemcpyAsync(hidden, rt->args.hidden + (size_t)stream * n, n * 4, cudaMemcpyDeviceToHost, s));
+    ST_CUDA(rt, cudaStreamSynchronize(s));
+  }
+  return ST_OK;
+}
+
+int st_load_state(st_runtime* rt, int stream, uint64_t position, const float* keys, const float* values,
+                  const float* hidden) {
+  if (!rt || !keys || !values || !hidden) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
+  if (rt->running) return rt->fail(ST_ERR_STATE, "stop the persistent worker before loading state");
+  if (stream < 0 || stream >= rt->desc.streams) return rt->fail(ST_ERR_INVALID, "stream index out of range");
+  const st_model_desc& m = rt->desc;
+  const size_t cache = (size_t)m.layers * m.width * m.window;
+  const int hd = m.width / m.heads;
+  float* tmp = nullptr;
+  ST_CUDA(rt, cudaMalloc(&tmp, cache * sizeof(float)));
+  int st = ST_OK;
+  for (int which = 0; which < 2 && st == ST_OK; ++which) {
+    const float* src = which == 0 ? keys : values;
+    char* base = (char*)(which == 0 ? rt->args.keys : rt->args.values) + (size_t)stream * cache * rt->elem;
+    st = rt->cuda(cudaMemcpy(tmp, src, cache * sizeof(float), cudaMemcpyHostToDevice), "state upload");
+    if (st != ST_OK) break;
+    const int rows = (int)(cache / hd), blocks = (int)std::min<size_t>((cache + 255) / 256, 4096);
+    if (m.mode == ST_MODE_FP16) k_convert<__half><<<blocks, 256, 0, rt->stream>>>(tmp, (__half*)base, rows, hd, 1, 0);
+    else if (m.mode == ST_MODE_BF16) k_convert<__nv_bfloat16><<<blocks, 256, 0, rt->stream>>>(tmp, (__nv_bfloat16*)base, rows, hd, 1, 0);
+    else k_convert<float><<<blocks, 256, 0, rt->stream>>>(tmp, (float*)base, rows, hd, 1, 0);
+    st = rt->cuda(cudaGetLastError(), "state convert");
+    if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "state convert");
+  }
+  cudaFree(tmp);
+  ST_TRY(st);
+  const size_t n = (size_t)m.layers * m.width;
+  unsigned long long p = position;
+  ST_CUDA(rt, cudaMemcpy(rt->args.hidden + (size_t)stream * n, hidden, n * 4, cudaMemcpyHostToDevice));
+  ST_CUDA(rt, cudaMemcpy(rt->args.position + stream, &p, sizeof p, cudaMemcpyHostToDevice));
+  return ST_OK;
+}
+
+static int device_trace_impl(st_runtime* rt, const float* dev_inputs, size_t count, float* dev_scores,
+                             double* us_per_step) {
+  const int S = rt->desc.streams;
+  const size_t stride = (size_t)S * rt->desc.features;
+  StepArgs a = rt->args;
+  a.input = rt->dev_input;
+  a.score = rt->dev_score;
+  ST_TRY(launch_reset(rt, 0, S));
+  ST_CUDA(rt, cudaEventRecord(rt->ev_start, rt->stream));
+  if (rt->opt.backend == ST_BACKEND_FUSED || rt->opt.backend == ST_BACKEND_PERSISTENT) {
+    ST_TRY(launch_trace(rt, a, dev_inputs, count, dev_scores));
+  } else {
+    const bool graph = rt->opt.backend == ST_BACKEND_GRAPH && !rt->opt.mapped;
+    for (size_t e = 0; e < count; ++e) {
+      ST_CUDA(rt, cudaMemcpyAsync(rt->dev_input, dev_inputs + e * stride, stride * 4, cudaMemcpyDeviceToDevice, rt->stream));
+      if (graph) {
+        ST_CUDA(rt, cudaGraphLaunch(rt->graph_exec, rt->stream));
+        rt->launches += 2 + 5ull * rt->desc.layers;
+      } else {
+        ST_TRY(launch_sequence(rt, a));
+      }
+      if (dev_scores)
+        ST_CUDA(rt, cudaMemcpyAsync(dev_scores + e * S, rt->dev_score, S * 4, cudaMemcpyDeviceToDevice, rt->stream));
+    }
+  }
+  ST_CUDA(rt, cudaEventRecord(rt->ev_stop, rt->stream));
+  ST_CUDA(rt, cudaEventSynchronize(rt->ev_stop));
+  ST_TRY(check_device_error(rt));
+  float ms = 0;
+  ST_CUDA(rt, cudaEventElapsedTime(&ms, rt->ev_start, rt->ev_stop));
+  if (us_per_step) *us_per_step = count ? ms * 1000.0 / (double)count : 0.0;
+  return ST_OK;
+}
+
+int st_device_trace(st_runtime* rt, const float* inputs, size_t count, float* scores, double* us_per_step) {
+  if (!rt || !inputs || count == 0) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
+  if (rt->opt.backend == ST_BACKEND_PERSISTENT) ST_TRY(st_stop(rt));
+  const int S = rt->desc.streams;
+  const size_t n = count * (size_t)S * rt->desc.features;
+  float* dev = nullptr;
+  float* dev_scores = nullptr;
+  ST_CUDA(rt, cudaMalloc(&dev, n * 4));
+  int st = rt->cuda(cudaMalloc(&dev_scores, count * (size_t)S * 4), "cudaMalloc scores");
+  if (st == ST_OK) st = rt->cuda(cudaMemcpy(dev, inputs, n * 4, cudaMemcpyHostToDevice), "trace upload");
+  if (st == ST_OK) st = device_trace_impl(rt, dev, count, dev_scores, us_per_step);
+  if (st == ST_OK && scores)
+    st = rt->cuda(cudaMemcpy(scores, dev_scores, count * (size_t)S * 4, cudaMemcpyDeviceToHost), "scores download");
+  cudaFree(dev);
+  cudaFree(dev_scores);
+  return st;
+}
+
+int st_device_trace_resident(st_runtime* rt, const float* device_inputs, size_t count, double* us_per_step,
+                             uint64_t* kernel_launches) {
+  if (!rt || !device_inputs || count == 0) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
+  if (rt->opt.backend == ST_BACKEND_PERSISTENT) ST_TRY(st_stop(rt));
+  const uint64_t before = rt->launches;
+  ST_TRY(device_trace_impl(rt, device_inputs, count, nullptr, us_per_step));
+  // The reset that precedes the timed region is not counted.
+  if (kernel_launches) *kernel_launches = rt->launches - before - 1;
+  return ST_OK;
+}
+
+int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
+  if (!rt) return ST_ERR_INVALID;
+  cudaFuncAttributes fa{};
+  const void* kernel = persistent_fn(rt);
+  std::string name = "k_persistent";
+  if (rt->opt.backend == ST_BACKEND_FUSED) {
+    kernel = rt->desc.mode == ST_MODE_FP16 ? Kernels<__half>::fused() : rt->desc.mode == ST_MODE_BF16 ? Kernels<__nv_bfloat16>::fused() : Kernels<float>::fused();
+    name = "k_fused";
+  } else if (rt->opt.backend == ST_BACKEND_CUDA || rt->opt.backend == ST_BACKEND_GRAPH) {
+    kernel = rt->desc.mode == ST_MODE_FP16 ? (const void*)k_ffn_in<__half> : rt->desc.mode == ST_MODE_BF16 ? (const void*)k_ffn_in<__nv_bfloat16> : (const void*)k_ffn_in<float>;
+    name = "k_ffn_in (per-op phase kernels)";
+  }
+  cudaFuncGetAttributes(&fa, kernel);
+  static const char* backends[] = {"cuda", "graph", "cublas", "cublas-graph", "fused", "persistent"};
+  static const char* modes[] = {"fp32", "fp16", "bf16"};
+  int pst = ST_OK;
+  std::ostringstream o;
+  o << "{\"environment\":" << probe_json(rt->device, &pst) << ",\"backend\":\"" << backends[rt->opt.backend]
+    << "\",\"blocks\":" << rt->grid << ",\"legal_cooperative_blocks\":" << rt->legal_blocks
+    << ",\"threads\":" << kThreads << ",\"resource_kernel\":\"" << name << "\""
+    << ",\"registers_per_thread\":" << fa.numRegs << ",\"local_bytes\":" << fa.localSizeBytes
+    << ",\"shared_bytes\":" << fa.sharedSizeBytes
+    << ",\"attention_implementation\":\"split-window partial softmax, " << kAttChunk << " slots per warp item\""
+    << ",\"matvec_implementation\":\"16-byte non-temporal loads, contiguous row ranges per CTA\""
+    << ",\"barriers_per_step\":" << forward_barrier_count(rt)
+    << ",\"transport\":\"" << (rt->opt.backend == ST_BACKEND_PERSISTENT ? "mapped-system-load-store" : rt->opt.mapped ? "mapped-stream-sync" : "pinned-copy-stream-sync") << "\""
+    << ",\"poll_policy\":\"" << (rt->opt.backoff ? "bounded-device-backoff-host-yield" : "tight") << "\""
+    << ",\"workspace_storage\":\"FP32 with explicit rounding to the storage type\""
+    << ",\"weights_and_kv_storage\":\"" << modes[rt->desc.mode] << "\""
+    << ",\"streams\":" << rt->desc.streams << ",\"weights_bytes\":" << rt->weights_bytes
+    << ",\"state_bytes\":" << rt->state_bytes << ",\"scratch_bytes\":" << rt->scratch_bytes << "}";
+  return copy_json(o.str(), json, capacity, needed);
+}
+
+int st_probe(int device, char* json, size_t capacity, size_t* needed) {
+  int st = ST_OK;
+  std::string s = probe_json(device, &st);
+  if (st != ST_OK) { g_create_error = "device probe failed"; return st; }
+  return copy_json(s, json, capacity, needed);
+}
+
+void st_destroy(st_runtime* rt) {
+  if (!rt) return;
+  if (rt->running && !rt->failed) {
+    if (st_stop(rt) != ST_OK && rt->stream) cudaStreamSynchronize(rt->stream);
+  } else if (rt->stream) {
+    cudaStreamSynchronize(rt->stream);
+  }
+  if (rt->graph_exec) cudaGraphExecDestroy(rt->graph_exec);
+  if (rt->graph) cudaGraphDestroy(rt->graph);
+  if (rt->ev_start) cudaEventDestroy(rt->ev_start);
+  if (rt->ev_stop) cudaEventDestroy(rt->ev_stop);
+  if (rt->stream) cudaStreamDestroy(rt->stream);
+  if (rt->aux) cudaStreamDestroy(rt->aux);
+  cudaFree(rt->weights);
+  cudaFree(rt->state);
+  cudaFree(rt->scratch);
+  if (rt->mb_h) cudaFreeHost(rt->mb_h);
+  if (rt->in_h) cudaFreeHost(rt->in_h);
+  if (rt->out_h) cudaFreeHost(rt->out_h);
+  delete rt;
+}
+
+}  // extern "C"

@@ -1,0 +1,283 @@
+"""Python host binding of the C ABI (include/streaming_b200.h).
+
+Mirrors the reference's ``Stream::Runtime`` interface (reference
+include/Runtime.hpp:7-46): ``Backend``, ``RuntimeOptions``, ``Snapshot`` and
+``Runtime.step / reset / stop / snapshot / info / device_trace``, plus
+``probe()``. Errors surface as ``StreamError`` (a ``RuntimeError``, as the
+reference throws ``std::runtime_error``) carrying the C status code.
+
+The CUDA library is mandatory: importing works without a GPU, but creating a
+Runtime loads ``lib/libstreaming_b200.so`` and fails loudly if it is missing or
+no B200 is present. There is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import enum
+import json
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+
+from .model import MODE_CODES, Model
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libstreaming_b200.so"
+
+ST_OK = 0
+STATUS_NAMES = {
+    -1: "INVALID", -2: "UNSUPPORTED", -3: "CUDA", -4: "STOPPED", -5: "EXHAUSTED",
+    -6: "WORKER_EXITED", -7: "DEVICE_TIMEOUT", -8: "HOST_TIMEOUT", -9: "STATE",
+}
+
+
+class StreamError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{message} [{STATUS_NAMES.get(code, code)}]")
+        self.code = code
+        self.status = STATUS_NAMES.get(code, str(code))
+
+
+class Backend(enum.IntEnum):
+    """reference include/Runtime.hpp:7, same order."""
+    CUDA = 0
+    GRAPH = 1
+    CUBLAS = 2
+    CUBLAS_GRAPH = 3
+    FUSED = 4
+    PERSISTENT = 5
+
+
+BACKEND_NAMES = {"cuda": Backend.CUDA, "graph": Backend.GRAPH, "cublas": Backend.CUBLAS,
+                 "cublas-graph": Backend.CUBLAS_GRAPH, "fused": Backend.FUSED,
+                 "persistent": Backend.PERSISTENT}
+
+
+@dataclass
+class RuntimeOptions:
+    """reference include/Runtime.hpp:8-19 (defaults kept). ``blocks=0`` selects one CTA per SM."""
+    backend: Backend = Backend.GRAPH
+    blocks: int = 1
+    backoff: bool = False
+    mapped: bool = False
+    vector_matvec: bool = False
+    fused_attention: bool = False
+    max_events: int = 0
+    initial_sequence: int = 0
+    idle_seconds: float = 30.0
+    device: int = 0
+
+
+@dataclass
+class Snapshot:
+    """reference include/Runtime.hpp:20-23."""
+    position: int
+    keys: np.ndarray = field(repr=False)
+    values: np.ndarray = field(repr=False)
+    hidden: np.ndarray = field(repr=False)
+
+
+class _ModelDesc(ctypes.Structure):
+    _fields_ = [("layers", ctypes.c_int), ("width", ctypes.c_int), ("heads", ctypes.c_int),
+                ("ffn", ctypes.c_int), ("window", ctypes.c_int), ("features", ctypes.c_int),
+                ("epsilon", ctypes.c_float), ("mode", ctypes.c_int), ("streams", ctypes.c_int)]
+
+
+class _Options(ctypes.Structure):
+    _fields_ = [("backend", ctypes.c_int), ("blocks", ctypes.c_int), ("backoff", ctypes.c_int),
+                ("mapped", ctypes.c_int), ("vector_matvec", ctypes.c_int), ("fused_attention", ctypes.c_int),
+                ("max_events", ctypes.c_uint64), ("initial_sequence", ctypes.c_uint64),
+                ("idle_seconds", ctypes.c_double), ("device", ctypes.c_int)]
+
+
+_lib = None
+F = ctypes.POINTER(ctypes.c_float)
+
+
+def library() -> ctypes.CDLL:
+    """Load the CUDA library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise StreamError(-3, f"CUDA library missing: {LIB_PATH} (run python -m streaming_transformer_b200.build)")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        P, I, S = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+        U64 = ctypes.c_uint64
+        sigs = {
+            "st_create": (I, [ctypes.POINTER(_ModelDesc), ctypes.POINTER(_Options), ctypes.POINTER(P)]),
+            "st_set_tensor": (I, [P, ctypes.c_char_p, F, S]),
+            "st_start": (I, [P]),
+            "st_step": (I, [P, F, F]),
+            "st_step_batch": (I, [P, F, F]),
+            "st_reset": (I, [P]),
+            "st_reset_stream": (I, [P, I]),
+            "st_stop": (I, [P]),
+            "st_snapshot": (I, [P, I, ctypes.POINTER(U64), F, F, F]),
+            "st_load_state": (I, [P, I, U64, F, F, F]),
+            "st_device_trace": (I, [P, F, S, F, ctypes.POINTER(ctypes.c_double)]),
+            "st_device_trace_resident": (I, [P, ctypes.c_void_p, S, ctypes.POINTER(ctypes.c_double),
+                                             ctypes.POINTER(U64)]),
+            "st_info": (I, [P, ctypes.c_char_p, S, ctypes.POINTER(S)]),
+            "st_probe": (I, [I, ctypes.c_char_p, S, ctypes.POINTER(S)]),
+            "st_kernel_launches": (U64, [P]),
+            "st_last_error": (ctypes.c_char_p, [P]),
+            "st_destroy": (None, [P]),
+            "st_abi_version": (I, []),
+            "st_default_options": (None, [ctypes.POINTER(_Options)]),
+        }
+        for name, (res, args) in sigs.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def _fptr(a: np.ndarray):
+    return a.ctypes.data_as(F)
+
+
+def _check(code: int, handle=None) -> None:
+    if code != ST_OK:
+        msg = library().st_last_error(handle)
+        raise StreamError(code, msg.decode() if msg else "error")
+
+
+def _json_call(fn, *args) -> dict:
+    needed = ctypes.c_size_t(0)
+    _check(fn(*args, None, 0, ctypes.byref(needed)))
+    buf = ctypes.create_string_buffer(needed.value)
+    _check(fn(*args, buf, needed.value, ctypes.byref(needed)))
+    return json.loads(buf.value.decode())
+
+
+def probe(device: int = 0) -> dict:
+    """reference probe() (src/cuda/Runtime.cu:134-161, 664)."""
+    return _json_call(library().st_probe, device)
+
+
+class Runtime:
+    """One runtime per device: device state for ``streams`` independent streams.
+
+    Owns every device and pinned buffer; ``close()`` (or garbage collection)
+    stops the resident worker before freeing them (reference
+    src/cuda/Runtime.cu:294-299).
+    """
+
+    def __init__(self, model: Model, options: RuntimeOptions | None = None, streams: int = 1):
+        self.model = model
+        self.options = options or RuntimeOptions()
+        self.streams = int(streams)
+        c = model.config
+        self.config = c
+        lib = library()
+        desc = _ModelDesc(c.layers, c.width, c.heads, c.ffn, c.window, c.features,
+                          float(c.epsilon), MODE_CODES[model.mode], self.streams)
+        o = self.options
+        opts = _Options(int(o.backend), int(o.blocks), int(bool(o.backoff)), int(bool(o.mapped)),
+                        int(bool(o.vector_matvec)), int(bool(o.fused_attention)), int(o.max_events),
+                        int(o.initial_sequence), float(o.idle_seconds), int(o.device))
+        handle = ctypes.c_void_p()
+        code = lib.st_create(ctypes.byref(desc), ctypes.byref(opts), ctypes.byref(handle))
+        if code != ST_OK:
+            raise StreamError(code, lib.st_last_error(None).decode())
+        self._h = handle
+        try:
+            for name in model.names():
+                data = np.ascontiguousarray(model.get(name), dtype=np.float32).ravel()
+                _check(lib.st_set_tensor(self._h, name.encode(), _fptr(data), data.size), self._h)
+            _check(lib.st_start(self._h), self._h)
+        except Exception:
+            self.close()
+            raise
+        self._in = np.zeros((self.streams, c.features), dtype=np.float32)
+        self._out = np.zeros(self.streams, dtype=np.float32)
+
+    # -- lifecycle
+    def close(self) -> None:
+        h = getattr(self, "_h", None)
+        if h:
+            library().st_destroy(h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # -- hot path
+    def step(self, event) -> float:
+        """reference Runtime::step: one event (features floats) -> one score."""
+        self._in[0, :] = np.asarray(event, dtype=np.float32).reshape(-1)[: self.config.features]
+        _check(library().st_step(self._h, _fptr(self._in), _fptr(self._out)), self._h)
+        return float(self._out[0])
+
+    def step_batch(self, events) -> np.ndarray:
+        """Advance every stream by one event: events [streams, features] -> scores [streams]."""
+        e = np.ascontiguousarray(events, dtype=np.float32).reshape(self.streams, self.config.features)
+        out = np.empty(self.streams, dtype=np.float32)
+        _check(library().st_step_batch(self._h, _fptr(e), _fptr(out)), self._h)
+        return out
+
+    def reset(self) -> None:
+        _check(library().st_reset(self._h), self._h)
+
+    def reset_stream(self, stream: int) -> None:
+        _check(library().st_reset_stream(self._h, int(stream)), self._h)
+
+    def stop(self) -> None:
+        _check(library().st_stop(self._h), self._h)
+
+    def snapshot(self, stream: int = 0) -> Snapshot:
+        c = self.config
+        shape = (c.layers, c.heads, c.window, c.head_dim)
+        keys = np.empty(shape, dtype=np.float32)
+        values = np.empty(shape, dtype=np.float32)
+        hidden = np.empty((c.layers, c.width), dtype=np.float32)
+        pos = ctypes.c_uint64(0)
+        _check(library().st_snapshot(self._h, int(stream), ctypes.byref(pos), _fptr(keys), _fptr(values),
+                                     _fptr(hidden)), self._h)
+        return Snapshot(int(pos.value), keys, values, hidden)
+
+    def load_state(self, position: int, keys, values, hidden, stream: int = 0) -> None:
+        k = np.ascontiguousarray(keys, dtype=np.float32)
+        v = np.ascontiguousarray(values, dtype=np.float32)
+        h = np.ascontiguousarray(hidden, dtype=np.float32)
+        _check(library().st_load_state(self._h, int(stream), int(position), _fptr(k), _fptr(v), _fptr(h)), self._h)
+
+    def info(self) -> dict:
+        return _json_call(library().st_info, self._h)
+
+    def device_trace(self, events, return_scores: bool = False):
+        """reference Runtime::deviceTrace: µs per step over a preloaded trace
+        ([count, features] or [count, streams, features]); resets first."""
+        e = np.ascontiguousarray(events, dtype=np.float32)
+        count = e.shape[0]
+        e = e.reshape(count, self.streams, self.config.features)
+        us = ctypes.c_double(0)
+        scores = np.empty((count, self.streams), dtype=np.float32) if return_scores else None
+        _check(library().st_device_trace(self._h, _fptr(e), count, _fptr(scores) if scores is not None else None,
+                                         ctypes.byref(us)), self._h)
+        if return_scores:
+            return us.value, (scores[:, 0] if self.streams == 1 else scores)
+        return us.value
+
+    def device_trace_resident(self, device_ptr: int, count: int) -> tuple[float, int]:
+        """Device-only timing with the trace already in device memory (pointer from
+        any allocator); returns (µs per step, kernels launched)."""
+        us = ctypes.c_double(0)
+        launches = ctypes.c_uint64(0)
+        _check(library().st_device_trace_resident(self._h, ctypes.c_void_p(device_ptr), int(count),
+                                                  ctypes.byref(us), ctypes.byref(launches)), self._h)
+        return us.value, int(launches.value)
+
+    @property
+    def kernel_launches(self) -> int:
+        return int(library().st_kernel_launches(self._h))
