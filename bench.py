@@ -1,0 +1,312 @@
+#!/usr/bin/env python
+"""Benchmark of the streaming step on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config NAME]
+
+A step is one event of one stream through ``Runtime::step`` (the reference's
+unit, reference bench/Main.cpp:223). The default workload is configs[1] of the
+benchmark definition, "c2-main-fp32": Main fp32, single stream, d512 L8 H8
+(head_dim 64) F2048 W128, 32 features, seeded N(0, 0.02) weights and N(0, 1)
+events (synthetic; no dataset exists for this model).
+
+Arms (both print the same metric/unit/config):
+  --impl b200 (default)
+    value   device-resident steps/s: the trace is preloaded in HBM and stepped
+            by one resident kernel (st_device_trace_resident); CUDA events on
+            the runtime's stream bracket exactly K steps; max over ranks.
+    e2e     the public API with host buffers: Runtime.step on the persistent
+            mailbox backend, K host calls, each copying the event in through
+            mapped pinned memory and reading the score back; host clock.
+    roofline, cpu_baseline (CPU oracle, 1 thread, bounded sample), clocks.
+  --impl reference
+    The reference's CPU step. Its Eigen implementation (src/cpu/Cpu.cpp)
+    cannot be built here (no Eigen), so the C restatement in oracle/ is timed
+    with every host thread, on a bounded sample; rank 0 only.
+Multi-GPU (torchrun): the single-stream configs do not shard, so every rank
+runs an independent replica stream (weak scaling, no collective on the step
+path); value = total steps of all ranks / max device time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from streaming_transformer_b200 import Backend, Runtime, RuntimeOptions  # noqa: E402
+from streaming_transformer_b200 import metrics, synthetic  # noqa: E402
+
+METRIC = "p50 µs/step per stream; aggregate steps/s at 1/2/4/8 B200; % of BW roofline"
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20000)
+    p.add_argument("--warmup", type=int, default=500)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--config", default="c2-main-fp32", choices=sorted(synthetic.CONFIGS))
+    p.add_argument("--window", type=int, default=0, help="override the window (C3 sweep)")
+    p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def workload(args):
+    config, mode = synthetic.CONFIGS[args.config]
+    if args.window:
+        config = synthetic.config_with_window(config, args.window)
+    return config, mode
+
+
+def config_json(args, config, mode, working_set):
+    return {
+        "workload": f"{args.config}: {mode} single stream per GPU, d{config.width} L{config.layers} "
+                    f"H{config.heads} hd{config.head_dim} F{config.ffn} W{config.window}, "
+                    f"{config.features} features",
+        "model": "local-causal pre-RMSNorm transformer (streaming step)",
+        "streams_per_gpu": 1,
+        "global_batch": 1,
+        "seq_len": config.window,
+        "parallelism": "replicas (independent streams, no collective)",
+        "data": "seeded N(0,0.02) weights, unit norm gains, N(0,1) events",
+        "l2": ("working set %.1f MB > 126 MB L2, no flush" % (working_set / 1e6)) if working_set > L2_BYTES
+              else ("working set %.1f MB fits in L2; no flush between steps (streaming state carries "
+                    "over step to step by design)" % (working_set / 1e6)),
+    }
+
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        peaks = json.loads(path.read_text())
+        return float(peaks["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (of measured)"
+    except (OSError, ValueError, KeyError):
+        return FALLBACK_HBM_GBS, "profiling-recipe fallback 6.65 TB/s (of fallback)"
+
+
+def measured_traffic(name):
+    path = ROOT / "profiles" / "traffic.json"
+    try:
+        entry = json.loads(path.read_text())[name]
+        return float(entry["dram_bytes_per_step"]), entry.get("source", "")
+    except (OSError, ValueError, KeyError):
+        return None, None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 200 ms while running."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.device)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, loaded_only=True):
+        rows = []
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[4:8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
+        sm = [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def time_cpu_oracle(model, events, threads, budget_s, max_steps):
+    """Oracle steps/s on `threads` host threads over a bounded sample from reset."""
+    from oracle.oracle import Oracle  # CPU baseline only
+    o = Oracle(model, threads=threads)
+    t0 = time.perf_counter()
+    o.run(events[:2])
+    per = max((time.perf_counter() - t0) / 2, 1e-6)
+    n = int(max(4, min(max_steps, budget_s / per, len(events))))
+    o.reset()
+    t0 = time.perf_counter()
+    o.run(events[:n])
+    dt = time.perf_counter() - t0
+    return n / dt, n, dt
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    config, mode = workload(args)
+    model = synthetic.make_model(config, mode, seed=42)
+    events = synthetic.make_events(max(args.steps, 16), config.features, seed=123)
+    from oracle.oracle import cpu_count
+    threads = cpu_count()
+    steps_per_s, n, dt = time_cpu_oracle(model, events, threads, budget_s=60.0, max_steps=args.steps)
+    ws = metrics.weight_bytes(config, mode) + 2 * config.layers * config.width * config.window * metrics.ELEM_BYTES[mode]
+    sample = (f"{n} consecutive events from reset of the {args.config} trace, C restatement of the reference "
+              f"CPU step (reference Eigen src/cpu/Cpu.cpp needs Eigen3, absent), {threads} threads, {dt:.1f} s")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": steps_per_s, "unit": "steps/s", "n_gpus": args.gpus,
+        "steps": n, "warmup": 0, "ms_per_step": 1000.0 / steps_per_s, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": mode, "data": "synthetic",
+        "config": config_json(args, config, mode, ws),
+        "cpu_baseline": {"value": steps_per_s, "unit": "steps/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": steps_per_s, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200(args):
+    import torch
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    def barrier(device_wide=True):
+        # While the persistent worker is resident a device-wide synchronize
+        # would wait for that kernel (until its idle budget ends it), so the
+        # e2e phase synchronizes torch's own stream only.
+        if dist:
+            dist.barrier()
+        if device_wide:
+            torch.cuda.synchronize()
+        else:
+            torch.cuda.current_stream().synchronize()
+
+    config, mode = workload(args)
+    model = synthetic.make_model(config, mode, seed=42)
+    K, W = max(1, args.steps), max(3, args.warmup)
+    events = synthetic.make_events(K + W, config.features, seed=123 + rank)
+    e2e_lat = []
+    with ClockSampler(local) as clocks:
+        rt = Runtime(model, RuntimeOptions(backend=Backend.PERSISTENT, blocks=0, device=local))
+        try:
+            # ---- e2e through the public API: host event in, host score out
+            for e in events[:W]:
+                rt.step(e)
+            rt.reset()
+            barrier(device_wide=False)
+            t_start = time.perf_counter()
+            for e in events[W:W + K]:
+                t0 = time.perf_counter_ns()
+                rt.step(e)
+                e2e_lat.append((time.perf_counter_ns() - t0) / 1000.0)
+            e2e_wall = time.perf_counter() - t_start
+            barrier(device_wide=False)
+            # ---- device-resident: trace preloaded in HBM, one resident kernel
+            dev_events = torch.from_numpy(np.ascontiguousarray(events)).cuda()
+            torch.cuda.synchronize()
+            rt.device_trace_resident(dev_events.data_ptr(), W)       # warm-up (untimed)
+            barrier()
+            us, launches = rt.device_trace_resident(dev_events[W:].data_ptr(), K)
+            barrier()
+            info = rt.info()
+        finally:
+            rt.close()
+    elapsed_s = us * K / 1e6
+    e2e_steps_s = K / e2e_wall
+    t = torch.tensor([elapsed_s, e2e_wall], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.destroy_process_group()
+    max_elapsed, max_e2e = float(t[0]), float(t[1])
+    if rank != 0:
+        return 0
+    value = world * K / max_elapsed
+    peak, peak_src = measured_peak()
+    alg = metrics.trace_bytes(config, mode, K)
+    achieved = alg / K / (us * 1e-6) / 1e9
+    traffic, traffic_src = measured_traffic(args.config)
+    ws = metrics.weight_bytes(config, mode) + 2 * config.layers * config.width * config.window * metrics.ELEM_BYTES[mode]
+    line = {
+        "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": max_elapsed * 1000.0 / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": mode, "data": "synthetic",
+        "config": config_json(args, config, mode, ws),
+        "p50_us_per_step_device": us,
+        "e2e": {"value": world * K / max_e2e, "unit": "steps/s", "h2d_bytes_per_step": 4 * config.features,
+                "d2h_bytes_per_step": 4, "p50_us": metrics.nearest_rank(e2e_lat, 0.5),
+                "p99_us": metrics.nearest_rank(e2e_lat, 0.99),
+                "path": "Runtime.step -> st_step, persistent mailbox, mapped pinned input/score, host clock"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "kernel": f"k_trace ({mode})",
+                     "algorithmic_bytes_per_step": alg / K, "peak_source": peak_src,
+                     "traffic_source": traffic_src},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "runtime": {"blocks": info.get("blocks"), "threads": info.get("threads"),
+                    "registers_per_thread": info.get("registers_per_thread"),
+                    "barriers_per_step": info.get("barriers_per_step")},
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        sps, n, dt = time_cpu_oracle(model, events, 1, args.cpu_seconds, K)
+        line["cpu_baseline"] = {
+            "value": sps, "unit": "steps/s", "cores": 1, "kind": "port",
+            "sample": f"{n} events from reset, C restatement of the reference CPU step, 1 thread, {dt:.1f} s"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

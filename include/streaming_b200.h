@@ -136,6 +136,17 @@ int st_snapshot(st_runtime* rt, int stream, uint64_t* position, float* keys,
 int st_load_state(st_runtime* rt, int stream, uint64_t position, const float* keys,
                   const float* values, const float* hidden);
 
+/* Per-op snapshot callback: name as in the reference trace ("input",
+ * "layers.<l>.q", "layers.<l>.k", "layers.<l>.v", "layers.<l>.attention",
+ * "layers.<l>.attention_residual", "layers.<l>.activation", "layers.<l>.hidden",
+ * "score.linear"), values widened to float. */
+typedef void (*st_trace_fn)(void* user, const char* name, const float* data, size_t count);
+
+/* One step of stream 0 with a synchronizing snapshot after every phase kernel
+ * (reference Runtime::traceStep, src/cuda/Runtime.cu:476-546). CUDA backend and
+ * streams == 1 only, as in the reference. State advances exactly as st_step. */
+int st_trace_step(st_runtime* rt, const float* input, float* score, st_trace_fn fn, void* user);
+
 /* Device-only timing over a preloaded host trace of `count` events
  * ([count][streams][features]): resets, then steps every event on the device
  * and reports microseconds per step from CUDA events (reference

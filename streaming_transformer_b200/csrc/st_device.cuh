@@ -76,6 +76,7 @@ struct StepArgs {
   int* error;                         // first error code, 0 = none (device memory)
   int* host_error;                    // mapped host mirror of the error word (may be null)
   unsigned long long bar_timeout_ns;  // bound on any single barrier wait
+  float* trace_attention;             // [S][d] merged attention, diagnostics only (null in timed paths)
 };
 
 // ---------------------------------------------------------------- storage types
@@ -507,6 +508,7 @@ __device__ void merge_attention(const StepArgs& a, int s, Smem& sm) {
       acc = fmaf(ld_cg(pc + 2 + dd), scale, acc);
     }
     sm.xs[e] = Storage<T>::round(acc / L);
+    if (a.trace_attention && blockIdx.x == 0) a.trace_attention[(size_t)s * a.width + e] = sm.xs[e];
   }
   __syncthreads();
 }

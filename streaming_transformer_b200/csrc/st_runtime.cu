@@ -589,7 +589,7 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   so = align_up(so + S * sizeof(unsigned long long), 256);
   rt->state_bytes = so;
   if (rt->cuda(cudaMalloc(&rt->state, so), "cudaMalloc state") != ST_OK) return bail(ST_ERR_CUDA);
-  if (rt->cuda(cudaMemset(rt->state, 0, so), "cudaMemset state") != ST_OK) return bail(ST_ERR_CUDA);
+  if (rt->cuda(cudaMemsetAsync(rt->state, 0, so, rt->stream), "cudaMemset state") != ST_OK) return bail(ST_ERR_CUDA);
 
   // ---- scratch
   const int nch = (m.window + kAttChunk - 1) / kAttChunk;
@@ -602,10 +602,12 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   const size_t rope_at = take((hd / 2) * sizeof(float)), ctl_at = take(sizeof(Control));
   rt->scratch_bytes = co;
   if (rt->cuda(cudaMalloc(&rt->scratch, co), "cudaMalloc scratch") != ST_OK) return bail(ST_ERR_CUDA);
-  if (rt->cuda(cudaMemset(rt->scratch, 0, co), "cudaMemset scratch") != ST_OK) return bail(ST_ERR_CUDA);
+  if (rt->cuda(cudaMemsetAsync(rt->scratch, 0, co, rt->stream), "cudaMemset scratch") != ST_OK) return bail(ST_ERR_CUDA);
   std::vector<float> freq(hd / 2);
   for (int i = 0; i < hd; i += 2) freq[i / 2] = powf(10000.0f, -(float)i / (float)hd);
-  if (rt->cuda(cudaMemcpy(rt->scratch + rope_at, freq.data(), freq.size() * 4, cudaMemcpyHostToDevice), "rope table") != ST_OK)
+  if (rt->cuda(cudaMemcpyAsync(rt->scratch + rope_at, freq.data(), freq.size() * 4, cudaMemcpyHostToDevice, rt->stream),
+               "rope table") != ST_OK ||
+      rt->cuda(cudaStreamSynchronize(rt->stream), "rope table") != ST_OK)
     return bail(ST_ERR_CUDA);
 
   // ---- mapped pinned memory
@@ -671,7 +673,9 @@ int st_set_tensor(st_runtime* rt, const char* name, const float* data, size_t co
   if (count != (size_t)s.rows * s.cols) return rt->fail(ST_ERR_INVALID, "Shape mismatch: %s", name);
   float* tmp = nullptr;
   ST_CUDA(rt, cudaMalloc(&tmp, count * sizeof(float)));
-  int st = rt->cuda(cudaMemcpy(tmp, data, count * sizeof(float), cudaMemcpyHostToDevice), "tensor upload");
+  // Stream-ordered: a pageable cudaMemcpy may return before its DMA lands, and
+  // the non-blocking stream is not ordered after the legacy stream.
+  int st = rt->cuda(cudaMemcpyAsync(tmp, data, count * sizeof(float), cudaMemcpyHostToDevice, rt->stream), "tensor upload");
   if (st == ST_OK) {
     const int blocks = (int)std::min<size_t>((count + 255) / 256, 4096);
     void* dst = rt->weights + s.offset;
@@ -812,7 +816,7 @@ int st_load_state(st_runtime* rt, int stream, uint64_t position, const float* ke
   for (int which = 0; which < 2 && st == ST_OK; ++which) {
     const float* src = which == 0 ? keys : values;
     char* base = (char*)(which == 0 ? rt->args.keys : rt->args.values) + (size_t)stream * cache * rt->elem;
-    st = rt->cuda(cudaMemcpy(tmp, src, cache * sizeof(float), cudaMemcpyHostToDevice), "state upload");
+    st = rt->cuda(cudaMemcpyAsync(tmp, src, cache * sizeof(float), cudaMemcpyHostToDevice, rt->stream), "state upload");
     if (st != ST_OK) break;
     const int rows = (int)(cache / hd), blocks = (int)std::min<size_t>((cache + 255) / 256, 4096);
     if (m.mode == ST_MODE_FP16) k_convert<__half><<<blocks, 256, 0, rt->stream>>>(tmp, (__half*)base, rows, hd, 1, 0);
@@ -825,8 +829,106 @@ int st_load_state(st_runtime* rt, int stream, uint64_t position, const float* ke
   ST_TRY(st);
   const size_t n = (size_t)m.layers * m.width;
   unsigned long long p = position;
-  ST_CUDA(rt, cudaMemcpy(rt->args.hidden + (size_t)stream * n, hidden, n * 4, cudaMemcpyHostToDevice));
-  ST_CUDA(rt, cudaMemcpy(rt->args.position + stream, &p, sizeof p, cudaMemcpyHostToDevice));
+  ST_CUDA(rt, cudaMemcpyAsync(rt->args.hidden + (size_t)stream * n, hidden, n * 4, cudaMemcpyHostToDevice, rt->stream));
+  ST_CUDA(rt, cudaMemcpyAsync(rt->args.position + stream, &p, sizeof p, cudaMemcpyHostToDevice, rt->stream));
+  ST_CUDA(rt, cudaStreamSynchronize(rt->stream));
+  return ST_OK;
+}
+
+}  // extern "C"
+
+template <typename T>
+static int trace_step_t(st_runtime* rt, st_trace_fn fn, void* user) {
+  const st_model_desc& m = rt->desc;
+  const int d = m.width, F = m.ffn, hd = d / m.heads, W = m.window;
+  const dim3 g(rt->grid), b(kThreads);
+  cudaStream_t s = rt->stream;
+  StepArgs a = rt->args;
+  float* attn = nullptr;
+  ST_CUDA(rt, cudaMalloc(&attn, d * sizeof(float)));
+  a.trace_attention = attn;
+  std::vector<float> buf(std::max(d, F));
+  auto emit = [&](const std::string& name, const float* dev, int count) -> int {
+    ST_CUDA(rt, cudaStreamSynchronize(s));
+    ST_CUDA(rt, cudaMemcpy(buf.data(), dev, count * sizeof(float), cudaMemcpyDeviceToHost));
+    fn(user, name.c_str(), buf.data(), (size_t)count);
+    return ST_OK;
+  };
+  auto emit_slot = [&](const std::string& name, const void* ring, int l, uint64_t t) -> int {
+    ST_CUDA(rt, cudaStreamSynchronize(s));
+    const int slot = (int)(t % (uint64_t)W);
+    std::vector<uint16_t> raw(hd);
+    for (int h = 0; h < m.heads; ++h) {
+      const size_t at = (((size_t)l * m.heads + h) * W + slot) * hd;
+      if (m.mode == ST_MODE_FP32) {
+        ST_CUDA(rt, cudaMemcpy(buf.data() + h * hd, (const float*)ring + at, hd * 4, cudaMemcpyDeviceToHost));
+      } else {
+        ST_CUDA(rt, cudaMemcpy(raw.data(), (const uint16_t*)ring + at, hd * 2, cudaMemcpyDeviceToHost));
+        for (int i = 0; i < hd; ++i)
+          buf[h * hd + i] = m.mode == ST_MODE_FP16 ? half_bits_to_float(raw[i]) : bf16_bits_to_float(raw[i]);
+      }
+    }
+    fn(user, name.c_str(), buf.data(), (size_t)d);
+    return ST_OK;
+  };
+  unsigned long long t = 0;
+  int st = rt->cuda(cudaMemcpy(&t, a.position, sizeof t, cudaMemcpyDeviceToHost), "position");
+  auto run = [&]() -> int {
+    ST_TRY(st);
+    k_input<T><<<g, b, 0, s>>>(a);
+    ST_TRY(emit("input", a.x, d));
+    for (int l = 0; l < m.layers; ++l) {
+      const std::string p = "layers." + std::to_string(l) + ".";
+      k_qkv<T><<<g, b, 0, s>>>(a, l);
+      ST_TRY(emit(p + "q", a.q, d));
+      ST_TRY(emit_slot(p + "k", a.keys, l, t));
+      ST_TRY(emit_slot(p + "v", a.values, l, t));
+      k_attention<T><<<g, b, 0, s>>>(a, l);
+      k_out<T><<<g, b, 0, s>>>(a, l);
+      ST_TRY(emit(p + "attention", attn, d));
+      ST_TRY(emit(p + "attention_residual", a.x2, d));
+      k_ffn_in<T><<<g, b, 0, s>>>(a, l);
+      ST_TRY(emit(p + "activation", a.act, F));
+      k_ffn_out<T><<<g, b, 0, s>>>(a, l);
+      ST_TRY(emit(p + "hidden", a.x, d));
+    }
+    k_final<T><<<dim3(1), b, 0, s>>>(a);
+    ST_TRY(emit("score.linear", a.score, 1));
+    rt->launches += 2 + 5ull * m.layers;
+    return rt->cuda(cudaGetLastError(), "trace launches");
+  };
+  st = run();
+  cudaFree(attn);
+  return st;
+}
+
+extern "C" {
+
+int st_trace_step(st_runtime* rt, const float* input, float* score, st_trace_fn fn, void* user) {
+  if (!rt || !input || !fn) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
+  if (rt->opt.backend != ST_BACKEND_CUDA) return rt->fail(ST_ERR_INVALID, "traceStep requires conventional custom CUDA");
+  if (rt->desc.streams != 1) return rt->fail(ST_ERR_INVALID, "traceStep supports one stream");
+  const size_t n = (size_t)rt->desc.features;
+  std::memcpy(rt->in_h, input, n * sizeof(float));
+  if (!rt->opt.mapped)
+    ST_CUDA(rt, cudaMemcpyAsync(rt->dev_input, rt->in_h, n * 4, cudaMemcpyHostToDevice, rt->stream));
+  int st;
+  switch (rt->desc.mode) {
+    case ST_MODE_FP16: st = trace_step_t<__half>(rt, fn, user); break;
+    case ST_MODE_BF16: st = trace_step_t<__nv_bfloat16>(rt, fn, user); break;
+    default: st = trace_step_t<float>(rt, fn, user); break;
+  }
+  ST_TRY(st);
+  ST_CUDA(rt, cudaStreamSynchronize(rt->stream));
+  ST_TRY(check_device_error(rt));
+  if (score) {
+    float v = 0;
+    if (rt->opt.mapped) v = rt->out_h[0];
+    else ST_CUDA(rt, cudaMemcpy(&v, rt->dev_score, 4, cudaMemcpyDeviceToHost));
+    *score = v;
+  }
   return ST_OK;
 }
 
@@ -875,10 +977,11 @@ int st_device_trace(st_runtime* rt, const float* inputs, size_t count, float* sc
   float* dev_scores = nullptr;
   ST_CUDA(rt, cudaMalloc(&dev, n * 4));
   int st = rt->cuda(cudaMalloc(&dev_scores, count * (size_t)S * 4), "cudaMalloc scores");
-  if (st == ST_OK) st = rt->cuda(cudaMemcpy(dev, inputs, n * 4, cudaMemcpyHostToDevice), "trace upload");
+  if (st == ST_OK) st = rt->cuda(cudaMemcpyAsync(dev, inputs, n * 4, cudaMemcpyHostToDevice, rt->stream), "trace upload");
   if (st == ST_OK) st = device_trace_impl(rt, dev, count, dev_scores, us_per_step);
   if (st == ST_OK && scores)
-    st = rt->cuda(cudaMemcpy(scores, dev_scores, count * (size_t)S * 4, cudaMemcpyDeviceToHost), "scores download");
+    st = rt->cuda(cudaMemcpyAsync(scores, dev_scores, count * (size_t)S * 4, cudaMemcpyDeviceToHost, rt->stream), "scores download");
+  if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "scores download");
   cudaFree(dev);
   cudaFree(dev_scores);
   return st;

@@ -92,6 +92,7 @@ class _Options(ctypes.Structure):
 
 _lib = None
 F = ctypes.POINTER(ctypes.c_float)
+TRACE_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float), ctypes.c_size_t)
 
 
 def library() -> ctypes.CDLL:
@@ -114,6 +115,7 @@ def library() -> ctypes.CDLL:
             "st_stop": (I, [P]),
             "st_snapshot": (I, [P, I, ctypes.POINTER(U64), F, F, F]),
             "st_load_state": (I, [P, I, U64, F, F, F]),
+            "st_trace_step": (I, [P, F, F, TRACE_FN, P]),
             "st_device_trace": (I, [P, F, S, F, ctypes.POINTER(ctypes.c_double)]),
             "st_device_trace_resident": (I, [P, ctypes.c_void_p, S, ctypes.POINTER(ctypes.c_double),
                                              ctypes.POINTER(U64)]),
@@ -162,6 +164,12 @@ class Runtime:
     Owns every device and pinned buffer; ``close()`` (or garbage collection)
     stops the resident worker before freeing them (reference
     src/cuda/Runtime.cu:294-299).
+
+    With the PERSISTENT backend a kernel stays resident on the device between
+    steps. A device-wide synchronize (``cudaDeviceSynchronize``,
+    ``torch.cuda.synchronize()``) issued meanwhile waits for that kernel, i.e.
+    until ``stop()`` or the idle budget ends it; synchronize individual
+    streams instead.
     """
 
     def __init__(self, model: Model, options: RuntimeOptions | None = None, streams: int = 1):
@@ -251,6 +259,19 @@ class Runtime:
         v = np.ascontiguousarray(values, dtype=np.float32)
         h = np.ascontiguousarray(hidden, dtype=np.float32)
         _check(library().st_load_state(self._h, int(stream), int(position), _fptr(k), _fptr(v), _fptr(h)), self._h)
+
+    def trace_step(self, event) -> dict[str, np.ndarray]:
+        """reference Runtime::traceStep: one step with per-op snapshots (CUDA backend)."""
+        trace: dict[str, np.ndarray] = {}
+
+        def capture(_user, name, data, count):
+            trace[name.decode()] = np.ctypeslib.as_array(data, shape=(count,)).copy()
+
+        cb = TRACE_FN(capture)
+        self._in[0, :] = np.asarray(event, dtype=np.float32).reshape(-1)[: self.config.features]
+        score = np.zeros(1, dtype=np.float32)
+        _check(library().st_trace_step(self._h, _fptr(self._in), _fptr(score), cb, None), self._h)
+        return trace
 
     def info(self) -> dict:
         return _json_call(library().st_info, self._h)
