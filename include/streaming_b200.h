@@ -160,6 +160,37 @@ int st_device_trace(st_runtime* rt, const float* inputs, size_t count, float* sc
 int st_device_trace_resident(st_runtime* rt, const float* device_inputs, size_t count,
                              double* us_per_step, uint64_t* kernel_launches);
 
+/* Allocation-free attention. No counterpart in the reference.
+ *
+ * Split-window attention over one layer's K/V ring, as the step computes it,
+ * for callers that cannot allocate device memory: code that runs where
+ * cudaMalloc is not allowed or not safe (a stream host callback, a process
+ * whose device memory pool belongs to another framework, a real-time loop
+ * that may not take the allocator's locks). Its chunk partials live in a fixed
+ * device array of ST_ATTENTION_STATIC_MAX_FLOATS floats (1 MiB) compiled into
+ * this library, which every GPU that loads the library keeps until the process
+ * exits. The call allocates and frees nothing.
+ *
+ *   q       [heads * head_dim] float, device memory, already rotated
+ *   keys    [heads][window][head_dim] storage type of `mode`, device memory
+ *   values  same layout as keys
+ *   out     [heads * head_dim] float, device memory; rounded to the storage
+ *           precision like the step's attention output
+ * position is the absolute position of the current event: ring slots
+ * 0 .. min(position + 1, window) - 1 are attended. Work is queued on `stream`
+ * (a cudaStream_t, NULL for the legacy stream); the call returns without
+ * waiting. The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture. Every call shares the one array and overwrites
+ * the previous call's partials, so calls that may overlap on the GPU (other
+ * streams, other host threads) race and must be serialized by the caller.
+ * Sizes needing more than the array holds are rejected with ST_ERR_INVALID;
+ * the message is in st_attention_static_error(). */
+#define ST_ATTENTION_STATIC_MAX_FLOATS 262144
+int st_attention_static(int device, int mode, int heads, int head_dim, int window, uint64_t position,
+                        const float* q, const void* keys, const void* values, float* out, void* stream);
+const char* st_attention_static_error(void);
+
 /* JSON description of the runtime: options, grid, kernel resources, layout
  * (reference Runtime::info, src/cuda/Runtime.cu:570-594). Writes at most
  * capacity bytes including the terminator; *needed gets the full length. */
