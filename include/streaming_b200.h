@@ -155,6 +155,13 @@ int st_trace_step(st_runtime* rt, const float* input, float* score, st_trace_fn 
 int st_device_trace(st_runtime* rt, const float* inputs, size_t count, float* scores,
                     double* us_per_step);
 
+/* Diagnostic device timeline: like st_device_trace (FUSED/PERSISTENT device
+ * loop), with CTA 0 recording clock64() at every phase boundary of every step
+ * into marks[0..capacity); *used receives the number written. New; the
+ * reference exposes no intra-step timing. */
+int st_device_timeline(st_runtime* rt, const float* inputs, size_t count, long long* marks, size_t capacity,
+                       size_t* used);
+
 /* Same, but `inputs` is a device pointer already resident in HBM and no score is
  * copied back; *kernel_launches receives the number of kernels launched. */
 int st_device_trace_resident(st_runtime* rt, const float* device_inputs, size_t count,
@@ -198,6 +205,15 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed);
 
 /* JSON device probe (reference deviceProbe/probe(), src/cuda/Runtime.cu:134-161). */
 int st_probe(int device, char* json, size_t capacity, size_t* needed);
+
+/* Transport and synchronization calibration (reference transportBench,
+ * src/cuda/Runtime.cu:706-814): mode "empty", "empty-graph", "copy",
+ * "ping-pong", "gpu-ping", or "grid-barrier" (device ns per grid barrier of the
+ * step kernels, one 512-thread CTA per SM). Writes a JSON report; csv_path
+ * (may be NULL) receives per-event samples. On error see st_transport_error(). */
+int st_transport_bench(int device, const char* mode, size_t count, int backoff, const char* csv_path,
+                       char* json, size_t capacity, size_t* needed);
+const char* st_transport_error(void);
 
 /* Kernels launched by this runtime since creation (for launch-count reporting). */
 uint64_t st_kernel_launches(const st_runtime* rt);

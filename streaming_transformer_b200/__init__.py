@@ -7,8 +7,8 @@ include/Runtime.hpp as the C++ one.
 """
 from .model import CheckpointError, Model, ModelConfig, tensor_shapes, write_checkpoint
 from .runtime import (Backend, BACKEND_NAMES, Runtime, RuntimeOptions, Snapshot, StreamError,
-                      library, probe)
+                      library, probe, transport_bench)
 
 __all__ = ["Backend", "BACKEND_NAMES", "CheckpointError", "Model", "ModelConfig", "Runtime",
-           "RuntimeOptions", "Snapshot", "StreamError", "library", "probe", "tensor_shapes",
+           "RuntimeOptions", "Snapshot", "StreamError", "library", "probe", "tensor_shapes", "transport_bench",
            "write_checkpoint"]

@@ -39,16 +39,16 @@ constexpr int kAttChunk = 32;               // ring slots per attention work ite
 constexpr int kMaxLayers = 16;
 constexpr int kUnroll = 8;                  // 16-byte loads in flight per lane
 
-enum ErrorCode : int { kOk = 0, kBarrierTimeout = 1, kAborted = 2 };
+enum ErrorCode : int { kOk = 0, kBarrierTimeout = 1, kAborted = 2, kClusterShape = 3 };
 enum Command : int { kRun = 1, kReset = 2, kStop = 3, kPing = 4 };
 
 struct LayerPtrs {
   const void* norm1;
   const void* norm2;
-  const void* qkv;     // [3d, d]: q rows, then k rows, then v rows
-  const void* out;     // [d, d]
+  const void* qkv;     // [H][3][hd][d]: per head its q rows, k rows, v rows
+  const void* out;     // [H][d][hd]: per head the out-projection columns it feeds
   const void* gateup;  // [2F, d]: row 2i = gate_i, row 2i+1 = up_i
-  const void* down;    // [d, F]
+  const void* down;    // [F][d]: W_down transposed
 };
 
 // Everything a step needs; passed by value to every kernel.
@@ -66,17 +66,25 @@ struct StepArgs {
   float* hidden;                      // [S][L][d]
   unsigned long long* position;       // [S]
   const float* input;                 // [S][features] (device or mapped host)
-  float* x;                           // [S][d] residual after each layer
-  float* x2;                          // [S][d] residual after attention
-  float* q;                           // [S][d] rotated, cast query
-  float* part;                        // [S][H][nchunks_max][hd + 2] attention partials
-  float* act;                         // [S][F] SwiGLU output
+  float* x;                           // [S][d] residual entering / leaving a layer (per-op backends)
+  float* x2;                          // [S][d] residual after attention (per-op backends)
+  float* q;                           // [S][d] rotated, cast query (op-level attention)
+  float* part;                        // [S][H][nchunks_max][hd + 2] op-level attention partials
+  float* act;                         // unused by the step kernels
   float* score;                       // [S]
   unsigned long long* bar_counter;    // grid barrier arrivals (monotonic)
   int* error;                         // first error code, 0 = none (device memory)
   int* host_error;                    // mapped host mirror of the error word (may be null)
   unsigned long long bar_timeout_ns;  // bound on any single barrier wait
+  float* pout;                        // [S][H][d] out-projection partial per head
+  float* dpart;                       // [S][clusters][d] down-projection partial per cluster
   float* trace_attention;             // [S][d] merged attention, diagnostics only (null in timed paths)
+  float* trace_qkv;                   // [S][3][d] rotated q, k and v, diagnostics only
+  float* trace_act;                   // [S][F] SwiGLU output, diagnostics only
+  long long* timeline;                // CTA 0 clock64() at phase boundaries, diagnostics only
+  int timeline_capacity;
+  int cluster_size;                   // CTAs per cluster the buffers were sized for
+  int clusters;                       // clusters in the grid (sizes dpart)
 };
 
 // ---------------------------------------------------------------- storage types
@@ -361,67 +369,9 @@ __device__ void cta_gemv(const T* W, int rows, int cols, int unit, Smem& sm, Epi
 }
 
 // ---------------------------------------------------------------- phases
-__device__ __forceinline__ unsigned long long stream_position(const StepArgs& a, int s) {
-  return ld_cg_u64(a.position + s);
-}
 
-// x = cast(W_in * input) (reference src/cpu/Cpu.cpp:65).
-template <typename T>
-__device__ void phase_input(const StepArgs& a, const float* input, Smem& sm) {
-  for (int s = 0; s < a.streams; ++s) {
-    for (int i = threadIdx.x; i < a.features; i += kThreads) sm.xs[i] = __ldcv(input + (size_t)s * a.features + i);
-    __syncthreads();
-    float* x = a.x + (size_t)s * a.width;
-    cta_gemv<T>((const T*)a.input_w, a.width, a.features, 1, sm, [&](int r0, int n) {
-      for (int i = threadIdx.x; i < n; i += kThreads) x[r0 + i] = Storage<T>::round(sm.rowsum[i]);
-    });
-  }
-}
-
-// norm1 -> q,k,v = cast(W z) -> RoPE on adjacent pairs, cast -> k,v into ring
-// slot t % W (reference src/cpu/Cpu.cpp:69-96, Primitives.cuh:144-166).
-template <typename T>
-__device__ void phase_qkv(const StepArgs& a, int l, Smem& sm) {
-  const int d = a.width, hd = a.head_dim, H = a.heads, W = a.window;
-  const LayerPtrs& w = a.layer[l];
-  for (int s = 0; s < a.streams; ++s) {
-    const unsigned long long t = stream_position(a, s);
-    const int slot = (int)(t % (unsigned long long)W);
-    norm_to_smem<T>(a.x + (size_t)s * d, (const T*)w.norm1, d, a.epsilon, sm);
-    T* keys = (T*)a.keys + (((size_t)s * a.layers + l) * H) * (size_t)W * hd;
-    T* values = (T*)a.values + (((size_t)s * a.layers + l) * H) * (size_t)W * hd;
-    float* q = a.q + (size_t)s * d;
-    const float tf = (float)t;
-    cta_gemv<T>((const T*)w.qkv, 3 * d, d, 2, sm, [&](int r0, int n) {
-      for (int p = threadIdx.x; p < n / 2; p += kThreads) {
-        const int row = r0 + 2 * p;
-        const int which = row / d, within = row - which * d;
-        const int head = within / hd, dim = within - head * hd;
-        float v0 = Storage<T>::round(sm.rowsum[2 * p]);
-        float v1 = Storage<T>::round(sm.rowsum[2 * p + 1]);
-        if (which < 2) {
-          const float angle = tf * a.rope_freq[dim >> 1];
-          const float co = cosf(angle), si = sinf(angle);
-          const float r0v = v0 * co - v1 * si;
-          const float r1v = v0 * si + v1 * co;
-          v0 = Storage<T>::round(r0v);
-          v1 = Storage<T>::round(r1v);
-        }
-        if (which == 0) {
-          q[within] = v0;
-          q[within + 1] = v1;
-        } else {
-          T* ring = which == 1 ? keys : values;
-          const size_t at = ((size_t)head * W + slot) * hd + dim;
-          Storage<T>::store(ring, at, v0);
-          Storage<T>::store(ring, at + 1, v1);
-        }
-      }
-    });
-  }
-}
-
-// One (stream, head, chunk of <= 32 ring slots) work item per warp: logits
+// One (stream, head, chunk of <= 32 ring slots) work item per warp, used by the
+// op-level attention entry point (st_static.cu).
 // q.K/sqrt(hd), chunk max, exp, sum and sum p*V -> partial (m, l, acc[hd]).
 // Physical ring slots [0, valid) are the retained history; softmax does not
 // depend on their order (reference src/cpu/Cpu.cpp:97-110).
@@ -466,127 +416,6 @@ __device__ void attention_item(const StepArgs& a, int l, int s, int h, int c, in
   }
 }
 
-template <typename T>
-__device__ void phase_attention(const StepArgs& a, int l) {
-  const int warp = threadIdx.x >> 5;
-  const int gw = blockIdx.x * kWarps + warp, nw = gridDim.x * kWarps;
-  const int H = a.heads, C = a.nchunks_max;
-  const int items = a.streams * H * C;
-  const int dpl = (a.head_dim + 31) / 32;
-  for (int it = gw; it < items; it += nw) {
-    const int s = it / (H * C), rem = it - s * H * C;
-    const int h = rem / C, c = rem - h * C;
-    const unsigned long long t = stream_position(a, s);
-    const int valid = t + 1 < (unsigned long long)a.window ? (int)(t + 1) : a.window;
-    if (c * kAttChunk >= valid) continue;
-    if (dpl <= 1) attention_item<T, 1>(a, l, s, h, c, valid);
-    else if (dpl <= 2) attention_item<T, 2>(a, l, s, h, c, valid);
-    else if (dpl <= 4) attention_item<T, 4>(a, l, s, h, c, valid);
-    else if (dpl <= 8) attention_item<T, 8>(a, l, s, h, c, valid);
-    else attention_item<T, 32>(a, l, s, h, c, valid);
-  }
-}
-
-// Merge the chunk partials of one stream into sm.xs = cast(attention) (all threads).
-template <typename T>
-__device__ void merge_attention(const StepArgs& a, int s, Smem& sm) {
-  const int hd = a.head_dim, H = a.heads, C = a.nchunks_max;
-  const unsigned long long t = stream_position(a, s);
-  const int valid = t + 1 < (unsigned long long)a.window ? (int)(t + 1) : a.window;
-  const int nc = (valid + kAttChunk - 1) / kAttChunk;
-  const float* part = a.part + (size_t)s * H * C * (hd + 2);
-  for (int e = threadIdx.x; e < a.width; e += kThreads) {
-    const int h = e / hd, dd = e - h * hd;
-    const float* ph = part + (size_t)h * C * (hd + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < nc; ++c) M = fmaxf(M, ld_cg(ph + (size_t)c * (hd + 2)));
-    float L = 0.f, acc = 0.f;
-    for (int c = 0; c < nc; ++c) {
-      const float* pc = ph + (size_t)c * (hd + 2);
-      const float scale = expf(ld_cg(pc) - M);
-      L = fmaf(ld_cg(pc + 1), scale, L);
-      acc = fmaf(ld_cg(pc + 2 + dd), scale, acc);
-    }
-    sm.xs[e] = Storage<T>::round(acc / L);
-    if (a.trace_attention && blockIdx.x == 0) a.trace_attention[(size_t)s * a.width + e] = sm.xs[e];
-  }
-  __syncthreads();
-}
-
-// attention -> cast(W_out a) -> x2 = cast(x + out) (reference src/cpu/Cpu.cpp:111-118).
-template <typename T>
-__device__ void phase_out(const StepArgs& a, int l, Smem& sm) {
-  const int d = a.width;
-  for (int s = 0; s < a.streams; ++s) {
-    merge_attention<T>(a, s, sm);
-    const float* x = a.x + (size_t)s * d;
-    float* x2 = a.x2 + (size_t)s * d;
-    cta_gemv<T>((const T*)a.layer[l].out, d, d, 1, sm, [&](int r0, int n) {
-      for (int i = threadIdx.x; i < n; i += kThreads)
-        x2[r0 + i] = Storage<T>::round(ld_cg(x + r0 + i) + Storage<T>::round(sm.rowsum[i]));
-    });
-  }
-}
-
-// norm2 -> gate, up = cast(W z) -> act = cast(silu(gate) * up)
-// (reference src/cpu/Cpu.cpp:120-126).
-template <typename T>
-__device__ void phase_ffn_in(const StepArgs& a, int l, Smem& sm) {
-  const int d = a.width, F = a.ffn;
-  const LayerPtrs& w = a.layer[l];
-  for (int s = 0; s < a.streams; ++s) {
-    norm_to_smem<T>(a.x2 + (size_t)s * d, (const T*)w.norm2, d, a.epsilon, sm);
-    float* act = a.act + (size_t)s * F;
-    cta_gemv<T>((const T*)w.gateup, 2 * F, d, 2, sm, [&](int r0, int n) {
-      for (int p = threadIdx.x; p < n / 2; p += kThreads) {
-        const float g = Storage<T>::round(sm.rowsum[2 * p]);
-        const float u = Storage<T>::round(sm.rowsum[2 * p + 1]);
-        act[(r0 >> 1) + p] = Storage<T>::round((g / (1.0f + expf(-g))) * u);
-      }
-    });
-  }
-}
-
-// act -> cast(W_down act) -> x = cast(x2 + down); hidden[l] = x
-// (reference src/cpu/Cpu.cpp:128-134).
-template <typename T>
-__device__ void phase_ffn_out(const StepArgs& a, int l, Smem& sm) {
-  const int d = a.width, F = a.ffn;
-  for (int s = 0; s < a.streams; ++s) {
-    const float* act = a.act + (size_t)s * F;
-    for (int i = threadIdx.x; i < F; i += kThreads) sm.xs[i] = ld_cg(act + i);
-    __syncthreads();
-    const float* x2 = a.x2 + (size_t)s * d;
-    float* x = a.x + (size_t)s * d;
-    float* hidden = a.hidden + ((size_t)s * a.layers + l) * d;
-    cta_gemv<T>((const T*)a.layer[l].down, d, F, 1, sm, [&](int r0, int n) {
-      for (int i = threadIdx.x; i < n; i += kThreads) {
-        const float v = Storage<T>::round(ld_cg(x2 + r0 + i) + Storage<T>::round(sm.rowsum[i]));
-        x[r0 + i] = v;
-        hidden[r0 + i] = v;
-      }
-    });
-  }
-}
-
-// Final norm and score head without a cast, then position++ (CTA 0 only;
-// reference src/cpu/Cpu.cpp:136-140, Primitives.cuh:270-276).
-template <typename T>
-__device__ void phase_final(const StepArgs& a, Smem& sm) {
-  if (blockIdx.x != 0) return;
-  for (int s = 0; s < a.streams; ++s) {
-    norm_to_smem<T>(a.x + (size_t)s * a.width, (const T*)a.final_norm, a.width, a.epsilon, sm);
-    // one row: block-wide dot product
-    float acc = 0.f;
-    for (int i = threadIdx.x; i < a.width; i += kThreads)
-      acc = fmaf(Storage<T>::load((const T*)a.score_w, i), sm.xs[i], acc);
-    const float total = block_sum(acc, sm);
-    if (threadIdx.x == 0) a.score[s] = total;
-    __syncthreads();
-  }
-  for (int s = threadIdx.x; s < a.streams; s += kThreads) a.position[s] = ld_cg_u64(a.position + s) + 1;
-}
-
 // Zero K/V/hidden and position for streams [s0, s1) (reference
 // src/cuda/Primitives.cuh:280-292), grid-stride over all CTAs.
 template <typename T>
@@ -603,30 +432,5 @@ __device__ void reset_streams(const StepArgs& a, int s0, int s1) {
   if (blockIdx.x == 0)
     for (int s = s0 + threadIdx.x; s < s1; s += kThreads) a.position[s] = 0ull;
 }
-
-// One full step across the grid, barriers between phases. Returns false if a
-// barrier gave up (the error word is set).
-template <typename T>
-__device__ bool forward(const StepArgs& a, const float* input, GridSync& gs, Smem& sm) {
-  phase_input<T>(a, input, sm);
-  if (!gs.sync(a, a.bar_timeout_ns)) return false;
-  for (int l = 0; l < a.layers; ++l) {
-    phase_qkv<T>(a, l, sm);
-    if (!gs.sync(a, a.bar_timeout_ns)) return false;
-    phase_attention<T>(a, l);
-    if (!gs.sync(a, a.bar_timeout_ns)) return false;
-    phase_out<T>(a, l, sm);
-    if (!gs.sync(a, a.bar_timeout_ns)) return false;
-    phase_ffn_in<T>(a, l, sm);
-    if (!gs.sync(a, a.bar_timeout_ns)) return false;
-    phase_ffn_out<T>(a, l, sm);
-    if (!gs.sync(a, a.bar_timeout_ns)) return false;
-  }
-  phase_final<T>(a, sm);
-  return true;
-}
-
-// Number of grid barriers forward() executes.
-__host__ __device__ inline int forward_barriers(int layers) { return 1 + 5 * layers; }
 
 }  // namespace st

@@ -1,16 +1,16 @@
 // st_kernels.cuh -- kernel entry points of the streaming step.
 //
-//   per-op (CUDA / GRAPH backends)   k_input, k_qkv, k_attention, k_out,
-//                                    k_ffn_in, k_ffn_out, k_final, k_reset
-//   FUSED                            k_fused: one cooperative launch per step
-//   device trace                     k_trace: a preloaded trace in one launch
-//   PERSISTENT                       k_persistent: resident, mapped mailbox
+//   per-op (CUDA / GRAPH backends)   k2_input, k2_attention, k2_ffn (cluster
+//                                    launches), k2_final, k_reset
+//   FUSED                            k2_fused: one cooperative cluster launch per step
+//   device trace                     k2_trace: a preloaded trace in one launch
+//   PERSISTENT                       k2_persistent: resident, mapped mailbox
 // They replace the reference's stage/input/norm/score/advance/reset kernels,
 // fused_kernel, trace_kernel and persistent_kernel (reference
 // src/cuda/Runtime.cu:16-132).
 #pragma once
 
-#include "st_device.cuh"
+#include "st_step.cuh"
 
 namespace st {
 
@@ -46,39 +46,32 @@ struct PersistArgs {
   int backoff;
 };
 
+#define ST_SMEM2 \
+  extern __shared__ __align__(16) unsigned char st_smem_raw[]; \
+  Smem2& sm = *reinterpret_cast<Smem2*>(st_smem_raw)
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) k_input(StepArgs a) {
-  __shared__ Smem sm;
-  phase_input<T>(a, a.input, sm);
+__global__ void __launch_bounds__(kThreads, 1) k2_input(StepArgs a) {
+  ST_SMEM2;
+  if (!cluster_shape_ok(a)) return;
+  op_input<T>(a, sm);
 }
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) k_qkv(StepArgs a, int l) {
-  __shared__ Smem sm;
-  phase_qkv<T>(a, l, sm);
+__global__ void __launch_bounds__(kThreads, 1) k2_attention(StepArgs a, int l) {
+  ST_SMEM2;
+  if (!cluster_shape_ok(a)) return;
+  op_attention<T>(a, l, sm);
 }
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) k_attention(StepArgs a, int l) {
-  phase_attention<T>(a, l);
+__global__ void __launch_bounds__(kThreads, 1) k2_ffn(StepArgs a, int l) {
+  ST_SMEM2;
+  if (!cluster_shape_ok(a)) return;
+  op_ffn<T>(a, l, sm);
 }
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) k_out(StepArgs a, int l) {
-  __shared__ Smem sm;
-  phase_out<T>(a, l, sm);
-}
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) k_ffn_in(StepArgs a, int l) {
-  __shared__ Smem sm;
-  phase_ffn_in<T>(a, l, sm);
-}
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) k_ffn_out(StepArgs a, int l) {
-  __shared__ Smem sm;
-  phase_ffn_out<T>(a, l, sm);
-}
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) k_final(StepArgs a) {
-  __shared__ Smem sm;
-  phase_final<T>(a, sm);
+__global__ void __launch_bounds__(kThreads, 1) k2_final(StepArgs a, int nclusters) {
+  ST_SMEM2;
+  op_final<T>(a, nclusters, sm);
 }
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) k_reset(StepArgs a, int s0, int s1) {
@@ -86,26 +79,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_reset(StepArgs a, int s0, int s
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) k_fused(StepArgs a, unsigned long long base) {
-  __shared__ Smem sm;
-  GridSync gs{base, 0};
-  forward<T>(a, a.input, gs, sm);
+__global__ void __launch_bounds__(kThreads, 1) k2_fused(StepArgs a, unsigned long long base) {
+  ST_SMEM2;
+  if (!cluster_shape_ok(a)) return;
+  ClusterGridSync gs{base, 0};
+  forward2<T>(a, a.input, gs, sm);
 }
 
 // Steps `count` preloaded events ([count][S][features], device memory) in one
-// launch. scores ([count][S]) may be null. One extra barrier per event keeps
-// the next input projection from overwriting x while CTA 0 still reads it.
+// launch. scores ([count][S]) may be null. The extra grid sync per event orders
+// CTA 0's position update before the next event reads the position.
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) k_trace(StepArgs a, const float* inputs, unsigned long long count,
-                                                      float* scores, unsigned long long base) {
-  __shared__ Smem sm;
-  GridSync gs{base, 0};
+__global__ void __launch_bounds__(kThreads, 1) k2_trace(StepArgs a, const float* inputs, unsigned long long count,
+                                                       float* scores, unsigned long long base) {
+  ST_SMEM2;
+  if (!cluster_shape_ok(a)) return;
+  ClusterGridSync gs{base, 0};
+  if (threadIdx.x == 0) sm.tl_n = 0;
+  __syncthreads();
   const size_t stride = (size_t)a.streams * a.features;
   for (unsigned long long e = 0; e < count; ++e) {
-    if (!forward<T>(a, inputs + e * stride, gs, sm)) return;
+    if (!forward2<T>(a, inputs + e * stride, gs, sm)) return;
     if (scores && blockIdx.x == 0)
       for (int s = threadIdx.x; s < a.streams; s += kThreads) scores[e * a.streams + s] = a.score[s];
-    if (!gs.sync(a, a.bar_timeout_ns)) return;
+    if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok)) return;
   }
 }
 
@@ -120,32 +117,44 @@ __device__ void persistent_exit(const StepArgs& a, const PersistArgs& p) {
 }
 
 // Resident worker (reference src/cuda/Runtime.cu:58-122): CTA 0 thread 0 polls
-// the mailbox within the idle budget and broadcasts the command; every CTA runs
-// it; CTA 0 publishes the score and the completion ID with release ordering.
+// the mailbox within the idle budget; on RUN, CTA 0 stages the mapped event
+// into device memory before the dispatch barrier (one PCIe read per value, by
+// one CTA); every CTA runs the command; CTA 0 publishes the score and the
+// completion ID with release ordering.
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) k_persistent(StepArgs a, PersistArgs p, unsigned long long base) {
-  __shared__ Smem sm;
+__global__ void __launch_bounds__(kThreads, 1) k2_persistent(StepArgs a, PersistArgs p, const float* mapped_input,
+                                                            unsigned long long base) {
+  ST_SMEM2;
   __shared__ Control local;
-  GridSync gs{base, 0};
+  if (!cluster_shape_ok(a)) { persistent_exit<T>(a, p); return; }
+  ClusterGridSync gs{base, 0};
   unsigned long long previous = p.initial_sequence, processed = 0;
+  const int nin = a.streams * a.features;
   while (true) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-      const unsigned long long start = globaltimer();
-      unsigned long long seq;
-      int exit = 0;
-      while ((seq = ld_acquire_sys(&p.mailbox->request)) == previous) {
-        if (globaltimer() - start >= p.idle_ns) { exit = 1; break; }
-        if (p.backoff) __nanosleep(128);
+    if (blockIdx.x == 0) {
+      if (threadIdx.x == 0) {
+        const unsigned long long start = globaltimer();
+        unsigned long long seq;
+        int exit = 0;
+        while ((seq = ld_acquire_sys(&p.mailbox->request)) == previous) {
+          if (globaltimer() - start >= p.idle_ns) { exit = 1; break; }
+          if (p.backoff) __nanosleep(128);
+        }
+        volatile Control* c = p.control;
+        c->exit = exit;
+        local.exit = exit;
+        if (!exit) {
+          local.command = *reinterpret_cast<volatile int*>(&p.mailbox->command);
+          c->sequence = seq;
+          c->command = local.command;
+          c->arg = *reinterpret_cast<volatile int*>(&p.mailbox->arg);
+        }
       }
-      volatile Control* c = p.control;
-      c->exit = exit;
-      if (!exit) {
-        c->sequence = seq;
-        c->command = *reinterpret_cast<volatile int*>(&p.mailbox->command);
-        c->arg = *reinterpret_cast<volatile int*>(&p.mailbox->arg);
-      }
+      __syncthreads();
+      if (!local.exit && local.command == kRun)
+        for (int i = threadIdx.x; i < nin; i += kThreads) const_cast<float*>(a.input)[i] = __ldcv(mapped_input + i);
     }
-    if (!gs.sync(a, p.dispatch_timeout_ns)) { persistent_exit<T>(a, p); return; }
+    if (!gs.sync(a, p.dispatch_timeout_ns, &sm.sync_ok)) { persistent_exit<T>(a, p); return; }
     if (threadIdx.x == 0) {
       const volatile Control* c = p.control;
       local.exit = c->exit;
@@ -158,20 +167,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_persistent(StepArgs a, PersistA
     const int command = local.command;
     const unsigned long long seq = local.sequence;
     if (command == kRun) {
-      if (!forward<T>(a, a.input, gs, sm)) { persistent_exit<T>(a, p); return; }
+      if (!forward2<T>(a, a.input, gs, sm)) { persistent_exit<T>(a, p); return; }
     } else if (command == kReset) {
       const int s0 = local.arg < 0 ? 0 : local.arg;
       const int s1 = local.arg < 0 ? a.streams : local.arg + 1;
       reset_streams<T>(a, s0, s1);
-      if (!gs.sync(a, a.bar_timeout_ns)) { persistent_exit<T>(a, p); return; }
+      if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok)) { persistent_exit<T>(a, p); return; }
     } else {
       if (command == kPing && blockIdx.x == 0 && threadIdx.x == 0) {
         unsigned long long checksum = 0;
-        for (int i = 0; i < a.features; ++i) checksum += __float_as_uint(__ldcv(a.input + i));
+        for (int i = 0; i < a.features; ++i) checksum += __float_as_uint(__ldcv(mapped_input + i));
         *reinterpret_cast<volatile unsigned long long*>(&p.mailbox->checksum) = checksum;
       }
       // No CTA may see the next command before every CTA has read this one.
-      if (!gs.sync(a, a.bar_timeout_ns)) { persistent_exit<T>(a, p); return; }
+      if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok)) { persistent_exit<T>(a, p); return; }
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) {
       __threadfence_system();
@@ -181,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_persistent(StepArgs a, PersistA
     if (command == kRun) ++processed;
     if (command == kStop || (p.max_events && processed >= p.max_events)) break;
   }
-  gs.sync(a, a.bar_timeout_ns);
+  gs.sync(a, a.bar_timeout_ns, &sm.sync_ok);
   persistent_exit<T>(a, p);
 }
 

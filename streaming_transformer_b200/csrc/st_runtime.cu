@@ -39,11 +39,18 @@ namespace {
 
 thread_local std::string g_create_error;
 
+// Where element (r, c) of a checkpoint tensor [rows, cols] lands in its region.
+enum LayoutKind : int {
+  kPlain = 0,      // dst row = r * p0 + p1 (p0 = 2 interleaves gate/up)
+  kQkvHead = 1,    // q/k/v [d, d] -> [H][3][hd][d]; p0 = which (0 q, 1 k, 2 v), p1 = hd
+  kOutHead = 2,    // out [d, d] -> [H][d][hd]; p1 = hd
+  kTranspose = 3   // down [d, F] -> [F][d]
+};
+
 struct TensorSlot {
   size_t offset;      // bytes into the weights slab (region start)
   int rows, cols;     // logical tensor shape (1-D tensors: rows = 1)
-  int row_step;       // destination row = row * row_step + row_offset
-  int row_offset;
+  int kind, p0, p1;   // LayoutKind and its parameters
   int index;          // presence flag index
 };
 
@@ -79,11 +86,23 @@ float bf16_bits_to_float(uint16_t h) {
 }
 
 template <typename T>
-__global__ void k_convert(const float* src, T* dst, int rows, int cols, int row_step, int row_offset) {
+__global__ void k_convert(const float* src, T* dst, int rows, int cols, int kind, int p0, int p1) {
   const size_t n = (size_t)rows * cols;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / cols, c = i - r * cols;
-    Storage<T>::store(dst, ((size_t)r * row_step + row_offset) * cols + c, src[i]);
+    size_t at;
+    if (kind == kQkvHead) {
+      const size_t h = r / p1, dim = r % p1;
+      at = ((h * 3 + p0) * p1 + dim) * cols + c;
+    } else if (kind == kOutHead) {
+      const size_t h = c / p1, e = c % p1;
+      at = (h * rows + r) * p1 + e;
+    } else if (kind == kTranspose) {
+      at = c * rows + r;
+    } else {
+      at = (r * p0 + p1) * cols + c;
+    }
+    Storage<T>::store(dst, at, src[i]);
   }
 }
 
@@ -95,7 +114,14 @@ struct st_runtime {
   int device = 0;
   int sms = 0;
   int grid = 1;
+  int cluster = 1;        // CTAs per cluster
+  int nclusters = 1;
   int legal_blocks = 1;
+  // Step kernels are plain cluster launches. A cooperative launch would add the
+  // co-residency guarantee, but a profiler replays it without its runtime
+  // cluster shape; the grid is instead sized from cudaOccupancyMaxActiveClusters
+  // (all clusters fit at once) and every grid-sync wait is bounded.
+  bool coop_clusters = false;
   size_t elem = 4;
   cudaStream_t stream = nullptr;
   cudaStream_t aux = nullptr;
@@ -159,107 +185,112 @@ struct st_runtime {
 
 namespace {
 
-int forward_barrier_count(const st_runtime* rt) { return forward_barriers(rt->desc.layers); }
+int forward_barrier_count(const st_runtime* rt) { return forward2_barriers(rt->desc.layers, rt->desc.streams); }
+
+constexpr size_t kSmem2 = sizeof(Smem2);
 
 template <typename T>
 struct Kernels {
-  static const void* persistent() { return (const void*)k_persistent<T>; }
-  static const void* fused() { return (const void*)k_fused<T>; }
-  static const void* trace() { return (const void*)k_trace<T>; }
+  static const void* input() { return (const void*)k2_input<T>; }
+  static const void* attention() { return (const void*)k2_attention<T>; }
+  static const void* ffn() { return (const void*)k2_ffn<T>; }
+  static const void* final_() { return (const void*)k2_final<T>; }
+  static const void* reset() { return (const void*)k_reset<T>; }
+  static const void* fused() { return (const void*)k2_fused<T>; }
+  static const void* trace() { return (const void*)k2_trace<T>; }
+  static const void* persistent() { return (const void*)k2_persistent<T>; }
+  static const void* convert() { return (const void*)k_convert<T>; }
 };
 
-const void* persistent_fn(const st_runtime* rt) {
-  switch (rt->desc.mode) {
-    case ST_MODE_FP16: return Kernels<__half>::persistent();
-    case ST_MODE_BF16: return Kernels<__nv_bfloat16>::persistent();
-    default: return Kernels<float>::persistent();
-  }
-}
+#define ST_KERNEL(rt, name) \
+  ((rt)->desc.mode == ST_MODE_FP16 ? Kernels<__half>::name() \
+   : (rt)->desc.mode == ST_MODE_BF16 ? Kernels<__nv_bfloat16>::name() : Kernels<float>::name())
 
-template <typename T>
-int launch_sequence_t(st_runtime* rt, const StepArgs& a) {
-  const dim3 g(rt->grid), b(kThreads);
-  cudaStream_t s = rt->stream;
-  k_input<T><<<g, b, 0, s>>>(a);
-  for (int l = 0; l < rt->desc.layers; ++l) {
-    k_qkv<T><<<g, b, 0, s>>>(a, l);
-    k_attention<T><<<g, b, 0, s>>>(a, l);
-    k_out<T><<<g, b, 0, s>>>(a, l);
-    k_ffn_in<T><<<g, b, 0, s>>>(a, l);
-    k_ffn_out<T><<<g, b, 0, s>>>(a, l);
-  }
-  k_final<T><<<dim3(1), b, 0, s>>>(a);
-  rt->launches += 2 + 5ull * rt->desc.layers;
-  return rt->cuda(cudaGetLastError(), "per-op launch");
-}
+const void* persistent_fn(const st_runtime* rt) { return ST_KERNEL(rt, persistent); }
 
-int launch_sequence(st_runtime* rt, const StepArgs& a) {
-  switch (rt->desc.mode) {
-    case ST_MODE_FP16: return launch_sequence_t<__half>(rt, a);
-    case ST_MODE_BF16: return launch_sequence_t<__nv_bfloat16>(rt, a);
-    default: return launch_sequence_t<float>(rt, a);
+// Launch with this runtime's cluster shape. `cooperative` requests the
+// co-residency guarantee when coop_clusters is set (off: see st_runtime).
+int launch_ex(st_runtime* rt, const void* fn, int grid, int cluster, bool cooperative, void** params) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem2;
+  cfg.stream = rt->stream;
+  cudaLaunchAttribute attrs[2];
+  int n = 0;
+  attrs[n].id = cudaLaunchAttributeClusterDimension;
+  attrs[n].val.clusterDim.x = cluster;
+  attrs[n].val.clusterDim.y = 1;
+  attrs[n].val.clusterDim.z = 1;
+  ++n;
+  if (cooperative && rt->coop_clusters) {
+    attrs[n].id = cudaLaunchAttributeCooperative;
+    attrs[n].val.cooperative = 1;
+    ++n;
   }
-}
-
-template <typename T>
-int launch_reset_t(st_runtime* rt, int s0, int s1) {
-  k_reset<T><<<rt->grid, kThreads, 0, rt->stream>>>(rt->args, s0, s1);
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, fn, params);
+  if (e != cudaSuccess && cooperative && rt->coop_clusters) {
+    (void)cudaGetLastError();
+    rt->coop_clusters = false;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelExC(&cfg, fn, params);
+  }
   rt->launches += 1;
-  return rt->cuda(cudaGetLastError(), "reset launch");
+  return rt->cuda(e, "cluster launch");
 }
+
+int launch_sequence(st_runtime* rt, const StepArgs& a0) {
+  StepArgs a = a0;
+  const void* kin = ST_KERNEL(rt, input);
+  const void* kat = ST_KERNEL(rt, attention);
+  const void* kff = ST_KERNEL(rt, ffn);
+  const void* kfi = ST_KERNEL(rt, final_);
+  void* p0[] = {&a};
+  ST_TRY(launch_ex(rt, kin, rt->grid, rt->cluster, false, p0));
+  for (int l = 0; l < rt->desc.layers; ++l) {
+    void* p1[] = {&a, &l};
+    ST_TRY(launch_ex(rt, kat, rt->grid, rt->cluster, false, p1));
+    ST_TRY(launch_ex(rt, kff, rt->grid, rt->cluster, false, p1));
+  }
+  int nc = rt->nclusters;
+  void* p2[] = {&a, &nc};
+  ST_TRY(launch_ex(rt, kfi, 1, 1, false, p2));
+  return ST_OK;
+}
+
+int sequence_launches(const st_runtime* rt) { return 2 + 2 * rt->desc.layers; }
 
 int launch_reset(st_runtime* rt, int s0, int s1) {
-  switch (rt->desc.mode) {
-    case ST_MODE_FP16: return launch_reset_t<__half>(rt, s0, s1);
-    case ST_MODE_BF16: return launch_reset_t<__nv_bfloat16>(rt, s0, s1);
-    default: return launch_reset_t<float>(rt, s0, s1);
-  }
+  StepArgs a = rt->args;
+  void* p[] = {&a, &s0, &s1};
+  return launch_ex(rt, ST_KERNEL(rt, reset), rt->grid, rt->cluster, false, p);
 }
 
-int launch_cooperative(st_runtime* rt, const void* fn, void** params) {
-  cudaError_t e = cudaLaunchCooperativeKernel(fn, dim3(rt->grid), dim3(kThreads), params, 0, rt->stream);
-  rt->launches += 1;
-  return rt->cuda(e, "cooperative launch");
-}
-
-template <typename T>
-int launch_fused_t(st_runtime* rt, StepArgs a) {
+int launch_fused(st_runtime* rt, const StepArgs& a0) {
+  StepArgs a = a0;
   unsigned long long base = rt->bar_base;
   void* params[] = {&a, &base};
-  ST_TRY(launch_cooperative(rt, (const void*)k_fused<T>, params));
-  rt->bar_base += (unsigned long long)forward_barrier_count(rt) * rt->grid;
+  ST_TRY(launch_ex(rt, ST_KERNEL(rt, fused), rt->grid, rt->cluster, true, params));
+  rt->bar_base += (unsigned long long)forward_barrier_count(rt) * rt->nclusters;
   return ST_OK;
 }
 
-int launch_fused(st_runtime* rt, const StepArgs& a) {
-  switch (rt->desc.mode) {
-    case ST_MODE_FP16: return launch_fused_t<__half>(rt, a);
-    case ST_MODE_BF16: return launch_fused_t<__nv_bfloat16>(rt, a);
-    default: return launch_fused_t<float>(rt, a);
-  }
-}
-
-template <typename T>
-int launch_trace_t(st_runtime* rt, StepArgs a, const float* inputs, unsigned long long count, float* scores) {
+int launch_trace(st_runtime* rt, const StepArgs& a0, const float* inputs, unsigned long long count, float* scores) {
+  StepArgs a = a0;
   unsigned long long base = rt->bar_base;
   void* params[] = {&a, &inputs, &count, &scores, &base};
-  ST_TRY(launch_cooperative(rt, (const void*)k_trace<T>, params));
-  rt->bar_base += count * (unsigned long long)(forward_barrier_count(rt) + 1) * rt->grid;
+  ST_TRY(launch_ex(rt, ST_KERNEL(rt, trace), rt->grid, rt->cluster, true, params));
+  rt->bar_base += count * (unsigned long long)(forward_barrier_count(rt) + 1) * rt->nclusters;
   return ST_OK;
-}
-
-int launch_trace(st_runtime* rt, const StepArgs& a, const float* inputs, unsigned long long count, float* scores) {
-  switch (rt->desc.mode) {
-    case ST_MODE_FP16: return launch_trace_t<__half>(rt, a, inputs, count, scores);
-    case ST_MODE_BF16: return launch_trace_t<__nv_bfloat16>(rt, a, inputs, count, scores);
-    default: return launch_trace_t<float>(rt, a, inputs, count, scores);
-  }
 }
 
 // Host-side check of the error word mirrored into mapped memory.
 int check_device_error(st_runtime* rt) {
   const int e = __atomic_load_n(&rt->mb_h->error, __ATOMIC_ACQUIRE);
   if (e == kBarrierTimeout) return rt->fail(ST_ERR_DEVICE_TIMEOUT, "device grid barrier wait exceeded its bound");
+  if (e == kClusterShape) return rt->fail(ST_ERR_CUDA, "kernel launched with a cluster shape other than the runtime's");
   if (e != 0) return rt->fail(ST_ERR_DEVICE_TIMEOUT, "device error code %d", e);
   return ST_OK;
 }
@@ -267,25 +298,15 @@ int check_device_error(st_runtime* rt) {
 // Load every kernel of this mode before a resident worker starts: lazy module
 // loading of a cold kernel can synchronize the context, which would wait for a
 // worker that is itself waiting for the host (reference src/cuda/Runtime.cu:288-290).
-template <typename T>
-int preload_t(st_runtime* rt) {
-  const void* fns[] = {(const void*)k_input<T>, (const void*)k_qkv<T>, (const void*)k_attention<T>,
-                       (const void*)k_out<T>, (const void*)k_ffn_in<T>, (const void*)k_ffn_out<T>,
-                       (const void*)k_final<T>, (const void*)k_reset<T>, (const void*)k_fused<T>,
-                       (const void*)k_trace<T>, (const void*)k_persistent<T>, (const void*)k_convert<T>};
+int preload(st_runtime* rt) {
+  const void* fns[] = {ST_KERNEL(rt, input), ST_KERNEL(rt, attention), ST_KERNEL(rt, ffn), ST_KERNEL(rt, final_),
+                       ST_KERNEL(rt, reset), ST_KERNEL(rt, fused), ST_KERNEL(rt, trace), ST_KERNEL(rt, persistent),
+                       ST_KERNEL(rt, convert)};
   for (const void* f : fns) {
     cudaFuncAttributes fa{};
     ST_CUDA(rt, cudaFuncGetAttributes(&fa, f));
   }
   return ST_OK;
-}
-
-int preload(st_runtime* rt) {
-  switch (rt->desc.mode) {
-    case ST_MODE_FP16: return preload_t<__half>(rt);
-    case ST_MODE_BF16: return preload_t<__nv_bfloat16>(rt);
-    default: return preload_t<float>(rt);
-  }
 }
 
 int start_persistent(st_runtime* rt) {
@@ -303,11 +324,12 @@ int start_persistent(st_runtime* rt) {
   p.control = rt->control;
   p.backoff = rt->opt.backoff;
   StepArgs a = rt->args;
-  a.input = rt->in_d;
+  a.input = rt->dev_input;
   a.score = rt->out_d;
+  const float* mapped = rt->in_d;
   unsigned long long base = rt->bar_base;
-  void* params[] = {&a, &p, &base};
-  ST_TRY(launch_cooperative(rt, persistent_fn(rt), params));
+  void* params[] = {&a, &p, &mapped, &base};
+  ST_TRY(launch_ex(rt, persistent_fn(rt), rt->grid, rt->cluster, true, params));
   rt->running = true;
   return ST_OK;
 }
@@ -388,7 +410,7 @@ int run_step_nonpersistent(st_runtime* rt) {
     ST_CUDA(rt, cudaMemcpyAsync(rt->dev_input, rt->in_h, in_bytes, cudaMemcpyHostToDevice, rt->stream));
   if (rt->opt.backend == ST_BACKEND_GRAPH) {
     ST_CUDA(rt, cudaGraphLaunch(rt->graph_exec, rt->stream));
-    rt->launches += 2 + 5ull * rt->desc.layers;
+    rt->launches += sequence_launches(rt);
   } else if (rt->opt.backend == ST_BACKEND_FUSED) {
     ST_TRY(launch_fused(rt, rt->args));
   } else {
@@ -519,16 +541,55 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   rt->sms = prop.multiProcessorCount;
   const st_model_desc& m = rt->desc;
   rt->elem = m.mode == ST_MODE_FP32 ? 4 : 2;
-  // Cooperative capacity from the compiled kernels (reference src/cuda/Runtime.cu:306-314).
-  int per_sm = 0, per_sm_fused = 0, per_sm_trace = 0;
-  const void* fk = m.mode == ST_MODE_FP16 ? Kernels<__half>::fused() : m.mode == ST_MODE_BF16 ? Kernels<__nv_bfloat16>::fused() : Kernels<float>::fused();
-  const void* tk = m.mode == ST_MODE_FP16 ? Kernels<__half>::trace() : m.mode == ST_MODE_BF16 ? Kernels<__nv_bfloat16>::trace() : Kernels<float>::trace();
-  if (rt->cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, persistent_fn(rt), kThreads, 0), "occupancy") != ST_OK ||
-      rt->cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_fused, fk, kThreads, 0), "occupancy") != ST_OK ||
-      rt->cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_trace, tk, kThreads, 0), "occupancy") != ST_OK)
-    return bail(ST_ERR_CUDA);
-  rt->legal_blocks = coop ? std::min(per_sm, std::min(per_sm_fused, per_sm_trace)) * rt->sms : 1;
-  rt->grid = o.blocks == 0 ? rt->sms : o.blocks;
+  // Every step kernel takes the same dynamic shared memory.
+  {
+    const void* fns[] = {ST_KERNEL(rt, input), ST_KERNEL(rt, attention), ST_KERNEL(rt, ffn), ST_KERNEL(rt, final_),
+                         ST_KERNEL(rt, reset), ST_KERNEL(rt, fused), ST_KERNEL(rt, trace), ST_KERNEL(rt, persistent)};
+    for (const void* f : fns)
+      if (rt->cuda(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem2),
+                   "cudaFuncSetAttribute") != ST_OK)
+        return bail(ST_ERR_CUDA);
+  }
+  // Cluster shape: 8 CTAs per cluster at full size; an explicit `blocks` takes
+  // its largest divisor <= 8. The cooperative limit is the number of co-resident
+  // clusters of the compiled kernels (reference src/cuda/Runtime.cu:306-314).
+  int cluster = 8;
+  if (o.blocks > 0) {
+    cluster = 1;
+    for (int c = std::min(8, o.blocks); c >= 1; --c)
+      if (o.blocks % c == 0) { cluster = c; break; }
+  }
+  int max_clusters = 1 << 30;
+  {
+    const void* fns[] = {ST_KERNEL(rt, fused), ST_KERNEL(rt, trace), ST_KERNEL(rt, persistent)};
+    for (const void* f : fns) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(cluster);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = kSmem2;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = cluster;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (rt->cuda(cudaOccupancyMaxActiveClusters(&n, f, &cfg), "cudaOccupancyMaxActiveClusters") != ST_OK)
+        return bail(ST_ERR_CUDA);
+      max_clusters = std::min(max_clusters, n);
+    }
+  }
+  if (!coop) max_clusters = 1;
+  rt->legal_blocks = max_clusters * cluster;
+  rt->cluster = cluster;
+  if (o.blocks == 0) {
+    const int nc = std::max(1, std::min(max_clusters, rt->sms / cluster));
+    rt->grid = nc * cluster;
+  } else {
+    rt->grid = o.blocks;
+  }
+  rt->nclusters = rt->grid / rt->cluster;
   const bool cooperative = o.backend == ST_BACKEND_FUSED || o.backend == ST_BACKEND_PERSISTENT;
   if (cooperative && rt->grid > rt->legal_blocks) {
     rt->fail(ST_ERR_INVALID, "Requested cooperative grid exceeds actual occupancy limit %d", rt->legal_blocks);
@@ -549,12 +610,12 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
     off = align_up(off + rows * cols * rt->elem, 256);
     return at;
   };
-  auto slot = [&](const std::string& name, size_t at, int rows, int cols, int step, int roff) {
-    rt->slots[name] = TensorSlot{at, rows, cols, step, roff, index++};
+  auto slot = [&](const std::string& name, size_t at, int rows, int cols, int kind, int p0, int p1) {
+    rt->slots[name] = TensorSlot{at, rows, cols, kind, p0, p1, index++};
   };
-  slot("input", region(d, m.features), d, m.features, 1, 0);
-  slot("final_norm", region(1, d), 1, d, 1, 0);
-  slot("score", region(1, d), 1, d, 1, 0);
+  slot("input", region(d, m.features), d, m.features, kPlain, 1, 0);
+  slot("final_norm", region(1, d), 1, d, kPlain, 1, 0);
+  slot("score", region(1, d), 1, d, kPlain, 1, 0);
   std::vector<size_t> qkv_at(L), gu_at(L), out_at(L), down_at(L), n1_at(L), n2_at(L);
   for (int l = 0; l < L; ++l) {
     const std::string p = "layers." + std::to_string(l) + ".";
@@ -564,15 +625,15 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
     out_at[l] = region(d, d);
     gu_at[l] = region(2 * (size_t)F, d);
     down_at[l] = region(d, F);
-    slot(p + "norm1", n1_at[l], 1, d, 1, 0);
-    slot(p + "norm2", n2_at[l], 1, d, 1, 0);
-    slot(p + "q", qkv_at[l], d, d, 1, 0);
-    slot(p + "k", qkv_at[l], d, d, 1, d);
-    slot(p + "v", qkv_at[l], d, d, 1, 2 * d);
-    slot(p + "out", out_at[l], d, d, 1, 0);
-    slot(p + "gate", gu_at[l], F, d, 2, 0);
-    slot(p + "up", gu_at[l], F, d, 2, 1);
-    slot(p + "down", down_at[l], d, F, 1, 0);
+    slot(p + "norm1", n1_at[l], 1, d, kPlain, 1, 0);
+    slot(p + "norm2", n2_at[l], 1, d, kPlain, 1, 0);
+    slot(p + "q", qkv_at[l], d, d, kQkvHead, 0, hd);
+    slot(p + "k", qkv_at[l], d, d, kQkvHead, 1, hd);
+    slot(p + "v", qkv_at[l], d, d, kQkvHead, 2, hd);
+    slot(p + "out", out_at[l], d, d, kOutHead, 0, hd);
+    slot(p + "gate", gu_at[l], F, d, kPlain, 2, 0);
+    slot(p + "up", gu_at[l], F, d, kPlain, 2, 1);
+    slot(p + "down", down_at[l], d, F, kTranspose, 0, 0);
   }
   rt->have.assign(index, 0);
   rt->weights_bytes = off;
@@ -598,6 +659,7 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   const size_t x_at = take(S * d * 4), x2_at = take(S * d * 4), q_at = take(S * d * 4);
   const size_t part_at = take(S * m.heads * (size_t)nch * (hd + 2) * 4);
   const size_t act_at = take(S * F * 4), score_at = take(S * 4), input_at = take(S * m.features * 4);
+  const size_t pout_at = take(S * m.heads * (size_t)d * 4), dpart_at = take(S * (size_t)rt->nclusters * d * 4);
   const size_t bar_at = take(sizeof(unsigned long long)), err_at = take(sizeof(int));
   const size_t rope_at = take((hd / 2) * sizeof(float)), ctl_at = take(sizeof(Control));
   rt->scratch_bytes = co;
@@ -654,10 +716,14 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   a.q = (float*)(rt->scratch + q_at);
   a.part = (float*)(rt->scratch + part_at);
   a.act = (float*)(rt->scratch + act_at);
+  a.pout = (float*)(rt->scratch + pout_at);
+  a.dpart = (float*)(rt->scratch + dpart_at);
   a.bar_counter = (unsigned long long*)(rt->scratch + bar_at);
   a.error = (int*)(rt->scratch + err_at);
   a.host_error = &rt->mb_d->error;
   a.bar_timeout_ns = 2ull * 1000000000ull;
+  a.cluster_size = rt->cluster;
+  a.clusters = rt->nclusters;
   rt->control = (Control*)(rt->scratch + ctl_at);
   *out = rt;
   return ST_OK;
@@ -679,9 +745,9 @@ int st_set_tensor(st_runtime* rt, const char* name, const float* data, size_t co
   if (st == ST_OK) {
     const int blocks = (int)std::min<size_t>((count + 255) / 256, 4096);
     void* dst = rt->weights + s.offset;
-    if (rt->desc.mode == ST_MODE_FP16) k_convert<__half><<<blocks, 256, 0, rt->stream>>>(tmp, (__half*)dst, s.rows, s.cols, s.row_step, s.row_offset);
-    else if (rt->desc.mode == ST_MODE_BF16) k_convert<__nv_bfloat16><<<blocks, 256, 0, rt->stream>>>(tmp, (__nv_bfloat16*)dst, s.rows, s.cols, s.row_step, s.row_offset);
-    else k_convert<float><<<blocks, 256, 0, rt->stream>>>(tmp, (float*)dst, s.rows, s.cols, s.row_step, s.row_offset);
+    if (rt->desc.mode == ST_MODE_FP16) k_convert<__half><<<blocks, 256, 0, rt->stream>>>(tmp, (__half*)dst, s.rows, s.cols, s.kind, s.p0, s.p1);
+    else if (rt->desc.mode == ST_MODE_BF16) k_convert<__nv_bfloat16><<<blocks, 256, 0, rt->stream>>>(tmp, (__nv_bfloat16*)dst, s.rows, s.cols, s.kind, s.p0, s.p1);
+    else k_convert<float><<<blocks, 256, 0, rt->stream>>>(tmp, (float*)dst, s.rows, s.cols, s.kind, s.p0, s.p1);
     st = rt->cuda(cudaGetLastError(), "convert launch");
     if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "convert");
   }
@@ -819,9 +885,9 @@ int st_load_state(st_runtime* rt, int stream, uint64_t position, const float* ke
     st = rt->cuda(cudaMemcpyAsync(tmp, src, cache * sizeof(float), cudaMemcpyHostToDevice, rt->stream), "state upload");
     if (st != ST_OK) break;
     const int rows = (int)(cache / hd), blocks = (int)std::min<size_t>((cache + 255) / 256, 4096);
-    if (m.mode == ST_MODE_FP16) k_convert<__half><<<blocks, 256, 0, rt->stream>>>(tmp, (__half*)base, rows, hd, 1, 0);
-    else if (m.mode == ST_MODE_BF16) k_convert<__nv_bfloat16><<<blocks, 256, 0, rt->stream>>>(tmp, (__nv_bfloat16*)base, rows, hd, 1, 0);
-    else k_convert<float><<<blocks, 256, 0, rt->stream>>>(tmp, (float*)base, rows, hd, 1, 0);
+    if (m.mode == ST_MODE_FP16) k_convert<__half><<<blocks, 256, 0, rt->stream>>>(tmp, (__half*)base, rows, hd, kPlain, 1, 0);
+    else if (m.mode == ST_MODE_BF16) k_convert<__nv_bfloat16><<<blocks, 256, 0, rt->stream>>>(tmp, (__nv_bfloat16*)base, rows, hd, kPlain, 1, 0);
+    else k_convert<float><<<blocks, 256, 0, rt->stream>>>(tmp, (float*)base, rows, hd, kPlain, 1, 0);
     st = rt->cuda(cudaGetLastError(), "state convert");
     if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "state convert");
   }
@@ -837,68 +903,48 @@ int st_load_state(st_runtime* rt, int stream, uint64_t position, const float* ke
 
 }  // extern "C"
 
-template <typename T>
-static int trace_step_t(st_runtime* rt, st_trace_fn fn, void* user) {
+static int trace_step_impl(st_runtime* rt, st_trace_fn fn, void* user) {
   const st_model_desc& m = rt->desc;
-  const int d = m.width, F = m.ffn, hd = d / m.heads, W = m.window;
-  const dim3 g(rt->grid), b(kThreads);
-  cudaStream_t s = rt->stream;
+  const int d = m.width, F = m.ffn;
   StepArgs a = rt->args;
-  float* attn = nullptr;
-  ST_CUDA(rt, cudaMalloc(&attn, d * sizeof(float)));
-  a.trace_attention = attn;
-  std::vector<float> buf(std::max(d, F));
+  float* dbg = nullptr;
+  ST_CUDA(rt, cudaMalloc(&dbg, (size_t)(5 * d + F) * sizeof(float)));
+  a.trace_qkv = dbg;
+  a.trace_attention = dbg + 3 * d;
+  a.trace_act = dbg + 4 * d;
+  std::vector<float> buf(std::max(3 * d, F));
   auto emit = [&](const std::string& name, const float* dev, int count) -> int {
-    ST_CUDA(rt, cudaStreamSynchronize(s));
+    ST_CUDA(rt, cudaStreamSynchronize(rt->stream));
     ST_CUDA(rt, cudaMemcpy(buf.data(), dev, count * sizeof(float), cudaMemcpyDeviceToHost));
     fn(user, name.c_str(), buf.data(), (size_t)count);
     return ST_OK;
   };
-  auto emit_slot = [&](const std::string& name, const void* ring, int l, uint64_t t) -> int {
-    ST_CUDA(rt, cudaStreamSynchronize(s));
-    const int slot = (int)(t % (uint64_t)W);
-    std::vector<uint16_t> raw(hd);
-    for (int h = 0; h < m.heads; ++h) {
-      const size_t at = (((size_t)l * m.heads + h) * W + slot) * hd;
-      if (m.mode == ST_MODE_FP32) {
-        ST_CUDA(rt, cudaMemcpy(buf.data() + h * hd, (const float*)ring + at, hd * 4, cudaMemcpyDeviceToHost));
-      } else {
-        ST_CUDA(rt, cudaMemcpy(raw.data(), (const uint16_t*)ring + at, hd * 2, cudaMemcpyDeviceToHost));
-        for (int i = 0; i < hd; ++i)
-          buf[h * hd + i] = m.mode == ST_MODE_FP16 ? half_bits_to_float(raw[i]) : bf16_bits_to_float(raw[i]);
-      }
-    }
-    fn(user, name.c_str(), buf.data(), (size_t)d);
-    return ST_OK;
-  };
-  unsigned long long t = 0;
-  int st = rt->cuda(cudaMemcpy(&t, a.position, sizeof t, cudaMemcpyDeviceToHost), "position");
   auto run = [&]() -> int {
-    ST_TRY(st);
-    k_input<T><<<g, b, 0, s>>>(a);
+    void* p0[] = {&a};
+    ST_TRY(launch_ex(rt, ST_KERNEL(rt, input), rt->grid, rt->cluster, false, p0));
     ST_TRY(emit("input", a.x, d));
     for (int l = 0; l < m.layers; ++l) {
       const std::string p = "layers." + std::to_string(l) + ".";
-      k_qkv<T><<<g, b, 0, s>>>(a, l);
-      ST_TRY(emit(p + "q", a.q, d));
-      ST_TRY(emit_slot(p + "k", a.keys, l, t));
-      ST_TRY(emit_slot(p + "v", a.values, l, t));
-      k_attention<T><<<g, b, 0, s>>>(a, l);
-      k_out<T><<<g, b, 0, s>>>(a, l);
-      ST_TRY(emit(p + "attention", attn, d));
+      void* p1[] = {&a, &l};
+      ST_TRY(launch_ex(rt, ST_KERNEL(rt, attention), rt->grid, rt->cluster, false, p1));
+      if (l > 0) ST_TRY(emit("layers." + std::to_string(l - 1) + ".hidden", a.hidden + (size_t)(l - 1) * d, d));
+      ST_TRY(emit(p + "q", a.trace_qkv, d));
+      ST_TRY(emit(p + "k", a.trace_qkv + d, d));
+      ST_TRY(emit(p + "v", a.trace_qkv + 2 * d, d));
+      ST_TRY(emit(p + "attention", a.trace_attention, d));
+      ST_TRY(launch_ex(rt, ST_KERNEL(rt, ffn), rt->grid, rt->cluster, false, p1));
       ST_TRY(emit(p + "attention_residual", a.x2, d));
-      k_ffn_in<T><<<g, b, 0, s>>>(a, l);
-      ST_TRY(emit(p + "activation", a.act, F));
-      k_ffn_out<T><<<g, b, 0, s>>>(a, l);
-      ST_TRY(emit(p + "hidden", a.x, d));
+      ST_TRY(emit(p + "activation", a.trace_act, F));
     }
-    k_final<T><<<dim3(1), b, 0, s>>>(a);
+    int nc = rt->nclusters;
+    void* p2[] = {&a, &nc};
+    ST_TRY(launch_ex(rt, ST_KERNEL(rt, final_), 1, 1, false, p2));
+    ST_TRY(emit("layers." + std::to_string(m.layers - 1) + ".hidden", a.hidden + (size_t)(m.layers - 1) * d, d));
     ST_TRY(emit("score.linear", a.score, 1));
-    rt->launches += 2 + 5ull * m.layers;
-    return rt->cuda(cudaGetLastError(), "trace launches");
+    return ST_OK;
   };
-  st = run();
-  cudaFree(attn);
+  const int st = run();
+  cudaFree(dbg);
   return st;
 }
 
@@ -914,13 +960,7 @@ int st_trace_step(st_runtime* rt, const float* input, float* score, st_trace_fn 
   std::memcpy(rt->in_h, input, n * sizeof(float));
   if (!rt->opt.mapped)
     ST_CUDA(rt, cudaMemcpyAsync(rt->dev_input, rt->in_h, n * 4, cudaMemcpyHostToDevice, rt->stream));
-  int st;
-  switch (rt->desc.mode) {
-    case ST_MODE_FP16: st = trace_step_t<__half>(rt, fn, user); break;
-    case ST_MODE_BF16: st = trace_step_t<__nv_bfloat16>(rt, fn, user); break;
-    default: st = trace_step_t<float>(rt, fn, user); break;
-  }
-  ST_TRY(st);
+  ST_TRY(trace_step_impl(rt, fn, user));
   ST_CUDA(rt, cudaStreamSynchronize(rt->stream));
   ST_TRY(check_device_error(rt));
   if (score) {
@@ -949,7 +989,7 @@ static int device_trace_impl(st_runtime* rt, const float* dev_inputs, size_t cou
       ST_CUDA(rt, cudaMemcpyAsync(rt->dev_input, dev_inputs + e * stride, stride * 4, cudaMemcpyDeviceToDevice, rt->stream));
       if (graph) {
         ST_CUDA(rt, cudaGraphLaunch(rt->graph_exec, rt->stream));
-        rt->launches += 2 + 5ull * rt->desc.layers;
+        rt->launches += sequence_launches(rt);
       } else {
         ST_TRY(launch_sequence(rt, a));
       }
@@ -987,6 +1027,41 @@ int st_device_trace(st_runtime* rt, const float* inputs, size_t count, float* sc
   return st;
 }
 
+int st_device_timeline(st_runtime* rt, const float* inputs, size_t count, long long* marks, size_t capacity,
+                       size_t* used) {
+  if (!rt || !inputs || !marks || count == 0 || capacity == 0) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
+  if (rt->opt.backend == ST_BACKEND_PERSISTENT) ST_TRY(st_stop(rt));
+  const size_t n = count * (size_t)rt->desc.streams * rt->desc.features;
+  float* dev = nullptr;
+  long long* tl = nullptr;
+  ST_CUDA(rt, cudaMalloc(&dev, n * 4));
+  int st = rt->cuda(cudaMalloc(&tl, capacity * sizeof(long long)), "cudaMalloc timeline");
+  if (st == ST_OK) st = rt->cuda(cudaMemsetAsync(tl, 0, capacity * sizeof(long long), rt->stream), "timeline clear");
+  if (st == ST_OK) st = rt->cuda(cudaMemcpyAsync(dev, inputs, n * 4, cudaMemcpyHostToDevice, rt->stream), "trace upload");
+  if (st == ST_OK) st = launch_reset(rt, 0, rt->desc.streams);
+  if (st == ST_OK) {
+    StepArgs a = rt->args;
+    a.input = rt->dev_input;
+    a.score = rt->dev_score;
+    a.timeline = tl;
+    a.timeline_capacity = (int)std::min<size_t>(capacity, 1u << 30);
+    st = launch_trace(rt, a, dev, count, nullptr);
+  }
+  if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "timeline run");
+  if (st == ST_OK) st = check_device_error(rt);
+  if (st == ST_OK) st = rt->cuda(cudaMemcpy(marks, tl, capacity * sizeof(long long), cudaMemcpyDeviceToHost), "timeline download");
+  if (st == ST_OK && used) {
+    size_t u = 0;
+    while (u < capacity && marks[u] != 0) ++u;
+    *used = u;
+  }
+  cudaFree(dev);
+  cudaFree(tl);
+  return st;
+}
+
 int st_device_trace_resident(st_runtime* rt, const float* device_inputs, size_t count, double* us_per_step,
                              uint64_t* kernel_launches) {
   if (!rt || !device_inputs || count == 0) return ST_ERR_INVALID;
@@ -1004,13 +1079,13 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
   if (!rt) return ST_ERR_INVALID;
   cudaFuncAttributes fa{};
   const void* kernel = persistent_fn(rt);
-  std::string name = "k_persistent";
+  std::string name = "k2_persistent";
   if (rt->opt.backend == ST_BACKEND_FUSED) {
-    kernel = rt->desc.mode == ST_MODE_FP16 ? Kernels<__half>::fused() : rt->desc.mode == ST_MODE_BF16 ? Kernels<__nv_bfloat16>::fused() : Kernels<float>::fused();
-    name = "k_fused";
+    kernel = ST_KERNEL(rt, fused);
+    name = "k2_fused";
   } else if (rt->opt.backend == ST_BACKEND_CUDA || rt->opt.backend == ST_BACKEND_GRAPH) {
-    kernel = rt->desc.mode == ST_MODE_FP16 ? (const void*)k_ffn_in<__half> : rt->desc.mode == ST_MODE_BF16 ? (const void*)k_ffn_in<__nv_bfloat16> : (const void*)k_ffn_in<float>;
-    name = "k_ffn_in (per-op phase kernels)";
+    kernel = ST_KERNEL(rt, ffn);
+    name = "k2_ffn (per-op block kernels)";
   }
   cudaFuncGetAttributes(&fa, kernel);
   static const char* backends[] = {"cuda", "graph", "cublas", "cublas-graph", "fused", "persistent"};
@@ -1021,9 +1096,11 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     << "\",\"blocks\":" << rt->grid << ",\"legal_cooperative_blocks\":" << rt->legal_blocks
     << ",\"threads\":" << kThreads << ",\"resource_kernel\":\"" << name << "\""
     << ",\"registers_per_thread\":" << fa.numRegs << ",\"local_bytes\":" << fa.localSizeBytes
-    << ",\"shared_bytes\":" << fa.sharedSizeBytes
-    << ",\"attention_implementation\":\"split-window partial softmax, " << kAttChunk << " slots per warp item\""
-    << ",\"matvec_implementation\":\"16-byte non-temporal loads, contiguous row ranges per CTA\""
+    << ",\"shared_bytes\":" << fa.sharedSizeBytes << ",\"dynamic_shared_bytes\":" << kSmem2
+    << ",\"cluster\":" << rt->cluster << ",\"clusters\":" << rt->nclusters
+    << ",\"cooperative_clusters\":" << (rt->coop_clusters ? "true" : "false")
+    << ",\"attention_implementation\":\"one cluster per head, window split over the cluster, partials merged through DSMEM\""
+    << ",\"matvec_implementation\":\"16-byte non-temporal loads; out- and down-projections K-split (per head, per ffn slice)\""
     << ",\"barriers_per_step\":" << forward_barrier_count(rt)
     << ",\"transport\":\"" << (rt->opt.backend == ST_BACKEND_PERSISTENT ? "mapped-system-load-store" : rt->opt.mapped ? "mapped-stream-sync" : "pinned-copy-stream-sync") << "\""
     << ",\"poll_policy\":\"" << (rt->opt.backoff ? "bounded-device-backoff-host-yield" : "tight") << "\""

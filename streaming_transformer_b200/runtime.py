@@ -117,6 +117,7 @@ def library() -> ctypes.CDLL:
             "st_load_state": (I, [P, I, U64, F, F, F]),
             "st_trace_step": (I, [P, F, F, TRACE_FN, P]),
             "st_device_trace": (I, [P, F, S, F, ctypes.POINTER(ctypes.c_double)]),
+            "st_device_timeline": (I, [P, F, S, ctypes.POINTER(ctypes.c_longlong), S, ctypes.POINTER(S)]),
             "st_device_trace_resident": (I, [P, ctypes.c_void_p, S, ctypes.POINTER(ctypes.c_double),
                                              ctypes.POINTER(U64)]),
             "st_info": (I, [P, ctypes.c_char_p, S, ctypes.POINTER(S)]),
@@ -150,6 +151,24 @@ def _json_call(fn, *args) -> dict:
     _check(fn(*args, None, 0, ctypes.byref(needed)))
     buf = ctypes.create_string_buffer(needed.value)
     _check(fn(*args, buf, needed.value, ctypes.byref(needed)))
+    return json.loads(buf.value.decode())
+
+
+def transport_bench(mode: str, count: int, backoff: bool = False, device: int = 0,
+                    csv_path: str | None = None) -> dict:
+    """reference transportBench (src/cuda/Runtime.cu:706-814) plus "grid-barrier"."""
+    lib = library()
+    fn = lib.st_transport_bench
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_char_p,
+                   ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]
+    lib.st_transport_error.restype = ctypes.c_char_p
+    buf = ctypes.create_string_buffer(1 << 16)
+    needed = ctypes.c_size_t(0)
+    code = fn(int(device), mode.encode(), int(count), int(bool(backoff)),
+              csv_path.encode() if csv_path else None, buf, len(buf), ctypes.byref(needed))
+    if code != ST_OK:
+        raise StreamError(code, lib.st_transport_error().decode())
     return json.loads(buf.value.decode())
 
 
@@ -289,6 +308,18 @@ class Runtime:
         if return_scores:
             return us.value, (scores[:, 0] if self.streams == 1 else scores)
         return us.value
+
+    def device_timeline(self, events, capacity: int = 1 << 16) -> np.ndarray:
+        """Diagnostic: CTA 0's clock64() at every phase boundary of a device-loop
+        run over ``events`` (see st_device_timeline); returns the marks."""
+        e = np.ascontiguousarray(events, dtype=np.float32)
+        count = e.shape[0]
+        marks = np.zeros(capacity, dtype=np.int64)
+        used = ctypes.c_size_t(0)
+        _check(library().st_device_timeline(self._h, _fptr(e), count,
+                                            marks.ctypes.data_as(ctypes.POINTER(ctypes.c_longlong)),
+                                            capacity, ctypes.byref(used)), self._h)
+        return marks[: used.value]
 
     def device_trace_resident(self, device_ptr: int, count: int) -> tuple[float, int]:
         """Device-only timing with the trace already in device memory (pointer from

@@ -108,7 +108,9 @@ def test_info_and_probe_describe_the_device():
     g = Golden("ref-small-fp32")
     rt = Runtime(g.model, RuntimeOptions(backend=Backend.PERSISTENT, blocks=0))
     info = rt.info()
-    assert info["blocks"] == p["sm_count"] and info["threads"] == 512
+    # one CTA per SM at most, whole clusters only (clusters of 8 pack per GPC)
+    assert 0 < info["blocks"] <= p["sm_count"] and info["threads"] == 512
+    assert info["blocks"] % info["cluster"] == 0 and info["clusters"] * info["cluster"] == info["blocks"]
     assert info["transport"] == "mapped-system-load-store"
     assert info["registers_per_thread"] > 0
     rt.close()
