@@ -33,13 +33,13 @@ namespace st {
 constexpr int kThreads = 512;               // threads per CTA in every kernel
 constexpr int kWarps = kThreads / 32;
 constexpr int kRowTile = 64;                // GEMV rows per shared-memory tile
-constexpr int kMaxCols = 4096;              // max(width, ffn, features)
+constexpr int kMaxCols = 1024;              // max(width, features, head_dim): GEMV input length
 constexpr int kMaxBlocksPerRow = kMaxCols / 4 / 32;  // fp32: 16-byte vectors / 32 lanes
 constexpr int kAttChunk = 32;               // ring slots per attention work item
 constexpr int kMaxLayers = 16;
 constexpr int kUnroll = 8;                  // 16-byte loads in flight per lane
 
-enum ErrorCode : int { kOk = 0, kBarrierTimeout = 1, kAborted = 2, kClusterShape = 3 };
+enum ErrorCode : int { kOk = 0, kBarrierTimeout = 1, kAborted = 2, kClusterShape = 3, kRingTable = 4 };
 enum Command : int { kRun = 1, kReset = 2, kStop = 3, kPing = 4 };
 
 struct LayerPtrs {
@@ -220,25 +220,45 @@ struct alignas(16) Smem {
   float xs[kMaxCols];                        // GEMV input vector (one stream)
   float red[kRowTile * kMaxBlocksPerRow];    // per-(row, 32-vector block) partials
   float rowsum[kRowTile];
-  float warp_scratch[kWarps];
+  float warp_scratch[kWarps];                // block_sum slot (16-byte aligned)
+  float max_scratch[kWarps];                 // block_max slot
   float scalar[4];
 };
+static_assert(kWarps % 4 == 0, "block reductions read the warp totals as float4");
 
-__device__ __forceinline__ float block_sum(float v, Smem& sm) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// Block-wide reductions in one barrier: each warp reduces its lanes, lane 0
+// posts the warp total into `slot` (kWarps floats, 16-byte aligned), and after
+// the barrier every thread combines the kWarps totals in the same fixed order.
+// Two uses of one slot must be separated by a __syncthreads; every caller
+// below reaches one (a GEMV tile, a norm's final barrier) before its next use.
+__device__ __forceinline__ float block_reduce_sum(float v, float* slot) {
   v = warp_sum(v);
-  __syncthreads();
-  if (lane == 0) sm.warp_scratch[warp] = v;
+  if ((threadIdx.x & 31) == 0) slot[threadIdx.x >> 5] = v;
   __syncthreads();
   float t = 0.f;
-  if (warp == 0) {
-    t = lane < kWarps ? sm.warp_scratch[lane] : 0.f;
-    t = warp_sum(t);
-    if (lane == 0) sm.scalar[0] = t;
+#pragma unroll
+  for (int w = 0; w < kWarps; w += 4) {
+    const float4 q = *reinterpret_cast<const float4*>(slot + w);
+    t += (q.x + q.y) + (q.z + q.w);
   }
-  __syncthreads();
-  return sm.scalar[0];
+  return t;
 }
+
+__device__ __forceinline__ float block_reduce_max(float v, float* slot) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) slot[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kWarps; w += 4) {
+    const float4 q = *reinterpret_cast<const float4*>(slot + w);
+    t = fmaxf(t, fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w)));
+  }
+  return t;
+}
+
+__device__ __forceinline__ float block_sum(float v, Smem& sm) { return block_reduce_sum(v, sm.warp_scratch); }
+__device__ __forceinline__ float block_max(float v, Smem& sm) { return block_reduce_max(v, sm.max_scratch); }
 
 // RMSNorm of a residual vector into sm.xs, cast to storage precision
 // (reference src/cpu/Cpu.cpp:43-57: scale = 1/sqrt(mean(x^2)+eps), out = x*scale*g).
@@ -276,7 +296,15 @@ __device__ __forceinline__ float dot_vec(const uint4& w, const float* x) {
 
 // rowsum[i] = sum_c W[row0 + i, c] * xs[c] for i < nrows (nrows <= kRowTile),
 // fp32 accumulation in a fixed order (bit-stable run to run). All threads call.
-template <typename T>
+template <bool kShared>
+__device__ __forceinline__ uint4 ld_weights(const void* p) {
+  if constexpr (kShared) return *reinterpret_cast<const uint4*>(p);
+  else return ld_stream(p);
+}
+
+// kShared: W points at rows staged in this CTA's shared memory (same
+// arithmetic, so both sources give bit-identical sums).
+template <typename T, bool kShared = false>
 __device__ void gemv_tile(const T* __restrict__ W, int row0, int nrows, int cols, Smem& sm) {
   constexpr int V = Storage<T>::kVec;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -294,7 +322,7 @@ __device__ void gemv_tile(const T* __restrict__ W, int row0, int nrows, int cols
         const int blk = b0 + u * kWarps;
         if (blk < nblk) {
           const int r = blk / bpr, cb = blk - r * bpr;
-          w[u] = ld_stream(base + (size_t)r * cols + (size_t)((cb << 5) + lane) * V);
+          w[u] = ld_weights<kShared>(base + (size_t)r * cols + (size_t)((cb << 5) + lane) * V);
         }
       }
 #pragma unroll
@@ -322,7 +350,7 @@ __device__ void gemv_tile(const T* __restrict__ W, int row0, int nrows, int cols
     for (int r0 = warp * rpw; r0 < nrows; r0 += kWarps * rpw) {
       const int r = r0 + sub;
       float acc = 0.f;
-      if (r < nrows) acc = dot_vec<T>(ld_stream(base + (size_t)r * cols + (size_t)c * V), sm.xs + c * V);
+      if (r < nrows) acc = dot_vec<T>(ld_weights<kShared>(base + (size_t)r * cols + (size_t)c * V), sm.xs + c * V);
       for (int o = vpr >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
       if (c == 0 && r < nrows) sm.rowsum[r] = acc;
     }
@@ -330,7 +358,7 @@ __device__ void gemv_tile(const T* __restrict__ W, int row0, int nrows, int cols
     for (int r = warp; r < nrows; r += kWarps) {
       float acc = 0.f;
       for (int c = lane; c < vpr; c += 32)
-        acc += dot_vec<T>(ld_stream(base + (size_t)r * cols + (size_t)c * V), sm.xs + c * V);
+        acc += dot_vec<T>(ld_weights<kShared>(base + (size_t)r * cols + (size_t)c * V), sm.xs + c * V);
       acc = warp_sum(acc);
       if (lane == 0) sm.rowsum[r] = acc;
     }

@@ -47,26 +47,49 @@ struct PersistArgs {
 };
 
 #define ST_SMEM2 \
-  extern __shared__ __align__(16) unsigned char st_smem_raw[]; \
-  Smem2& sm = *reinterpret_cast<Smem2*>(st_smem_raw)
+  extern __shared__ __align__(128) unsigned char st_smem_raw[]; \
+  Smem2& sm = *reinterpret_cast<Smem2*>(st_smem_raw); \
+  RingSmem& rs = *reinterpret_cast<RingSmem*>(st_smem_raw + sizeof(Smem2)); \
+  unsigned char* ring_buf = st_smem_raw + kRingOffset; \
+  (void)rs; \
+  (void)ring_buf; \
+  for (int i_ = threadIdx.x; i_ < a.head_dim / 2; i_ += kThreads) sm.rope[i_] = a.rope_freq[i_]; \
+  __syncthreads()
+
+// Ring setup shared by the step kernels (kRing variants only; the host chose
+// them after ring_supported). `steps` bounds the chunks issued (0: unbounded,
+// resident kernel). Returns false, with the error word set, when the chunk
+// table could not be built -- the whole grid then leaves before any barrier.
+template <typename T, bool kRing>
+__device__ bool ring_setup(const StepArgs& a, Ring& rg, RingSmem& rs, unsigned char* buf, unsigned long long steps) {
+  rg.enabled = false;
+  rg.consumed = 0;
+  if constexpr (!kRing) return true;
+  const ClusterPos cp = ClusterPos::get();
+  const Where w{(int)cp.rank, (int)cp.size, (int)cp.id, (int)cp.count};
+  const unsigned long long limit = steps ? steps * chunks_per_step(a, w, sizeof(T)) : ~0ull;
+  ring_begin(a, rg, rs, buf, kRingCapacity, w, sizeof(T), limit, true);
+  if (!rg.enabled && threadIdx.x == 0) set_error(a, kRingTable);
+  return rg.enabled;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) k2_input(StepArgs a) {
   ST_SMEM2;
   if (!cluster_shape_ok(a)) return;
-  op_input<T>(a, sm);
+  op_input<T>(a, sm, rs);
 }
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) k2_attention(StepArgs a, int l) {
   ST_SMEM2;
   if (!cluster_shape_ok(a)) return;
-  op_attention<T>(a, l, sm);
+  op_attention<T>(a, l, sm, rs);
 }
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) k2_ffn(StepArgs a, int l) {
   ST_SMEM2;
   if (!cluster_shape_ok(a)) return;
-  op_ffn<T>(a, l, sm);
+  op_ffn<T>(a, l, sm, rs);
 }
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) k2_final(StepArgs a, int nclusters) {
@@ -78,18 +101,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_reset(StepArgs a, int s0, int s
   reset_streams<T>(a, s0, s1);
 }
 
-template <typename T>
+template <typename T, bool kRing>
 __global__ void __launch_bounds__(kThreads, 1) k2_fused(StepArgs a, unsigned long long base) {
   ST_SMEM2;
   if (!cluster_shape_ok(a)) return;
   ClusterGridSync gs{base, 0};
-  forward2<T>(a, a.input, gs, sm);
+  Ring rg;
+  if (!ring_setup<T, kRing>(a, rg, rs, ring_buf, 1)) return;
+  forward2<T, StepCfg<kRing, false>>(a, a.input, gs, sm, rg, rs);
+  ring_drain(a, rg, rs);
 }
 
 // Steps `count` preloaded events ([count][S][features], device memory) in one
-// launch. scores ([count][S]) may be null. The extra grid sync per event orders
+// launch; the kDiag variant also records the phase timeline. scores ([count][S]) may be null. The extra grid sync per event orders
 // CTA 0's position update before the next event reads the position.
-template <typename T>
+template <typename T, bool kRing, bool kDiag>
 __global__ void __launch_bounds__(kThreads, 1) k2_trace(StepArgs a, const float* inputs, unsigned long long count,
                                                        float* scores, unsigned long long base) {
   ST_SMEM2;
@@ -97,13 +123,16 @@ __global__ void __launch_bounds__(kThreads, 1) k2_trace(StepArgs a, const float*
   ClusterGridSync gs{base, 0};
   if (threadIdx.x == 0) sm.tl_n = 0;
   __syncthreads();
+  Ring rg;
+  if (!ring_setup<T, kRing>(a, rg, rs, ring_buf, count)) return;
   const size_t stride = (size_t)a.streams * a.features;
   for (unsigned long long e = 0; e < count; ++e) {
-    if (!forward2<T>(a, inputs + e * stride, gs, sm)) return;
+    if (!forward2<T, StepCfg<kRing, kDiag>>(a, inputs + e * stride, gs, sm, rg, rs)) break;
     if (scores && blockIdx.x == 0)
       for (int s = threadIdx.x; s < a.streams; s += kThreads) scores[e * a.streams + s] = a.score[s];
-    if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok)) return;
+    if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok, nullptr, kRing ? &rg : nullptr, &rs)) break;
   }
+  ring_drain(a, rg, rs);
 }
 
 template <typename T>
@@ -121,13 +150,15 @@ __device__ void persistent_exit(const StepArgs& a, const PersistArgs& p) {
 // into device memory before the dispatch barrier (one PCIe read per value, by
 // one CTA); every CTA runs the command; CTA 0 publishes the score and the
 // completion ID with release ordering.
-template <typename T>
+template <typename T, bool kRing>
 __global__ void __launch_bounds__(kThreads, 1) k2_persistent(StepArgs a, PersistArgs p, const float* mapped_input,
                                                             unsigned long long base) {
   ST_SMEM2;
   __shared__ Control local;
   if (!cluster_shape_ok(a)) { persistent_exit<T>(a, p); return; }
   ClusterGridSync gs{base, 0};
+  Ring rg;
+  if (!ring_setup<T, kRing>(a, rg, rs, ring_buf, 0)) { persistent_exit<T>(a, p); return; }
   unsigned long long previous = p.initial_sequence, processed = 0;
   const int nin = a.streams * a.features;
   while (true) {
@@ -154,7 +185,11 @@ __global__ void __launch_bounds__(kThreads, 1) k2_persistent(StepArgs a, Persist
       if (!local.exit && local.command == kRun)
         for (int i = threadIdx.x; i < nin; i += kThreads) const_cast<float*>(a.input)[i] = __ldcv(mapped_input + i);
     }
-    if (!gs.sync(a, p.dispatch_timeout_ns, &sm.sync_ok)) { persistent_exit<T>(a, p); return; }
+    if (!gs.sync(a, p.dispatch_timeout_ns, &sm.sync_ok, nullptr, kRing ? &rg : nullptr, &rs)) {
+      ring_drain(a, rg, rs);
+      persistent_exit<T>(a, p);
+      return;
+    }
     if (threadIdx.x == 0) {
       const volatile Control* c = p.control;
       local.exit = c->exit;
@@ -167,12 +202,16 @@ __global__ void __launch_bounds__(kThreads, 1) k2_persistent(StepArgs a, Persist
     const int command = local.command;
     const unsigned long long seq = local.sequence;
     if (command == kRun) {
-      if (!forward2<T>(a, a.input, gs, sm)) { persistent_exit<T>(a, p); return; }
+      if (!forward2<T, StepCfg<kRing, false>>(a, a.input, gs, sm, rg, rs)) {
+        ring_drain(a, rg, rs);
+        persistent_exit<T>(a, p);
+        return;
+      }
     } else if (command == kReset) {
       const int s0 = local.arg < 0 ? 0 : local.arg;
       const int s1 = local.arg < 0 ? a.streams : local.arg + 1;
       reset_streams<T>(a, s0, s1);
-      if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok)) { persistent_exit<T>(a, p); return; }
+      if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok)) { ring_drain(a, rg, rs); persistent_exit<T>(a, p); return; }
     } else {
       if (command == kPing && blockIdx.x == 0 && threadIdx.x == 0) {
         unsigned long long checksum = 0;
@@ -180,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1) k2_persistent(StepArgs a, Persist
         *reinterpret_cast<volatile unsigned long long*>(&p.mailbox->checksum) = checksum;
       }
       // No CTA may see the next command before every CTA has read this one.
-      if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok)) { persistent_exit<T>(a, p); return; }
+      if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok)) { ring_drain(a, rg, rs); persistent_exit<T>(a, p); return; }
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) {
       __threadfence_system();
@@ -191,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) k2_persistent(StepArgs a, Persist
     if (command == kStop || (p.max_events && processed >= p.max_events)) break;
   }
   gs.sync(a, a.bar_timeout_ns, &sm.sync_ok);
+  ring_drain(a, rg, rs);
   persistent_exit<T>(a, p);
 }
 

@@ -22,6 +22,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <map>
@@ -122,6 +123,10 @@ struct st_runtime {
   // cluster shape; the grid is instead sized from cudaOccupancyMaxActiveClusters
   // (all clusters fit at once) and every grid-sync wait is bounded.
   bool coop_clusters = false;
+  // Device-loop kernels stream their weights through the shared-memory ring
+  // (st_ring.cuh) when the configuration allows it (ring_supported); the
+  // environment variable ST_WEIGHT_RING=0 selects the direct-load variants.
+  bool ring = false;
   size_t elem = 4;
   cudaStream_t stream = nullptr;
   cudaStream_t aux = nullptr;
@@ -187,7 +192,7 @@ namespace {
 
 int forward_barrier_count(const st_runtime* rt) { return forward2_barriers(rt->desc.layers, rt->desc.streams); }
 
-constexpr size_t kSmem2 = sizeof(Smem2);
+constexpr size_t kSmem2 = kStepSmemBytes;
 
 template <typename T>
 struct Kernels {
@@ -196,17 +201,31 @@ struct Kernels {
   static const void* ffn() { return (const void*)k2_ffn<T>; }
   static const void* final_() { return (const void*)k2_final<T>; }
   static const void* reset() { return (const void*)k_reset<T>; }
-  static const void* fused() { return (const void*)k2_fused<T>; }
-  static const void* trace() { return (const void*)k2_trace<T>; }
-  static const void* persistent() { return (const void*)k2_persistent<T>; }
+  static const void* fused(bool ring) { return ring ? (const void*)k2_fused<T, true> : (const void*)k2_fused<T, false>; }
+  static const void* trace(bool ring, bool diag = false) {
+    if (diag) return ring ? (const void*)k2_trace<T, true, true> : (const void*)k2_trace<T, false, true>;
+    return ring ? (const void*)k2_trace<T, true, false> : (const void*)k2_trace<T, false, false>;
+  }
+  static const void* persistent(bool ring) {
+    return ring ? (const void*)k2_persistent<T, true> : (const void*)k2_persistent<T, false>;
+  }
   static const void* convert() { return (const void*)k_convert<T>; }
 };
 
 #define ST_KERNEL(rt, name) \
   ((rt)->desc.mode == ST_MODE_FP16 ? Kernels<__half>::name() \
    : (rt)->desc.mode == ST_MODE_BF16 ? Kernels<__nv_bfloat16>::name() : Kernels<float>::name())
+// The device-loop kernels in the weight-ring or direct-load variant the runtime chose.
+#define ST_LOOP_KERNEL(rt, name) \
+  ((rt)->desc.mode == ST_MODE_FP16 ? Kernels<__half>::name((rt)->ring) \
+   : (rt)->desc.mode == ST_MODE_BF16 ? Kernels<__nv_bfloat16>::name((rt)->ring) : Kernels<float>::name((rt)->ring))
+// The trace kernel with the phase timeline compiled in.
+#define ST_TIMELINE_KERNEL(rt) \
+  ((rt)->desc.mode == ST_MODE_FP16 ? Kernels<__half>::trace((rt)->ring, true) \
+   : (rt)->desc.mode == ST_MODE_BF16 ? Kernels<__nv_bfloat16>::trace((rt)->ring, true) \
+                                     : Kernels<float>::trace((rt)->ring, true))
 
-const void* persistent_fn(const st_runtime* rt) { return ST_KERNEL(rt, persistent); }
+const void* persistent_fn(const st_runtime* rt) { return ST_LOOP_KERNEL(rt, persistent); }
 
 // Launch with this runtime's cluster shape. `cooperative` requests the
 // co-residency guarantee when coop_clusters is set (off: see st_runtime).
@@ -272,16 +291,18 @@ int launch_fused(st_runtime* rt, const StepArgs& a0) {
   StepArgs a = a0;
   unsigned long long base = rt->bar_base;
   void* params[] = {&a, &base};
-  ST_TRY(launch_ex(rt, ST_KERNEL(rt, fused), rt->grid, rt->cluster, true, params));
+  ST_TRY(launch_ex(rt, ST_LOOP_KERNEL(rt, fused), rt->grid, rt->cluster, true, params));
   rt->bar_base += (unsigned long long)forward_barrier_count(rt) * rt->nclusters;
   return ST_OK;
 }
 
-int launch_trace(st_runtime* rt, const StepArgs& a0, const float* inputs, unsigned long long count, float* scores) {
+int launch_trace(st_runtime* rt, const StepArgs& a0, const float* inputs, unsigned long long count, float* scores,
+                 bool timeline = false) {
   StepArgs a = a0;
   unsigned long long base = rt->bar_base;
   void* params[] = {&a, &inputs, &count, &scores, &base};
-  ST_TRY(launch_ex(rt, ST_KERNEL(rt, trace), rt->grid, rt->cluster, true, params));
+  ST_TRY(launch_ex(rt, timeline ? ST_TIMELINE_KERNEL(rt) : ST_LOOP_KERNEL(rt, trace), rt->grid, rt->cluster, true,
+                   params));
   rt->bar_base += count * (unsigned long long)(forward_barrier_count(rt) + 1) * rt->nclusters;
   return ST_OK;
 }
@@ -291,6 +312,7 @@ int check_device_error(st_runtime* rt) {
   const int e = __atomic_load_n(&rt->mb_h->error, __ATOMIC_ACQUIRE);
   if (e == kBarrierTimeout) return rt->fail(ST_ERR_DEVICE_TIMEOUT, "device grid barrier wait exceeded its bound");
   if (e == kClusterShape) return rt->fail(ST_ERR_CUDA, "kernel launched with a cluster shape other than the runtime's");
+  if (e == kRingTable) return rt->fail(ST_ERR_STATE, "weight ring chunk table does not fit this configuration");
   if (e != 0) return rt->fail(ST_ERR_DEVICE_TIMEOUT, "device error code %d", e);
   return ST_OK;
 }
@@ -300,8 +322,8 @@ int check_device_error(st_runtime* rt) {
 // worker that is itself waiting for the host (reference src/cuda/Runtime.cu:288-290).
 int preload(st_runtime* rt) {
   const void* fns[] = {ST_KERNEL(rt, input), ST_KERNEL(rt, attention), ST_KERNEL(rt, ffn), ST_KERNEL(rt, final_),
-                       ST_KERNEL(rt, reset), ST_KERNEL(rt, fused), ST_KERNEL(rt, trace), ST_KERNEL(rt, persistent),
-                       ST_KERNEL(rt, convert)};
+                       ST_KERNEL(rt, reset), ST_LOOP_KERNEL(rt, fused), ST_LOOP_KERNEL(rt, trace), ST_LOOP_KERNEL(rt, persistent),
+                       ST_TIMELINE_KERNEL(rt), ST_KERNEL(rt, convert)};
   for (const void* f : fns) {
     cudaFuncAttributes fa{};
     ST_CUDA(rt, cudaFuncGetAttributes(&fa, f));
@@ -544,7 +566,16 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   // Every step kernel takes the same dynamic shared memory.
   {
     const void* fns[] = {ST_KERNEL(rt, input), ST_KERNEL(rt, attention), ST_KERNEL(rt, ffn), ST_KERNEL(rt, final_),
-                         ST_KERNEL(rt, reset), ST_KERNEL(rt, fused), ST_KERNEL(rt, trace), ST_KERNEL(rt, persistent)};
+                         ST_KERNEL(rt, reset), nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                         nullptr, nullptr};
+    for (int r = 0; r < 2; ++r) {
+      rt->ring = r == 1;
+      fns[5 + 3 * r] = ST_LOOP_KERNEL(rt, fused);
+      fns[6 + 3 * r] = ST_LOOP_KERNEL(rt, trace);
+      fns[7 + 3 * r] = ST_LOOP_KERNEL(rt, persistent);
+      fns[11 + r] = ST_TIMELINE_KERNEL(rt);
+    }
+    rt->ring = false;
     for (const void* f : fns)
       if (rt->cuda(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem2),
                    "cudaFuncSetAttribute") != ST_OK)
@@ -561,7 +592,15 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   }
   int max_clusters = 1 << 30;
   {
-    const void* fns[] = {ST_KERNEL(rt, fused), ST_KERNEL(rt, trace), ST_KERNEL(rt, persistent)};
+    const void* fns[8];
+    for (int r = 0; r < 2; ++r) {
+      rt->ring = r == 1;
+      fns[4 * r] = ST_LOOP_KERNEL(rt, fused);
+      fns[4 * r + 1] = ST_LOOP_KERNEL(rt, trace);
+      fns[4 * r + 2] = ST_LOOP_KERNEL(rt, persistent);
+      fns[4 * r + 3] = ST_TIMELINE_KERNEL(rt);
+    }
+    rt->ring = false;
     for (const void* f : fns) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(cluster);
@@ -724,6 +763,10 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   a.bar_timeout_ns = 2ull * 1000000000ull;
   a.cluster_size = rt->cluster;
   a.clusters = rt->nclusters;
+  {
+    const char* env = std::getenv("ST_WEIGHT_RING");
+    rt->ring = ring_supported(a, rt->elem, rt->cluster, rt->nclusters) && !(env && env[0] == '0');
+  }
   rt->control = (Control*)(rt->scratch + ctl_at);
   *out = rt;
   return ST_OK;
@@ -1047,7 +1090,7 @@ int st_device_timeline(st_runtime* rt, const float* inputs, size_t count, long l
     a.score = rt->dev_score;
     a.timeline = tl;
     a.timeline_capacity = (int)std::min<size_t>(capacity, 1u << 30);
-    st = launch_trace(rt, a, dev, count, nullptr);
+    st = launch_trace(rt, a, dev, count, nullptr, true);
   }
   if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "timeline run");
   if (st == ST_OK) st = check_device_error(rt);
@@ -1081,7 +1124,7 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
   const void* kernel = persistent_fn(rt);
   std::string name = "k2_persistent";
   if (rt->opt.backend == ST_BACKEND_FUSED) {
-    kernel = ST_KERNEL(rt, fused);
+    kernel = ST_LOOP_KERNEL(rt, fused);
     name = "k2_fused";
   } else if (rt->opt.backend == ST_BACKEND_CUDA || rt->opt.backend == ST_BACKEND_GRAPH) {
     kernel = ST_KERNEL(rt, ffn);
@@ -1099,6 +1142,7 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     << ",\"shared_bytes\":" << fa.sharedSizeBytes << ",\"dynamic_shared_bytes\":" << kSmem2
     << ",\"cluster\":" << rt->cluster << ",\"clusters\":" << rt->nclusters
     << ",\"cooperative_clusters\":" << (rt->coop_clusters ? "true" : "false")
+    << ",\"weight_ring\":" << (rt->ring ? "true" : "false")
     << ",\"attention_implementation\":\"one cluster per head, window split over the cluster, partials merged through DSMEM\""
     << ",\"matvec_implementation\":\"16-byte non-temporal loads; out- and down-projections K-split (per head, per ffn slice)\""
     << ",\"barriers_per_step\":" << forward_barrier_count(rt)

@@ -1,42 +1,55 @@
 // st_step.cuh -- the streaming step, organised around thread-block clusters.
 //
-// Measured on B200: a grid-wide barrier costs ~1.3 us and a hardware cluster
-// barrier ~0.24 us, so a step is built from two grid-wide dependencies per
-// layer and cheap cluster-local exchanges (DSMEM) for everything else. The
-// grid is NC clusters of CS CTAs (CS = 8 at full size). Per layer:
+// Measured on B200: a grid-wide barrier costs ~1.3 us, a hardware cluster
+// barrier ~0.24 us and a 512-thread __syncthreads ~0.06 us, so a step is built
+// from two grid-wide dependencies per layer, cheap cluster-local exchanges
+// (DSMEM) and as few CTA barriers as the data flow allows. The grid is NC
+// clusters of CS CTAs (CS = 8 at full size). Per layer:
 //
 //  attention block (cluster c owns heads c, c + NC, ...; other clusters idle)
 //    z = norm1(x)                      every CTA, from its shared-memory copy of x
-//    q,k,v rows of head h              split over the cluster's CTAs; RoPE + cast in
-//                                      the epilogue; values broadcast to every CTA of
-//                                      the cluster through distributed shared memory;
-//                                      k, v stored to ring slot t % W
+//    q,k,v rows of head h              row pairs split over the cluster's CTAs, one
+//                                      warp per pair; RoPE + cast in the warp's
+//                                      epilogue; values broadcast to every CTA of the
+//                                      cluster through DSMEM; k, v stored to slot t % W
 //    cluster barrier
-//    attention over [0, valid)         slots split over the cluster; (m, l, acc)
-//                                      partials broadcast through DSMEM
+//    attention over [0, valid)         slots split over the cluster; every warp keeps
+//                                      an online-softmax partial (m, l, acc) over its
+//                                      slots (K, V rows prefetched into shared memory
+//                                      with cp.async while the projections run); the
+//                                      CTA merges its warps and broadcasts (m, l, acc)
 //    cluster barrier
 //    merge -> attn_h (cast); out-projection K-split by head: P[h] = W_out[:, h] attn_h,
 //                                      output rows split over the cluster -> global
 //  grid sync A
 //  FFN block (every CTA)
 //    x' = cast(x + cast(sum_h P[h]))   redundantly, heads summed in a fixed order
-//    z = norm2(x'); gate/up rows of this CTA's ffn slice -> act = cast(silu(g) u)
+//    z = norm2(x'); gate/up row pairs of this CTA's ffn slice -> act = cast(silu(g) u)
 //    down-projection K-split over the slice (W_down stored transposed, [F][d]):
 //                                      partial d-vector, reduce-scattered inside the
 //                                      cluster through DSMEM -> D[cluster] -> global
 //  grid sync B
 //    x = cast(x' + cast(sum_c D[c]))   redundantly, clusters summed in a fixed order
 //
-// The input projection is computed redundantly by every CTA (no grid sync), and
-// CTA 0 runs the final norm and score head. The same block functions run as
-// separate kernels for the per-op and graph backends, where a kernel boundary
+// GEMVs: one warp (or a power-of-two lane group for short rows) computes a row
+// or a row pair completely -- lanes over 16-byte vectors, a butterfly over the
+// group -- so the epilogue runs in the same warp with no CTA barrier. With the
+// weight ring (kRing) the rows come from shared-memory chunks that warps
+// consume and release independently; otherwise straight from HBM. Both give
+// bit-identical sums, so every backend produces the same bits.
+//
+// The input projection is computed by every cluster (rows split over its CTAs),
+// and CTA 0 runs the final norm and score head. The per-op and graph backends
+// run the same block functions as separate kernels, where a kernel boundary
 // replaces each grid sync and the residual crosses kernels through global
 // buffers written by CTA 0. Cast points and op order follow the reference step
-// (reference src/cpu/Cpu.cpp:59-141); the GEMV sums are reassociated (per-head
-// and per-slice partials), which the fp32 1e-5 tolerance absorbs.
+// (reference src/cpu/Cpu.cpp:59-141); the sums are reassociated (per-lane
+// partials, per-head and per-slice partials, per-warp softmax partials), which
+// the fp32 1e-5 tolerance absorbs.
 #pragma once
 
 #include "st_device.cuh"
+#include "st_ring.cuh"
 
 namespace st {
 
@@ -45,28 +58,82 @@ constexpr int kMaxWidth = 1024;
 constexpr int kMaxHeadDim = 1024;
 constexpr int kMaxWindow = 4096;
 constexpr int kMaxFfn = 4096;
+constexpr int kAttDims = 256;                 // head dims one attention pass covers
+constexpr int kAttPerLane = kAttDims / 32;
+constexpr int kKvBytes = 16 * 1024;           // K and V rows one CTA prefetches per head
 
-// Dynamic shared memory of one CTA (~125 KB).
-struct alignas(16) Smem2 {
-  Smem g;                                        // GEMV input / reductions
+// Shared scratch of one step CTA (~110 KB; the weight ring takes the rest of
+// the CTA's shared memory). The attention buffers and the FFN buffers are
+// never live together (a grid sync separates them) and share one union; every
+// DSMEM target sits at the same offset in every CTA.
+struct alignas(128) Smem2 {
+  Smem g;                                        // GEMV input (event, attn_h) / reductions
   float xres[kMaxWidth];                         // residual entering the block
   float x2res[kMaxWidth];                        // residual after attention
   float qkv[3 * kMaxHeadDim];                    // q, k, v of the current head (DSMEM target)
-  float apart[kMaxCluster * (kMaxHeadDim + 2)];  // attention partials per rank (DSMEM target)
-  float dred[2 * kMaxWidth];                     // down partial rows per rank (DSMEM target)
-  float act[kMaxFfn];                            // this CTA's SwiGLU slice
-  float logits[kMaxWindow];
-  float gpart[2 * kMaxWidth];                    // per-group attention accumulators
-  float head[2];                                 // m, l of this CTA's attention partial
+  union {
+    struct {
+      float apart[kMaxCluster * (kMaxHeadDim + 2)];  // CTA attention partials per rank (DSMEM target)
+      float wpart[kWarps * (kAttDims + 2)];          // per-warp attention partials
+      alignas(16) unsigned char kv[kKvBytes];        // this CTA's K rows, then V rows
+    } at;
+    struct {
+      float act[kMaxFfn];                            // this CTA's SwiGLU slice
+      float dred[2 * kMaxWidth];                     // down partial rows per rank (DSMEM target)
+    } ff;
+  } u;
+  float gpart[2 * kMaxWidth];                    // down-projection group partials
+  float z[kMaxWidth];                            // norm output (GEMV input of QKV and gate/up)
+  float rope[kMaxHeadDim / 2];                   // RoPE frequencies, loaded once per launch
+  float2 rope_cs[kMaxHeadDim / 2];               // cos, sin of t * frequency for the current stream
+  unsigned long long t;                          // position of the stream being stepped
   int sync_ok;                                   // verdict of the last grid sync (DSMEM target)
   int tl_n;                                      // timeline entries written by this CTA
 };
 
-// Phase-boundary timestamp (CTA 0, thread 0) when a timeline buffer is given.
-__device__ __forceinline__ void tl_mark(const StepArgs& a, Smem2& sm) {
-  if (a.timeline && blockIdx.x == 0 && threadIdx.x == 0 && sm.tl_n < a.timeline_capacity)
-    a.timeline[sm.tl_n++] = clock64();
+// Dynamic shared memory of the step kernels: Smem2, the ring header, then the
+// ring bytes up to the per-block opt-in limit (227 KB on sm_100, 1 KB of it
+// left for the kernels' static shared variables).
+constexpr size_t kSmemLimit = 227 * 1024;
+constexpr size_t kStaticSmemReserve = 1024;
+constexpr size_t kRingOffset = (sizeof(Smem2) + sizeof(RingSmem) + 127) / 128 * 128;
+constexpr size_t kStepSmemBytes = kSmemLimit - kStaticSmemReserve;
+constexpr unsigned kRingCapacity = (unsigned)((kStepSmemBytes - kRingOffset) / 128 * 128);
+static_assert(kRingCapacity >= 2 * kChunkBytes, "the weight ring needs room for two chunks");
+
+// Timeline mark tags: the interval since the previous mark is charged to the
+// tag of the mark that ends it.
+enum TimelineTag : int {
+  kTlStepStart = 1, kTlInput, kTlNorm1, kTlRingWait, kTlGemv, kTlQkvRows, kTlQkvShared, kTlKvWait, kTlMerge,
+  kTlPv, kTlAttention, kTlPartialsShared, kTlOutProj, kTlSyncArrive, kTlSyncWait, kTlResidualHeads, kTlNorm2,
+  kTlGateUp, kTlDownPartial, kTlClusterReduce, kTlResidualClusters, kTlStepEnd, kTlRingFill, kTlIssueAt
+};
+
+// Phase-boundary mark (CTA 0, thread 0) when a timeline buffer is given:
+// clock64() << 8 | tag. Compiled only into the diagnostic kernel variants.
+template <bool kDiag = true>
+__device__ __forceinline__ void tl_mark(const StepArgs& a, Smem2& sm, int tag) {
+  if constexpr (kDiag)
+    if (a.timeline && blockIdx.x == 0 && threadIdx.x == 0 && sm.tl_n < a.timeline_capacity)
+      a.timeline[sm.tl_n++] = (long long)((clock64() << 8) | (long long)tag);
 }
+
+// Diagnostics: the issue time of the chunk just acquired, as a mark tagged
+// kTlIssueAt (not an interval; the host pairs it with the next mark).
+__device__ __forceinline__ void tl_mark_issue(const StepArgs& a, Smem2& sm, const RingSmem& rs, const Ring& rg) {
+  if (a.timeline && blockIdx.x == 0 && threadIdx.x == 0 && sm.tl_n < a.timeline_capacity)
+    a.timeline[sm.tl_n++] = (long long)((rs.issued_at[(rg.consumed) % kRingChunks] << 8) | (long long)kTlIssueAt);
+}
+
+// Compile-time shape of a step kernel: weights through the shared-memory ring
+// (kRing) or straight from HBM; diagnostics (timeline marks, trace buffers)
+// compiled in (kDiag) or not. The hot kernels carry no diagnostic code, which
+// keeps the per-layer instruction footprint small.
+template <bool R, bool D>
+struct StepCfg {
+  static constexpr bool kRing = R;
+  static constexpr bool kDiag = D;
+};
 
 // ---------------------------------------------------------------- cluster helpers
 __device__ __forceinline__ unsigned cluster_rank() {
@@ -108,13 +175,21 @@ __device__ __forceinline__ void dsmem_store_u32(int* local, unsigned rank, int v
   asm volatile("st.shared::cluster.u32 [%0], %1;" :: "r"(remote), "r"(v) : "memory");
 }
 
+// 16-byte global -> shared copy through L2 (generic proxy), and its waits.
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_addr(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 struct ClusterPos {
   unsigned rank, size, id, count;
   __device__ static ClusterPos get() { return {cluster_rank(), cluster_size(), cluster_id(), cluster_count()}; }
 };
 
 // Grid-wide barrier in cluster units. The cluster first meets at a hardware
-// barrier, then its rank-0 CTA alone arrives on the global counter and waits
+// barrier, then one thread of its rank-0 CTA (the ring issuer, which keeps
+// issuing weight chunks while it polls) alone arrives on the global counter and waits
 // (bounded, with the error word checked) and writes its verdict into every
 // CTA of the cluster through DSMEM before a second cluster barrier. Every CTA
 // of a cluster therefore returns the same verdict, so a failed wait can never
@@ -123,20 +198,31 @@ struct ClusterPos {
 struct ClusterGridSync {
   unsigned long long base;
   unsigned long long epoch;
-  __device__ bool sync(const StepArgs& a, unsigned long long timeout_ns, int* ok_slot) {
-    __threadfence();  // this thread's global writes, visible GPU-wide before the release below
+  // The cluster barrier (release/acquire at cluster scope) orders every
+  // thread's earlier writes before the arriving thread's gpu-scope release,
+  // so only that thread fences.
+  // With a ring, thread 0 of every CTA issues weight chunks once the whole
+  // CTA has arrived (every earlier chunk released), and the waiting thread
+  // keeps issuing while it polls, so the next phases' weights land during the
+  // wait.
+  __device__ bool sync(const StepArgs& a, unsigned long long timeout_ns, int* ok_slot, Smem2* tl = nullptr,
+                       Ring* rg = nullptr, RingSmem* rs = nullptr) {
     cluster_sync();
+    if (tl) tl_mark(a, *tl, kTlSyncArrive);
+    if (rg) ring_fill(*rg, *rs);
     const unsigned rank = cluster_rank();
-    if (rank == 0 && threadIdx.x == 0) {
+    if (rank == 0 && threadIdx.x == kIssuer) {
       epoch += 1;
       const unsigned long long target = base + epoch * cluster_count();
       int good = ld_volatile_int(a.error) == 0;
       if (good) {
+        __threadfence();
         red_release_gpu_add(a.bar_counter, 1ull);
         unsigned long long start = 0;
         unsigned int polls = 0;
         while (ld_acquire_gpu(a.bar_counter) < target) {
           if ((++polls & 63u) == 0) {
+            if (rg) ring_fill(*rg, *rs);
             if (ld_volatile_int(a.error) != 0) { good = 0; break; }
             const unsigned long long now = globaltimer();
             if (start == 0) start = now;
@@ -148,6 +234,7 @@ struct ClusterGridSync {
       for (unsigned k = 0; k < n; ++k) dsmem_store_u32(ok_slot, k, good);
     }
     cluster_sync();
+    if (tl) tl_mark(a, *tl, kTlSyncWait);
     return *reinterpret_cast<volatile int*>(ok_slot) != 0;
   }
 };
@@ -167,200 +254,472 @@ __device__ __forceinline__ void split(int units, int part, int parts, int& lo, i
   hi = (int)(((long long)units * (part + 1)) / parts);
 }
 
-// GEMV over rows [r_begin, r_end) of W (row-major, `cols`) against sm.g.xs, in
-// tiles; epi(r0, n) consumes sm.g.rowsum[0..n).
-template <typename T, typename Epi>
-__device__ void rows_gemv(const T* W, int r_begin, int r_end, int cols, Smem& sm, Epi epi) {
-  for (int r0 = r_begin; r0 < r_end; r0 += kRowTile) {
-    const int n = min(kRowTile, r_end - r0);
-    gemv_tile<T>(W, r0, n, cols, sm);
-    epi(r0, n);
-    __syncthreads();
-  }
-}
-
-// RMSNorm of a shared-memory vector into sm.g.xs (reference src/cpu/Cpu.cpp:43-57).
-template <typename T>
-__device__ void norm_smem(const float* x, const T* gain, int width, float eps, Smem2& sm) {
-  float s = 0.f;
-  for (int i = threadIdx.x; i < width; i += kThreads) s += x[i] * x[i];
-  const float total = block_sum(s, sm.g);
-  const float scale = 1.0f / sqrtf(total / (float)width + eps);
-  for (int i = threadIdx.x; i < width; i += kThreads)
-    sm.g.xs[i] = Storage<T>::round(x[i] * scale * Storage<T>::load(gain, i));
-  __syncthreads();
-}
-
 __device__ __forceinline__ int valid_length(unsigned long long t, int window) {
   return t + 1 < (unsigned long long)window ? (int)(t + 1) : window;
 }
 
-// ---------------------------------------------------------------- blocks
-// x = cast(W_in input) for stream s into `dst` (shared memory), all rows, this CTA.
+// ---------------------------------------------------------------- warp GEMV
+// Geometry of a GEMV over rows of `cols` elements of type T. Aligned rows
+// (cols a multiple of the 16-byte vector) are split over a power-of-two group
+// of `lpr` lanes, each lane taking vectors sl, sl + lpr, ...; unaligned rows
+// fall back to one warp per row with scalar loads.
 template <typename T>
-__device__ void block_input(const StepArgs& a, int s, const float* input, float* dst, Smem2& sm) {
-  for (int i = threadIdx.x; i < a.features; i += kThreads) sm.g.xs[i] = __ldcv(input + (size_t)s * a.features + i);
-  __syncthreads();
-  rows_gemv<T>((const T*)a.input_w, 0, a.width, a.features, sm.g, [&](int r0, int n) {
-    for (int i = threadIdx.x; i < n; i += kThreads) dst[r0 + i] = Storage<T>::round(sm.g.rowsum[i]);
-  });
+struct RowGeom {
+  int cols, units, lpr, rpw;
+  bool vec;
+  __device__ RowGeom(int c, int u, int l, int r, bool v) : cols(c), units(u), lpr(l), rpw(r), vec(v) {}
+  __device__ explicit RowGeom(int c) : cols(c) {
+    constexpr int V = Storage<T>::kVec;
+    vec = (c % V) == 0;
+    units = vec ? c / V : c;
+    int p = 1;
+    while (p < units && p < 32) p <<= 1;
+    lpr = vec ? p : 32;
+    rpw = 32 / lpr;
+  }
+};
+
+// The lane's share of a GEMV input vector xs, held in registers for a whole
+// phase: the V floats of each vector sl + lpr * k, k < kN, that its rows meet
+// (zeros past the row). Every row the warp computes reuses them, so shared
+// memory carries the weights only.
+template <typename T>
+struct XRegs {
+  static constexpr int V = Storage<T>::kVec;
+  static constexpr int kN = kMaxCols / V / 32;  // vectors per lane at most
+  float x[kN * V];
+  __device__ __forceinline__ void load(const float* xs, const RowGeom<T>& g, int sl) {
+#pragma unroll
+    for (int k = 0; k < kN; ++k) {
+      const int v = sl + g.lpr * k;
+#pragma unroll
+      for (int e = 0; e < V; e += 4) {
+        const float4 q = g.vec && v < g.units ? *reinterpret_cast<const float4*>(xs + v * V + e)
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[k * V + e] = q.x;
+        x[k * V + e + 1] = q.y;
+        x[k * V + e + 2] = q.z;
+        x[k * V + e + 3] = q.w;
+      }
+    }
+  }
+};
+
+__device__ __forceinline__ uint4 ld_shared_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(smem_addr(p)));
+  return r;
 }
 
-// Attention for head h of stream s over this CTA's share of [0, valid): logits,
-// local softmax statistics and sum p V; the current slot's k, v come from the
-// cluster-shared sm.qkv, older slots from the ring. Leaves (m, l) in sm.head and
-// acc in sm.gpart[0..hd).
+// Sum over one 16-byte weight vector times V register floats, in element order.
 template <typename T>
-__device__ void attention_share(const StepArgs& a, int l, int s, int h, int j0, int j1, int slot, Smem2& sm) {
-  const int hd = a.head_dim, W = a.window, H = a.heads;
+__device__ __forceinline__ float dot_regs(const uint4& w, const float* x) {
+  constexpr int V = Storage<T>::kVec;
+  float f[V];
+  Storage<T>::unpack(w, f);
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < V; ++k) acc = fmaf(f[k], x[k], acc);
+  return acc;
+}
+
+// U dot products of consecutive rows (row stride `cols`) by the lpr lanes of
+// one group; every lane of the group returns the full sums. Lanes of an
+// invalid group compute zeros but still take part in the shuffles. Aligned
+// rows use the register copy xr; unaligned rows read xs.
+template <typename T, int U, bool kShared>
+__device__ __forceinline__ void dot_rows(const T* row, const RowGeom<T>& g, int sl, const XRegs<T>& xr,
+                                         const float* xs, bool valid, float (&out)[U]) {
+  constexpr int V = Storage<T>::kVec;
+  constexpr int kN = XRegs<T>::kN;
+  constexpr int kB = 4;  // vectors per lane in flight per row
+#pragma unroll
+  for (int u = 0; u < U; ++u) out[u] = 0.f;
+  if (g.vec) {
+#pragma unroll
+    for (int k0 = 0; k0 < kN; k0 += kB) {
+      if (sl + g.lpr * k0 >= g.units) break;
+      uint4 w[U][kB];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+          const int v = sl + g.lpr * (k0 + b);
+          const T* p = row + (size_t)u * g.cols + (size_t)v * V;
+          if (valid && v < g.units) {
+            if constexpr (kShared) w[u][b] = ld_shared_v4(p);
+            else w[u][b] = ld_stream(p);
+          } else {
+            w[u][b] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int b = 0; b < kB; ++b)
+          if (sl + g.lpr * (k0 + b) < g.units) out[u] += dot_regs<T>(w[u][b], xr.x + (k0 + b) * V);
+    }
+  } else if (valid) {
+    for (int e = sl; e < g.cols; e += 32)
+#pragma unroll
+      for (int u = 0; u < U; ++u) out[u] = fmaf(Storage<T>::load(row + (size_t)u * g.cols, e), xs[e], out[u]);
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+    for (int o = g.lpr >> 1; o > 0; o >>= 1) out[u] += __shfl_xor_sync(0xffffffffu, out[u], o);
+}
+
+// Rows [0, n) of W (n a multiple of U) against the input vector (xr in
+// registers, xs in shared memory), in groups of U rows spread over the warps;
+// epi(row, v[U], sl) runs on every lane of the group that computed rows
+// row .. row+U-1 (sl = lane within the group). No CTA barrier.
+// Groups are dealt to warps by their index within the whole span (g0 = index
+// of this block's first group), so consecutive chunks of one span go to
+// different warps and are computed concurrently.
+template <typename T, int U, bool kShared, typename Epi>
+__device__ __forceinline__ void warp_rows_x(const T* W, int n, const RowGeom<T>& g, const XRegs<T>& xr,
+                                            const float* xs, Epi&& epi, int g0 = 0) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const size_t head_base = ((((size_t)s * a.layers + l) * H + h) * (size_t)W) * hd;
-  const T* K = (const T*)a.keys + head_base;
-  const T* V = (const T*)a.values + head_base;
+  const int sub = lane / g.lpr, sl = lane - sub * g.lpr;
+  const int groups = n / U, per_pass = kWarps * g.rpw;
+  const int first = ((warp * g.rpw - g0) % per_pass + per_pass) % per_pass;
+  for (int base = first; base < groups; base += per_pass) {
+    const int gi = base + sub;
+    const bool valid = gi < groups;
+    float v[U];
+    dot_rows<T, U, kShared>(W + (size_t)(valid ? gi : 0) * U * g.cols, g, sl, xr, xs, valid, v);
+    if (valid) epi(gi * U, v, sl);
+  }
+}
+
+// Same, loading the register copy of xs first.
+template <typename T, int U, bool kShared, typename Epi>
+__device__ __forceinline__ void warp_rows(const T* W, int n, const RowGeom<T>& g, const float* xs, Epi&& epi) {
+  XRegs<T> xr;
+  xr.load(xs, g, (threadIdx.x & 31) % g.lpr);
+  warp_rows_x<T, U, kShared>(W, n, g, xr, xs, epi);
+}
+
+// The next `rows` rows of the ring's current span (groups of U rows, as the
+// chunk table was cut), chunk by chunk; epi gets rows relative to the span.
+template <typename T, int U, class Cfg, typename Epi>
+__device__ __forceinline__ void ring_rows(const StepArgs& a, Ring& rg, RingSmem& rs, Smem2& sm, int rows,
+                                          const RowGeom<T>& g, const float* xs, Epi&& epi) {
+  const int rpc = rows_per_chunk(g.cols * (int)sizeof(T), U);
+  XRegs<T> xr;
+  xr.load(xs, g, (threadIdx.x & 31) % g.lpr);
+  for (int c0 = 0; c0 < rows; c0 += rpc) {
+    const int n = min(rpc, rows - c0);
+    const T* p = (const T*)ring_acquire(a, rg, rs);
+    tl_mark<Cfg::kDiag>(a, sm, kTlRingWait);
+    if constexpr (Cfg::kDiag) tl_mark_issue(a, sm, rs, rg);
+    warp_rows_x<T, U, true>(p, n, g, xr, xs, [&](int r, const float (&v)[U], int sl) { epi(c0 + r, v, sl); }, c0 / U);
+    tl_mark<Cfg::kDiag>(a, sm, kTlGemv);
+    ring_release(rg, rs);
+    tl_mark<Cfg::kDiag>(a, sm, kTlRingFill);
+  }
+}
+
+// The issuer reclaims released chunks and issues more (kRing only); called
+// right after barriers, when every warp has released what it consumed.
+template <class Cfg>
+__device__ __forceinline__ void ring_poll(Ring& rg, RingSmem& rs) {
+  if constexpr (Cfg::kRing) ring_fill(rg, rs);
+}
+
+// Rows [0, rows) of a weight matrix: from the ring (kRing) or straight from
+// global memory at W.
+template <typename T, int U, class Cfg, typename Epi>
+__device__ __forceinline__ void gemv_rows(const StepArgs& a, Ring& rg, RingSmem& rs, Smem2& sm, const T* W, int rows,
+                                          const RowGeom<T>& g, const float* xs, Epi&& epi) {
+  if constexpr (Cfg::kRing) ring_rows<T, U, Cfg>(a, rg, rs, sm, rows, g, xs, epi);
+  else warp_rows<T, U, false>(W, rows, g, xs, epi);
+}
+
+// ---------------------------------------------------------------- norms and residuals
+// RMSNorm of x into out, cast to storage precision (reference
+// src/cpu/Cpu.cpp:43-57: scale = 1/sqrt(mean(x^2)+eps), out = x*scale*g).
+// Thread i reads x[i], x[i + kThreads], ...: callers that just wrote x with
+// the same mapping need no barrier first. Ends with a barrier (out complete).
+template <typename T>
+__device__ __forceinline__ void norm_vec(const float* x, const T* gain, int width, float eps, Smem2& sm, float* out) {
+  float s = 0.f;
+#pragma unroll 1
+  for (int i = threadIdx.x; i < width; i += kThreads) s += x[i] * x[i];
+  const float total = block_sum(s, sm.g);
+  const float scale = 1.0f / sqrtf(total / (float)width + eps);
+#pragma unroll 1
+  for (int i = threadIdx.x; i < width; i += kThreads) out[i] = Storage<T>::round(x[i] * scale * Storage<T>::load(gain, i));
+  __syncthreads();
+}
+
+// The norm with its gain vector from the ring (kRing) or from `gain`.
+template <typename T, class Cfg>
+__device__ __forceinline__ void norm_block(const StepArgs& a, Ring& rg, RingSmem& rs, Smem2& sm, const float* x,
+                                           const T* gain, float* out) {
+  if constexpr (Cfg::kRing) {
+    const T* g = (const T*)ring_acquire(a, rg, rs);
+    norm_vec<T>(x, g, a.width, a.epsilon, sm, out);
+    ring_release(rg, rs);
+  } else {
+    norm_vec<T>(x, gain, a.width, a.epsilon, sm, out);
+  }
+}
+
+// p[0] + p[stride] + ... + p[(n-1) stride], added in index order, with the
+// L2 loads issued 16 at a time ahead of the adds (the partials were written
+// by other CTAs of this launch, so they are read with ld.global.cg).
+__device__ __forceinline__ float sum_rows(const float* p, int stride, int n) {
+  float acc = 0.f;
+#pragma unroll 1
+  for (int k0 = 0; k0 < n; k0 += 16) {
+    float v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[u] = k0 + u < n ? ld_cg(p + (size_t)(k0 + u) * stride) : 0.f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+      if (k0 + u < n) acc += v[u];
+  }
+  return acc;
+}
+
+// x' = cast(x + cast(sum_h P[h])) from sm.xres into sm.x2res (thread i writes
+// element i, i + kThreads, ...; no barrier).
+template <typename T>
+__device__ __forceinline__ void residual_from_heads(const StepArgs& a, int s, Smem2& sm) {
+  const int d = a.width;
+  const float* P = a.pout + (size_t)s * a.heads * d;
+#pragma unroll 1
+  for (int i = threadIdx.x; i < d; i += kThreads)
+    sm.x2res[i] = Storage<T>::round(sm.xres[i] + Storage<T>::round(sum_rows(P + i, d, a.heads)));
+}
+
+// x = cast(x' + cast(sum_c D[c])) from sm.x2res into sm.xres (same mapping; no barrier).
+template <typename T>
+__device__ __forceinline__ void residual_from_clusters(const StepArgs& a, int s, int nclusters, Smem2& sm) {
+  const int d = a.width;
+  const float* D = a.dpart + (size_t)s * nclusters * d;
+#pragma unroll 1
+  for (int i = threadIdx.x; i < d; i += kThreads)
+    sm.xres[i] = Storage<T>::round(sm.x2res[i] + Storage<T>::round(sum_rows(D + i, d, nclusters)));
+}
+
+// ---------------------------------------------------------------- blocks
+// Position of stream s into sm.t (read by other threads after the next barrier).
+__device__ __forceinline__ void load_position(const StepArgs& a, int s, Smem2& sm) {
+  if (threadIdx.x == 0) sm.t = ld_cg_u64(a.position + s);
+}
+
+// RoPE rotation of the current position, angle = float(t) * frequency
+// (reference src/cpu/Cpu.cpp:81-89), for every dim pair; needs sm.t visible,
+// and is read after the caller's next barrier.
+__device__ __forceinline__ void rope_table(const StepArgs& a, Smem2& sm) {
+  const float tf = (float)sm.t;
+  for (int i = threadIdx.x; i < a.head_dim / 2; i += kThreads) {
+    const float angle = tf * sm.rope[i];
+    sm.rope_cs[i] = make_float2(cosf(angle), sinf(angle));
+  }
+}
+
+// x = cast(W_in input) for stream s into sm.xres. With the ring the cluster
+// splits the rows and broadcasts them into every member through DSMEM;
+// otherwise this CTA computes every row. Ends after a barrier.
+template <typename T, class Cfg>
+__device__ void step_input(const StepArgs& a, int s, const float* input, const ClusterPos& cp, Smem2& sm, Ring& rg,
+                           RingSmem& rs) {
+  for (int i = threadIdx.x; i < a.features; i += kThreads) sm.g.xs[i] = __ldcv(input + (size_t)s * a.features + i);
+  __syncthreads();
+  rope_table(a, sm);  // sm.t was written before the barrier; published by the barrier below
+  const RowGeom<T> g(a.features);
+  if constexpr (Cfg::kRing) {
+    int lo, hi;
+    split(a.width, (int)cp.rank, (int)cp.size, lo, hi);
+    ring_rows<T, 1, Cfg>(a, rg, rs, sm, hi - lo, g, sm.g.xs, [&](int r, const float (&v)[1], int sl) {
+      const float x = Storage<T>::round(v[0]);
+      for (unsigned k = (unsigned)sl; k < cp.size; k += (unsigned)g.lpr) dsmem_store(&sm.xres[lo + r], k, x);
+    });
+    cluster_sync();
+  } else {
+    warp_rows<T, 1, false>((const T*)a.input_w, a.width, g, sm.g.xs, [&](int r, const float (&v)[1], int sl) {
+      if (sl == 0) sm.xres[r] = Storage<T>::round(v[0]);
+    });
+    __syncthreads();
+  }
+}
+
+// Issue cp.async copies of this CTA's K and V rows [j0, j1) of one head into
+// sm.u.at.kv (K rows, then V rows), skipping the slot this step overwrites.
+// Returns false (nothing issued) when they do not fit or are not 16-byte rows.
+template <typename T>
+__device__ __forceinline__ bool kv_prefetch(const T* keys, const T* values, int j0, int j1, int slot, int hd,
+                                            Smem2& sm) {
+  const int row_bytes = hd * (int)sizeof(T);
+  const int n = j1 - j0;
+  if (row_bytes % 16 != 0 || 2 * n * row_bytes > kKvBytes) return false;
+  const int vpr = row_bytes / 16, vecs = n * vpr;
+  for (int i = threadIdx.x; i < 2 * vecs; i += kThreads) {
+    const bool is_v = i >= vecs;
+    const int k = is_v ? i - vecs : i;
+    const int j = j0 + k / vpr;
+    if (j == slot) continue;
+    const char* src = (const char*)(is_v ? values : keys) + (size_t)j0 * row_bytes + (size_t)k * 16;
+    cp_async16(sm.u.at.kv + (size_t)i * 16, src);
+  }
+  cp_async_commit();
+  return true;
+}
+
+// Attention of head h over this CTA's slots [j0, j1): every warp folds its
+// slots j0 + warp, j0 + warp + kWarps, ... into an online-softmax partial
+// (m, l, acc) (reference src/cpu/Cpu.cpp:97-110: logits q.k / sqrt(hd), softmax
+// over the retained slots, sum p v); the CTA merges its warps in warp order
+// and broadcasts (m, l, acc) into apart[rank] of every CTA of the cluster.
+// Head dims are covered kAttDims at a time (one pass for hd <= 256).
+template <typename T, class Cfg>
+__device__ void attention_share(const StepArgs& a, int l, int s, int h, int j0, int j1, int slot, bool kv_smem,
+                                const ClusterPos& cp, Smem2& sm) {
+  const int hd = a.head_dim, W = a.window;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const size_t head_base = ((((size_t)s * a.layers + l) * a.heads + h) * (size_t)W) * hd;
+  const T* Kg = (const T*)a.keys + head_base;
+  const T* Vg = (const T*)a.values + head_base;
+  const T* Ks = reinterpret_cast<const T*>(sm.u.at.kv);
+  const T* Vs = Ks + (size_t)(j1 - j0) * hd;
   const float* q = sm.qkv;
   const float* kcur = sm.qkv + hd;
   const float* vcur = sm.qkv + 2 * hd;
-  const int n = j1 - j0;
-  const float inv = sqrtf((float)hd);
-  // logits: warp per slot, lanes over dims
-  for (int j = j0 + warp; j < j1; j += kWarps) {
-    float dot = 0.f;
-    if (j == slot) {
-      for (int i = lane; i < hd; i += 32) dot = fmaf(q[i], kcur[i], dot);
-    } else {
-      const T* krow = K + (size_t)j * hd;
-      for (int i = lane; i < hd; i += 32) dot = fmaf(q[i], Storage<T>::load_cg(krow, i), dot);
-    }
-    dot = warp_sum(dot);
-    if (lane == 0) sm.logits[j - j0] = dot / inv;
-  }
-  __syncthreads();
-  float m = -INFINITY;
-  for (int j = threadIdx.x; j < n; j += kThreads) m = fmaxf(m, sm.logits[j]);
-  // block max
-  m = warp_max(m);
-  if (lane == 0) sm.g.warp_scratch[warp] = m;
-  __syncthreads();
-  if (warp == 0) {
-    float t = lane < kWarps ? sm.g.warp_scratch[lane] : -INFINITY;
-    t = warp_max(t);
-    if (lane == 0) sm.g.scalar[1] = t;
-  }
-  __syncthreads();
-  m = sm.g.scalar[1];
-  float psum = 0.f;
-  for (int j = threadIdx.x; j < n; j += kThreads) {
-    const float p = expf(sm.logits[j] - m);
-    sm.logits[j] = p;
-    psum += p;
-  }
-  const float lsum = block_sum(psum, sm.g);
-  // acc[d] = sum_j p_j V[j][d]. With hd < kThreads the CTA splits into
-  // `groups` thread groups over dims, group g taking slots j0+g, j0+g+groups, ...;
-  // the group sums are then added in group order.
-  if (hd < kThreads) {
-    const int groups = kThreads / hd;
-    const int g = threadIdx.x / hd, dd = threadIdx.x - g * hd;
-    if (g < groups) {
-      float acc = 0.f;
-      for (int j = j0 + g; j < j1; j += groups) {
-        const float v = j == slot ? vcur[dd] : Storage<T>::load_cg(V + (size_t)j * hd, dd);
-        acc = fmaf(sm.logits[j - j0], v, acc);
+  const float root = sqrtf((float)hd);
+  float* wp = sm.u.at.wpart + warp * (kAttDims + 2);
+  float* mine = sm.u.at.apart + (size_t)cp.rank * (hd + 2);
+  for (int b = 0; b < hd; b += kAttDims) {
+    const int nb = min(kAttDims, hd - b);
+    float m = -INFINITY, lsum = 0.f, acc[kAttPerLane];
+#pragma unroll
+    for (int k = 0; k < kAttPerLane; ++k) acc[k] = 0.f;
+    for (int j = j0 + warp; j < j1; j += kWarps) {
+      const bool cur = j == slot;
+      const T* krow = kv_smem ? Ks + (size_t)(j - j0) * hd : Kg + (size_t)j * hd;
+      const T* vrow = kv_smem ? Vs + (size_t)(j - j0) * hd : Vg + (size_t)j * hd;
+      float dot = 0.f;
+      for (int i = lane; i < hd; i += 32) {
+        const float kv = cur ? kcur[i] : kv_smem ? Storage<T>::load(krow, i) : Storage<T>::load_cg(krow, i);
+        dot = fmaf(q[i], kv, dot);
       }
-      sm.gpart[g * hd + dd] = acc;
-    }
-    __syncthreads();
-    float total = 0.f;
-    if (threadIdx.x < hd)
-      for (int gg = 0; gg < groups; ++gg) total += sm.gpart[gg * hd + threadIdx.x];
-    __syncthreads();
-    if (threadIdx.x < hd) sm.gpart[threadIdx.x] = total;
-  } else {
-    for (int dd = threadIdx.x; dd < hd; dd += kThreads) {
-      float acc = 0.f;
-      for (int j = j0; j < j1; ++j) {
-        const float v = j == slot ? vcur[dd] : Storage<T>::load_cg(V + (size_t)j * hd, dd);
-        acc = fmaf(sm.logits[j - j0], v, acc);
+      dot = warp_sum(dot);
+      const float logit = dot / root;
+      const float mn = fmaxf(m, logit);
+      const float so = expf(m - mn), p = expf(logit - mn);
+      lsum = lsum * so + p;
+      m = mn;
+#pragma unroll
+      for (int k = 0; k < kAttPerLane; ++k) {
+        const int dd = lane + 32 * k;
+        if (dd < nb) {
+          const float v = cur ? vcur[b + dd] : kv_smem ? Storage<T>::load(vrow, b + dd) : Storage<T>::load_cg(vrow, b + dd);
+          acc[k] = fmaf(acc[k], so, p * v);
+        }
       }
-      sm.gpart[dd] = acc;
     }
+    if (lane == 0) {
+      wp[0] = m;
+      wp[1] = lsum;
+    }
+#pragma unroll
+    for (int k = 0; k < kAttPerLane; ++k)
+      if (lane + 32 * k < nb) wp[2 + lane + 32 * k] = acc[k];
+    __syncthreads();
+    if (b == 0) tl_mark<Cfg::kDiag>(a, sm, kTlPv);
+    // CTA merge in warp order; item (rank k, value i) per thread, i = 0: m,
+    // 1: l, 2..: acc[b + i - 2]; every item recomputes the merge weights.
+    const int vals = nb + 2, items = vals * (int)cp.size;
+    for (int it = threadIdx.x; it < items; it += kThreads) {
+      const int k = it / vals, i = it - k * vals;
+      if (b > 0 && i < 2) continue;  // m and l were sent with the first pass
+      float M = -INFINITY;
+      for (int w = 0; w < kWarps; ++w) {
+        const float* pw = sm.u.at.wpart + w * (kAttDims + 2);
+        if (pw[1] > 0.f) M = fmaxf(M, pw[0]);
+      }
+      float r = 0.f;
+      for (int w = 0; w < kWarps; ++w) {
+        const float* pw = sm.u.at.wpart + w * (kAttDims + 2);
+        if (pw[1] > 0.f) r = fmaf(pw[i == 1 ? 1 : i], expf(pw[0] - M), r);
+      }
+      const float v = i == 0 ? M : r;
+      dsmem_store(mine + (i < 2 ? i : b + i), (unsigned)k, v);
+    }
+    if (b + kAttDims < hd) __syncthreads();  // wpart is rewritten by the next pass
   }
-  if (threadIdx.x == 0) {
-    sm.head[0] = n > 0 ? m : -INFINITY;
-    sm.head[1] = n > 0 ? lsum : 0.f;
-  }
-  __syncthreads();
 }
 
-// One head h of one stream, run by the CTAs of one cluster.
-template <typename T>
-__device__ void attention_head(const StepArgs& a, int l, int s, int h, const ClusterPos& cp, Smem2& sm) {
+// One head h of one stream, run by the CTAs of one cluster; z (norm1 output)
+// is in sm.z. Leaves P[h] rows of this CTA in global memory.
+template <typename T, class Cfg>
+__device__ void attention_head(const StepArgs& a, int l, int s, int h, const ClusterPos& cp, Smem2& sm, Ring& rg,
+                               RingSmem& rs) {
   const int d = a.width, hd = a.head_dim, W = a.window;
   const LayerPtrs& w = a.layer[l];
-  const unsigned long long t = ld_cg_u64(a.position + s);
+  const unsigned long long t = sm.t;
   const int slot = (int)(t % (unsigned long long)W);
   const int valid = valid_length(t, W);
   T* keys = (T*)a.keys + ((((size_t)s * a.layers + l) * a.heads + h) * (size_t)W) * hd;
   T* values = (T*)a.values + ((((size_t)s * a.layers + l) * a.heads + h) * (size_t)W) * hd;
-  // q, k, v rows of head h (head-major [H][3 hd][d]); pairs split over the cluster.
-  const T* Wh = (const T*)w.qkv + (size_t)h * 3 * hd * d;
-  int lo, hi;
-  split(3 * hd / 2, cp.rank, cp.size, lo, hi);
-  const float tf = (float)t;
-  rows_gemv<T>(Wh, 2 * lo, 2 * hi, d, sm.g, [&](int r0, int n) {
-    for (int p = threadIdx.x; p < n / 2; p += kThreads) {
-      const int row = r0 + 2 * p;
-      const int which = row / hd, dim = row - which * hd;
-      float v0 = Storage<T>::round(sm.g.rowsum[2 * p]);
-      float v1 = Storage<T>::round(sm.g.rowsum[2 * p + 1]);
-      if (which < 2) {
-        const float angle = tf * a.rope_freq[dim >> 1];
-        const float co = cosf(angle), si = sinf(angle);
-        const float r0v = v0 * co - v1 * si;
-        const float r1v = v0 * si + v1 * co;
-        v0 = Storage<T>::round(r0v);
-        v1 = Storage<T>::round(r1v);
-      }
-      for (unsigned k = 0; k < cp.size; ++k) {
-        dsmem_store(&sm.qkv[row], k, v0);
-        dsmem_store(&sm.qkv[row + 1], k, v1);
-      }
-      if (which > 0) {
-        T* ring = which == 1 ? keys : values;
-        const size_t at = (size_t)slot * hd + dim;
-        Storage<T>::store(ring, at, v0);
-        Storage<T>::store(ring, at + 1, v1);
-      }
-    }
-  });
-  tl_mark(a, sm);  // qkv rows done
-  cluster_sync();
-  tl_mark(a, sm);  // q, k, v shared
-  if (a.trace_qkv && cp.rank == 0)
-    for (int i = threadIdx.x; i < 3 * hd; i += kThreads)
-      a.trace_qkv[(size_t)s * 3 * d + (size_t)(i / hd) * d + (size_t)h * hd + i % hd] = sm.qkv[i];
-  // this CTA's share of the retained slots
   int j0, j1;
-  split(valid, cp.rank, cp.size, j0, j1);
-  attention_share<T>(a, l, s, h, j0, j1, slot, sm);
-  tl_mark(a, sm);  // attention share done
-  float* mine = sm.apart + (size_t)cp.rank * (hd + 2);
-  for (int i = threadIdx.x; i < hd + 2; i += kThreads) {
-    const float v = i == 0 ? sm.head[0] : i == 1 ? sm.head[1] : sm.gpart[i - 2];
-    for (unsigned k = 0; k < cp.size; ++k) dsmem_store(mine + i, k, v);
-  }
+  split(valid, (int)cp.rank, (int)cp.size, j0, j1);
+  const bool kv_smem = kv_prefetch<T>(keys, values, j0, j1, slot, hd, sm);
+  // q, k, v rows of head h (head-major [H][3 hd][d]); pairs split over the cluster.
+  int lo, hi;
+  split(3 * hd / 2, (int)cp.rank, (int)cp.size, lo, hi);
+  const RowGeom<T> gd(d);
+  auto qkv_epi = [&](int r, const float (&v)[2], int sl) {
+    const int row = 2 * lo + r;
+    const int which = row / hd, dim = row - which * hd;
+    float v0 = Storage<T>::round(v[0]);
+    float v1 = Storage<T>::round(v[1]);
+    if (which < 2) {
+      const float2 cs = sm.rope_cs[dim >> 1];
+      const float r0v = v0 * cs.x - v1 * cs.y;
+      const float r1v = v0 * cs.y + v1 * cs.x;
+      v0 = Storage<T>::round(r0v);
+      v1 = Storage<T>::round(r1v);
+    }
+    for (unsigned k = (unsigned)sl; k < cp.size; k += (unsigned)gd.lpr) {
+      dsmem_store(&sm.qkv[row], k, v0);
+      dsmem_store(&sm.qkv[row + 1], k, v1);
+    }
+    if (which > 0 && sl == gd.lpr - 1) {
+      T* ring = which == 1 ? keys : values;
+      const size_t at = (size_t)slot * hd + dim;
+      Storage<T>::store(ring, at, v0);
+      Storage<T>::store(ring, at + 1, v1);
+    }
+  };
+  gemv_rows<T, 2, Cfg>(a, rg, rs, sm, (const T*)w.qkv + ((size_t)h * 3 * hd + 2 * (size_t)lo) * d, 2 * (hi - lo),
+                         gd, sm.z, qkv_epi);
+  if (kv_smem) cp_async_wait_all();
+  tl_mark<Cfg::kDiag>(a, sm, kTlQkvRows);
   cluster_sync();
-  tl_mark(a, sm);  // partials shared
+  ring_poll<Cfg>(rg, rs);
+  tl_mark<Cfg::kDiag>(a, sm, kTlQkvShared);
+  if constexpr (Cfg::kDiag)
+    if (a.trace_qkv && cp.rank == 0)
+      for (int i = threadIdx.x; i < 3 * hd; i += kThreads)
+        a.trace_qkv[(size_t)s * 3 * d + (size_t)(i / hd) * d + (size_t)h * hd + i % hd] = sm.qkv[i];
+  attention_share<T, Cfg>(a, l, s, h, j0, j1, slot, kv_smem, cp, sm);
+  tl_mark<Cfg::kDiag>(a, sm, kTlAttention);
+  cluster_sync();
+  tl_mark<Cfg::kDiag>(a, sm, kTlPartialsShared);
   // merge the cluster's partials in rank order -> attn_h (cast) in sm.g.xs[0..hd)
   for (int i = threadIdx.x; i < hd; i += kThreads) {
     float M = -INFINITY;
     for (unsigned k = 0; k < cp.size; ++k) {
-      const float* pk = sm.apart + (size_t)k * (hd + 2);
+      const float* pk = sm.u.at.apart + (size_t)k * (hd + 2);
       if (pk[1] > 0.f) M = fmaxf(M, pk[0]);
     }
     float L = 0.f, acc = 0.f;
     for (unsigned k = 0; k < cp.size; ++k) {
-      const float* pk = sm.apart + (size_t)k * (hd + 2);
+      const float* pk = sm.u.at.apart + (size_t)k * (hd + 2);
       if (pk[1] > 0.f) {
         const float scale = expf(pk[0] - M);
         L = fmaf(pk[1], scale, L);
@@ -368,121 +727,121 @@ __device__ void attention_head(const StepArgs& a, int l, int s, int h, const Clu
       }
     }
     sm.g.xs[i] = Storage<T>::round(acc / L);
-    if (a.trace_attention && cp.rank == 0) a.trace_attention[(size_t)s * d + (size_t)h * hd + i] = sm.g.xs[i];
+    if constexpr (Cfg::kDiag)
+      if (a.trace_attention && cp.rank == 0) a.trace_attention[(size_t)s * d + (size_t)h * hd + i] = sm.g.xs[i];
   }
   __syncthreads();
+  tl_mark<Cfg::kDiag>(a, sm, kTlMerge);
   // out-projection partial of this head: rows split over the cluster ([H][d][hd] layout)
-  const T* Wo = (const T*)w.out + (size_t)h * d * hd;
-  split(d, cp.rank, cp.size, lo, hi);
-  float* P = a.pout + ((size_t)s * a.heads + h) * d;
-  rows_gemv<T>(Wo, lo, hi, hd, sm.g, [&](int r0, int n) {
-    for (int i = threadIdx.x; i < n; i += kThreads) P[r0 + i] = sm.g.rowsum[i];
-  });
-  tl_mark(a, sm);  // merge + out-projection partial done
+  split(d, (int)cp.rank, (int)cp.size, lo, hi);
+  float* P = a.pout + ((size_t)s * a.heads + h) * d + lo;
+  const RowGeom<T> gh(hd);
+  gemv_rows<T, 1, Cfg>(a, rg, rs, sm, (const T*)w.out + ((size_t)h * d + lo) * hd, hi - lo, gh, sm.g.xs,
+                         [&](int r, const float (&v)[1], int sl) {
+                           if (sl == 0) P[r] = v[0];
+                         });
+  tl_mark<Cfg::kDiag>(a, sm, kTlOutProj);
 }
 
-// x' = cast(x + cast(sum_h P[h])) from sm.xres into sm.x2res.
-template <typename T>
-__device__ void residual_from_heads(const StepArgs& a, int s, Smem2& sm) {
-  const int d = a.width;
-  const float* P = a.pout + (size_t)s * a.heads * d;
-  for (int i = threadIdx.x; i < d; i += kThreads) {
-    float acc = 0.f;
-    for (int h = 0; h < a.heads; ++h) acc += ld_cg(P + (size_t)h * d + i);
-    sm.x2res[i] = Storage<T>::round(sm.xres[i] + Storage<T>::round(acc));
-  }
-  __syncthreads();
-}
-
-// x = cast(x' + cast(sum_c D[c])) from sm.x2res into sm.xres.
-template <typename T>
-__device__ void residual_from_clusters(const StepArgs& a, int s, int nclusters, Smem2& sm) {
-  const int d = a.width;
-  const float* D = a.dpart + (size_t)s * nclusters * d;
-  for (int i = threadIdx.x; i < d; i += kThreads) {
-    float acc = 0.f;
-    for (int c = 0; c < nclusters; ++c) acc += ld_cg(D + (size_t)c * d + i);
-    sm.xres[i] = Storage<T>::round(sm.x2res[i] + Storage<T>::round(acc));
-  }
-  __syncthreads();
-}
-
-// FFN block for stream s: needs sm.x2res (x'); leaves D[cluster] in global memory.
-template <typename T>
-__device__ void block_ffn(const StepArgs& a, int l, int s, const ClusterPos& cp, Smem2& sm) {
+// FFN block for stream s: needs sm.x2res (x', written with the norm's thread
+// mapping); leaves D[cluster] in global memory.
+template <typename T, class Cfg>
+__device__ void block_ffn(const StepArgs& a, int l, int s, const ClusterPos& cp, Smem2& sm, Ring& rg, RingSmem& rs) {
   const int d = a.width, F = a.ffn;
   const LayerPtrs& w = a.layer[l];
-  norm_smem<T>(sm.x2res, (const T*)w.norm2, d, a.epsilon, sm);
-  tl_mark(a, sm);  // norm2 done
+  norm_block<T, Cfg>(a, rg, rs, sm, sm.x2res, (const T*)w.norm2, sm.z);
+  tl_mark<Cfg::kDiag>(a, sm, kTlNorm2);
   const int G = (int)(cp.count * cp.size), gi = (int)(cp.id * cp.size + cp.rank);
   int lo, hi;
   split(F, gi, G, lo, hi);
-  float* act_trace = a.trace_act ? a.trace_act + (size_t)s * F : nullptr;
-  rows_gemv<T>((const T*)w.gateup, 2 * lo, 2 * hi, d, sm.g, [&](int r0, int n) {
-    for (int p = threadIdx.x; p < n / 2; p += kThreads) {
-      const float g = Storage<T>::round(sm.g.rowsum[2 * p]);
-      const float u = Storage<T>::round(sm.g.rowsum[2 * p + 1]);
-      const int f = (r0 >> 1) + p;
-      const float v = Storage<T>::round((g / (1.0f + expf(-g))) * u);
-      sm.act[f - lo] = v;
-      if (act_trace) act_trace[f] = v;
-    }
-  });
-  tl_mark(a, sm);  // gate/up + SwiGLU done
+  float* act_trace = Cfg::kDiag && a.trace_act ? a.trace_act + (size_t)s * F : nullptr;
+  const RowGeom<T> gd(d);
+  gemv_rows<T, 2, Cfg>(a, rg, rs, sm, (const T*)w.gateup + 2 * (size_t)lo * d, 2 * (hi - lo), gd, sm.z,
+                         [&](int r, const float (&v)[2], int sl) {
+                           if (sl != 0) return;
+                           const float gt = Storage<T>::round(v[0]);
+                           const float up = Storage<T>::round(v[1]);
+                           const int f = lo + (r >> 1);
+                           const float x = Storage<T>::round((gt / (1.0f + expf(-gt))) * up);
+                           sm.u.ff.act[f - lo] = x;
+                           if (Cfg::kDiag && act_trace) act_trace[f] = x;
+                         });
+  __syncthreads();
+  ring_poll<Cfg>(rg, rs);
+  tl_mark<Cfg::kDiag>(a, sm, kTlGateUp);
   // partial[row] = sum_{f in slice} W_down^T[f][row] act[f]. With d < kThreads
   // the CTA splits into `groups` thread groups over rows, group g taking
-  // f = lo+g, lo+g+groups, ...; loads are issued 8 at a time before use.
-  const T* WdT = (const T*)w.down;  // [F][d]
+  // f = lo+g, lo+g+groups, ...; each thread accumulates f in ascending order.
+  constexpr int kCols = kMaxWidth / kThreads;  // columns per thread at most
   const int groups = d >= kThreads ? 1 : kThreads / d;
-  const int seg = (d + (int)cp.size - 1) / (int)cp.size;
-  float* part = sm.gpart;  // [groups][d], groups * d <= max(kThreads, d)
-  {
-    const int g = d >= kThreads ? 0 : (int)threadIdx.x / d;
-    if (g < groups) {
-      for (int row = (d >= kThreads ? (int)threadIdx.x : (int)threadIdx.x - g * d); row < d; row += (d >= kThreads ? kThreads : d)) {
-        float acc = 0.f;
-        for (int f0 = lo + g; f0 < hi; f0 += 8 * groups) {
-          float wv[8];
+  const int tpg = d >= kThreads ? kThreads : d;  // threads per group
+  const int g = (int)threadIdx.x / tpg, c0 = (int)threadIdx.x - g * tpg;
+  const bool active = g < groups;
+  float acc[kCols];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int f = f0 + u * groups;
-            wv[u] = f < hi ? Storage<T>::load(WdT, (size_t)f * d + row) : 0.f;
-          }
+  for (int k = 0; k < kCols; ++k) acc[k] = 0.f;
+  auto rows_from = [&](const T* rows, int f_begin, int f_end) {
+    // `rows` holds W_down^T rows f_begin .. f_end-1 (row stride d)
+    if (!active) return;
+    int f = f_begin + ((g - (f_begin - lo)) % groups + groups) % groups;
+    for (; f < f_end; f += groups) {
+      const float av = sm.u.ff.act[f - lo];
+      const T* wrow = rows + (size_t)(f - f_begin) * d;
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int f = f0 + u * groups;
-            if (f < hi) acc = fmaf(wv[u], sm.act[f - lo], acc);
-          }
-        }
-        part[g * d + row] = acc;
+      for (int k = 0; k < kCols; ++k) {
+        const int c = c0 + k * tpg;
+        if (c < d && (k == 0 || tpg == kThreads)) acc[k] = fmaf(Storage<T>::load(wrow, c), av, acc[k]);
       }
     }
+  };
+  if constexpr (Cfg::kRing) {
+    const int rpc = rows_per_chunk(d * (int)sizeof(T), 1);
+    for (int f0 = lo; f0 < hi; f0 += rpc) {
+      const int n = min(rpc, hi - f0);
+      const T* p = (const T*)ring_acquire(a, rg, rs);
+      tl_mark<Cfg::kDiag>(a, sm, kTlRingWait);
+      rows_from(p, f0, f0 + n);
+      ring_release(rg, rs);
+    }
+  } else {
+    rows_from((const T*)w.down + (size_t)lo * d, lo, hi);  // W_down^T, [F][d]
   }
-  __syncthreads();
+  float* part = sm.gpart;  // [groups][d]
+  if (groups > 1) {
+    if (active) part[g * d + c0] = acc[0];
+    __syncthreads();
+  }
   // sum groups in order, then reduce-scatter to the owning rank of each row segment
-  for (int row = threadIdx.x; row < d; row += kThreads) {
-    float acc = 0.f;
-    for (int gg = 0; gg < groups; ++gg) acc += part[gg * d + row];
+  const int seg = (d + (int)cp.size - 1) / (int)cp.size;
+#pragma unroll
+  for (int k = 0; k < kCols; ++k) {
+    const int row = (int)threadIdx.x + k * kThreads;
+    if (row >= d) continue;
+    float v = acc[k];
+    if (groups > 1) {
+      v = 0.f;
+      for (int gg = 0; gg < groups; ++gg) v += part[gg * d + row];
+    }
     const unsigned owner = (unsigned)(row / seg);
-    dsmem_store(&sm.dred[cp.rank * seg + (row - (int)owner * seg)], owner, acc);
+    dsmem_store(&sm.u.ff.dred[cp.rank * seg + (row - (int)owner * seg)], owner, v);
   }
-  tl_mark(a, sm);  // down partial done
+  tl_mark<Cfg::kDiag>(a, sm, kTlDownPartial);
   cluster_sync();
+  ring_poll<Cfg>(rg, rs);
   const int r_lo = (int)cp.rank * seg, r_hi = min(d, r_lo + seg);
   float* D = a.dpart + ((size_t)s * cp.count + cp.id) * d;
   for (int row = r_lo + threadIdx.x; row < r_hi; row += kThreads) {
-    float acc = 0.f;
-    for (unsigned k = 0; k < cp.size; ++k) acc += sm.dred[k * seg + (row - r_lo)];
-    D[row] = acc;
+    float v = 0.f;
+    for (unsigned k = 0; k < cp.size; ++k) v += sm.u.ff.dred[k * seg + (row - r_lo)];
+    D[row] = v;
   }
-  __syncthreads();
-  tl_mark(a, sm);  // cluster reduce done
+  tl_mark<Cfg::kDiag>(a, sm, kTlClusterReduce);
 }
 
 // Final RMSNorm + score head (no cast) for stream s from sm.xres; CTA 0 only.
 template <typename T>
 __device__ void block_score(const StepArgs& a, int s, Smem2& sm) {
-  norm_smem<T>(sm.xres, (const T*)a.final_norm, a.width, a.epsilon, sm);
+  norm_vec<T>(sm.xres, (const T*)a.final_norm, a.width, a.epsilon, sm, sm.g.xs);
   float acc = 0.f;
   for (int i = threadIdx.x; i < a.width; i += kThreads)
     acc = fmaf(Storage<T>::load((const T*)a.score_w, i), sm.g.xs[i], acc);
@@ -491,6 +850,8 @@ __device__ void block_score(const StepArgs& a, int s, Smem2& sm) {
   __syncthreads();
 }
 
+// hidden[s][l] and the residual buffer a.x from x (thread i writes element i,
+// i + kThreads, ...).
 __device__ __forceinline__ void write_hidden(const StepArgs& a, int s, int l, const float* x) {
   float* hidden = a.hidden + ((size_t)s * a.layers + l) * a.width;
   float* xg = a.x + (size_t)s * a.width;
@@ -500,31 +861,36 @@ __device__ __forceinline__ void write_hidden(const StepArgs& a, int s, int l, co
   }
 }
 
-// Whole step inside one cooperative cluster launch; `input` is [S][features].
-// Every CTA keeps x and x' in shared memory. Streams run one after another.
-template <typename T>
-__device__ bool forward2(const StepArgs& a, const float* input, ClusterGridSync& gs, Smem2& sm) {
+// Whole step inside one cluster launch; `input` is [S][features]. Every CTA
+// keeps x and x' in shared memory; streams run one after another.
+template <typename T, class Cfg>
+__device__ bool forward2(const StepArgs& a, const float* input, ClusterGridSync& gs, Smem2& sm, Ring& rg,
+                         RingSmem& rs) {
   const ClusterPos cp = ClusterPos::get();
   for (int s = 0; s < a.streams; ++s) {
-    tl_mark(a, sm);  // step start
-    block_input<T>(a, s, input, sm.xres, sm);
-    tl_mark(a, sm);  // input projection done
+    // CTA 0 may still read its x for the previous stream's score while the
+    // next input projection writes x through DSMEM.
+    if (s > 0) cluster_sync();
+    tl_mark<Cfg::kDiag>(a, sm, kTlStepStart);
+    load_position(a, s, sm);
+    step_input<T, Cfg>(a, s, input, cp, sm, rg, rs);
+    tl_mark<Cfg::kDiag>(a, sm, kTlInput);
     for (int l = 0; l < a.layers; ++l) {
-      for (int h = (int)cp.id; h < a.heads; h += (int)cp.count) {
-        norm_smem<T>(sm.xres, (const T*)a.layer[l].norm1, a.width, a.epsilon, sm);
-        tl_mark(a, sm);  // norm1 done
-        attention_head<T>(a, l, s, h, cp, sm);
-        if (h + (int)cp.count < a.heads) cluster_sync();
+      if ((int)cp.id < a.heads) {
+        norm_block<T, Cfg>(a, rg, rs, sm, sm.xres, (const T*)a.layer[l].norm1, sm.z);
+        tl_mark<Cfg::kDiag>(a, sm, kTlNorm1);
+        for (int h = (int)cp.id; h < a.heads; h += (int)cp.count) {
+          attention_head<T, Cfg>(a, l, s, h, cp, sm, rg, rs);
+          if (h + (int)cp.count < a.heads) cluster_sync();
+        }
       }
-      if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok)) return false;
-      tl_mark(a, sm);  // grid sync A done
+      if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok, Cfg::kDiag ? &sm : nullptr, Cfg::kRing ? &rg : nullptr, &rs)) return false;
       residual_from_heads<T>(a, s, sm);
-      tl_mark(a, sm);  // x' done
-      block_ffn<T>(a, l, s, cp, sm);
-      if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok)) return false;
-      tl_mark(a, sm);  // grid sync B done
+      tl_mark<Cfg::kDiag>(a, sm, kTlResidualHeads);
+      block_ffn<T, Cfg>(a, l, s, cp, sm, rg, rs);
+      if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok, Cfg::kDiag ? &sm : nullptr, Cfg::kRing ? &rg : nullptr, &rs)) return false;
       residual_from_clusters<T>(a, s, (int)cp.count, sm);
-      tl_mark(a, sm);  // x done
+      tl_mark<Cfg::kDiag>(a, sm, kTlResidualClusters);
       if (blockIdx.x == 0) write_hidden(a, s, l, sm.xres);
     }
     if (blockIdx.x == 0) block_score<T>(a, s, sm);
@@ -537,12 +903,18 @@ __device__ bool forward2(const StepArgs& a, const float* input, ClusterGridSync&
 __host__ __device__ inline int forward2_barriers(int layers, int streams) { return 2 * layers * streams; }
 
 // ---------------------------------------------------------------- per-op kernels' bodies
+// The per-op kernels also serve st_trace_step, so they carry the trace hooks.
+using OpCfg = StepCfg<false, true>;
+
 // Residual state crosses kernels through a.x (x entering the layer / after it)
-// and a.x2 (x' after attention), written by CTA 0.
+// and a.x2 (x' after attention), written by CTA 0. They run the direct-load
+// block functions, which give the same bits as the ring ones.
 template <typename T>
-__device__ void op_input(const StepArgs& a, Smem2& sm) {
+__device__ void op_input(const StepArgs& a, Smem2& sm, RingSmem& rs) {
+  const ClusterPos cp = ClusterPos::get();
+  Ring off{};
   for (int s = 0; s < a.streams; ++s) {
-    block_input<T>(a, s, a.input, sm.xres, sm);
+    step_input<T, OpCfg>(a, s, a.input, cp, sm, off, rs);
     if (blockIdx.x == 0) {
       float* xg = a.x + (size_t)s * a.width;
       for (int i = threadIdx.x; i < a.width; i += kThreads) xg[i] = sm.xres[i];
@@ -554,39 +926,42 @@ __device__ void op_input(const StepArgs& a, Smem2& sm) {
 // Layer l's attention block; for l > 0 it first completes layer l-1's residual
 // from a.x2 and the down partials.
 template <typename T>
-__device__ void op_attention(const StepArgs& a, int l, Smem2& sm) {
+__device__ void op_attention(const StepArgs& a, int l, Smem2& sm, RingSmem& rs) {
   const ClusterPos cp = ClusterPos::get();
+  Ring off{};
   for (int s = 0; s < a.streams; ++s) {
+    load_position(a, s, sm);
     if (l == 0) {
       for (int i = threadIdx.x; i < a.width; i += kThreads) sm.xres[i] = ld_cg(a.x + (size_t)s * a.width + i);
-      __syncthreads();
     } else {
       for (int i = threadIdx.x; i < a.width; i += kThreads) sm.x2res[i] = ld_cg(a.x2 + (size_t)s * a.width + i);
-      __syncthreads();
       residual_from_clusters<T>(a, s, (int)cp.count, sm);
       if (blockIdx.x == 0) write_hidden(a, s, l - 1, sm.xres);
-      __syncthreads();
     }
+    norm_block<T, OpCfg>(a, off, rs, sm, sm.xres, (const T*)a.layer[l].norm1, sm.z);
+    rope_table(a, sm);
+    __syncthreads();
     for (int h = (int)cp.id; h < a.heads; h += (int)cp.count) {
-      norm_smem<T>(sm.xres, (const T*)a.layer[l].norm1, a.width, a.epsilon, sm);
-      attention_head<T>(a, l, s, h, cp, sm);
+      attention_head<T, OpCfg>(a, l, s, h, cp, sm, off, rs);
       if (h + (int)cp.count < a.heads) cluster_sync();
     }
+    cluster_sync();  // sm.t, z and the attention buffers are reused by the next stream
   }
 }
 
 template <typename T>
-__device__ void op_ffn(const StepArgs& a, int l, Smem2& sm) {
+__device__ void op_ffn(const StepArgs& a, int l, Smem2& sm, RingSmem& rs) {
   const ClusterPos cp = ClusterPos::get();
+  Ring off{};
   for (int s = 0; s < a.streams; ++s) {
     for (int i = threadIdx.x; i < a.width; i += kThreads) sm.xres[i] = ld_cg(a.x + (size_t)s * a.width + i);
-    __syncthreads();
     residual_from_heads<T>(a, s, sm);
     if (blockIdx.x == 0) {
       float* x2 = a.x2 + (size_t)s * a.width;
       for (int i = threadIdx.x; i < a.width; i += kThreads) x2[i] = sm.x2res[i];
     }
-    block_ffn<T>(a, l, s, cp, sm);
+    block_ffn<T, OpCfg>(a, l, s, cp, sm, off, rs);
+    cluster_sync();  // the FFN buffers are reused by the next stream
   }
 }
 
@@ -596,10 +971,8 @@ __device__ void op_final(const StepArgs& a, int nclusters, Smem2& sm) {
   if (blockIdx.x != 0) return;
   for (int s = 0; s < a.streams; ++s) {
     for (int i = threadIdx.x; i < a.width; i += kThreads) sm.x2res[i] = ld_cg(a.x2 + (size_t)s * a.width + i);
-    __syncthreads();
     residual_from_clusters<T>(a, s, nclusters, sm);
     write_hidden(a, s, a.layers - 1, sm.xres);
-    __syncthreads();
     block_score<T>(a, s, sm);
   }
   for (int s = threadIdx.x; s < a.streams; s += kThreads) a.position[s] = ld_cg_u64(a.position + s) + 1;

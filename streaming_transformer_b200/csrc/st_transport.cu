@@ -14,6 +14,18 @@
 //                 in tagged 8-byte records (value | epoch), each CTA writing its
 //                 slice and polling every record until its tag matches
 //   cluster-barrier  device time of one hardware cluster barrier, clusters of 8
+//   bulk-stream / load-stream  every CTA (one per SM) streams its own 1 MiB of
+//                 HBM `count` times, either through a 4 x 32 KiB shared-memory
+//                 ring fed by cp.async.bulk (thread 0 issuing, all threads
+//                 waiting on the slot mbarriers) or with 16-byte vector loads;
+//                 reports GB/s and thread 0's cycles inside the issue
+//   icache        cycles per pass over 8-64 KB of straight-line code (512
+//                 threads per SM): instruction fetch cost of the step's code
+//   primitives    SM cycles per call of the step's building blocks, every CTA
+//                 (one per SM) calling each one `count` times back to back:
+//                 __syncthreads, block_sum, gemv_tile on 16 x 512 and 64 x 64
+//                 fp32 tiles read from shared or global memory, and the step's
+//                 warp-per-row GEMV (warp_rows) on the same shared tiles
 // Every device wait is bounded (30 s budget, globaltimer) and every host wait
 // gives up after 60 s.
 #include <cuda_runtime.h>
@@ -31,6 +43,8 @@
 
 #include "../../include/streaming_b200.h"
 #include "st_device.cuh"
+#include "st_ring.cuh"
+#include "st_step.cuh"
 
 using namespace st;
 
@@ -124,6 +138,158 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(kThreads, 1) k_clust
   }
 }
 
+// Streams `bytes_per_cta` from src + blockIdx.x * bytes_per_cta, `rounds` times,
+// through kStreamSlots fixed slots of kStreamSlotBytes.
+constexpr int kStreamSlots = 4;
+constexpr int kStreamSlotBytes = 32 * 1024;
+struct alignas(128) StreamRing {
+  unsigned char slot[kStreamSlots][kStreamSlotBytes];
+  unsigned long long full[kStreamSlots];
+};
+
+__global__ void __launch_bounds__(kThreads, 1) k_bulk_stream(const char* src, size_t bytes_per_cta, int rounds,
+                                                             unsigned long long* issue_cycles, float* sink) {
+  extern __shared__ __align__(128) unsigned char raw[];
+  StreamRing& rs = *reinterpret_cast<StreamRing*>(raw);
+  const char* base = src + (size_t)blockIdx.x * bytes_per_cta;
+  const unsigned long long total = (unsigned long long)rounds * (bytes_per_cta / kStreamSlotBytes);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStreamSlots; ++i) mbar_init(&rs.full[i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  unsigned long long issued = 0, spent = 0;
+  const size_t chunks = bytes_per_cta / kStreamSlotBytes;
+  auto issue = [&]() {
+    const int slot = (int)(issued % kStreamSlots);
+    const long long c0 = clock64();
+    mbar_expect_tx(&rs.full[slot], kStreamSlotBytes);
+    bulk_copy(rs.slot[slot], base + (issued % chunks) * kStreamSlotBytes, kStreamSlotBytes, &rs.full[slot]);
+    spent += (unsigned long long)(clock64() - c0);
+    ++issued;
+  };
+  if (threadIdx.x == 0)
+    while (issued < total && issued < kStreamSlots) issue();
+  float acc = 0.f;
+  for (unsigned long long c = 0; c < total; ++c) {
+    const int slot = (int)(c % kStreamSlots);
+    const unsigned parity = (unsigned)((c / kStreamSlots) & 1ull);
+    const unsigned long long t0 = globaltimer();
+    while (!mbar_try_wait(&rs.full[slot], parity))
+      if (globaltimer() - t0 > 2000000000ull) break;
+    const float4* p = reinterpret_cast<const float4*>(rs.slot[slot]);
+    for (int i = threadIdx.x; i < kStreamSlotBytes / 16; i += kThreads) {
+      const float4 v = p[i];
+      acc += v.x + v.y + v.z + v.w;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && issued < total) issue();
+  }
+  if (threadIdx.x == 0) issue_cycles[blockIdx.x] = spent / (issued ? issued : 1);
+  if (acc == 12345.f) sink[blockIdx.x] = acc;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) k_load_stream(const char* src, size_t bytes_per_cta, int rounds, float* sink) {
+  const uint4* base = reinterpret_cast<const uint4*>(src + (size_t)blockIdx.x * bytes_per_cta);
+  const size_t n = bytes_per_cta / 16;
+  float acc = 0.f;
+  for (int r = 0; r < rounds; ++r) {
+    for (size_t i = threadIdx.x; i < n; i += (size_t)kThreads * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const size_t j = i + (size_t)u * kThreads;
+        v[u] = j < n ? ld_stream(base + j) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc += __uint_as_float(v[u].x);
+    }
+  }
+  if (acc == 12345.f) sink[blockIdx.x] = acc;
+}
+
+// Straight-line code of N independent-chain FMAs per warp (asm, so none is
+// folded), looped `reps` times: cycles per pass against the code size show
+// the instruction cache capacity the step kernels must fit in.
+template <int N>
+__device__ __forceinline__ void fma_block(float& a, float& b, float& c, float& d) {
+#pragma unroll
+  for (int i = 0; i < N; i += 4) {
+    asm volatile("fma.rn.f32 %0, %0, 0f3F800054, 0f3F000000;" : "+f"(a));
+    asm volatile("fma.rn.f32 %0, %0, 0f3F800054, 0f3F000000;" : "+f"(b));
+    asm volatile("fma.rn.f32 %0, %0, 0f3F800054, 0f3F000000;" : "+f"(c));
+    asm volatile("fma.rn.f32 %0, %0, 0f3F800054, 0f3F000000;" : "+f"(d));
+  }
+}
+
+template <int N>
+__global__ void __launch_bounds__(kThreads, 1) k_icache(int reps, unsigned long long* out, float* sink) {
+  float a = threadIdx.x, b = a + 1.f, c = a + 2.f, d = a + 3.f;
+  __syncthreads();
+  const long long c0 = clock64();
+  for (int r = 0; r < reps; ++r) fma_block<N>(a, b, c, d);
+  __syncthreads();
+  const long long c1 = clock64();
+  if (threadIdx.x == 0) out[blockIdx.x] = (unsigned long long)((c1 - c0) / reps);
+  if (a + b + c + d == 12345.f) sink[threadIdx.x] = a;
+}
+
+constexpr int kPrimitives = 10;
+
+__global__ void __launch_bounds__(kThreads, 1) k_primitives(const float* wglobal, int reps, unsigned long long* out) {
+  extern __shared__ __align__(128) unsigned char raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(raw);
+  float* tile = reinterpret_cast<float*>(raw + ((sizeof(Smem) + 127) / 128) * 128);
+  for (int i = threadIdx.x; i < 16 * 512; i += kThreads) tile[i] = wglobal[i];
+  for (int i = threadIdx.x; i < kMaxCols; i += kThreads) sm.xs[i] = 0.001f * (float)i;
+  __syncthreads();
+  float sink = 0.f;
+  for (int prim = 0; prim < kPrimitives; ++prim) {
+    __syncthreads();
+    const long long c0 = clock64();
+    for (int r = 0; r < reps; ++r) {
+      switch (prim) {
+        case 0: __syncthreads(); break;
+        case 1: sink += block_sum((float)threadIdx.x, sm); __syncthreads(); break;
+        case 2: gemv_tile<float, true>(tile, 0, 16, 512, sm); sink += sm.rowsum[threadIdx.x & 15]; break;
+        case 3: gemv_tile<float, false>(wglobal, 0, 16, 512, sm); sink += sm.rowsum[threadIdx.x & 15]; break;
+        case 4: gemv_tile<float, true>(tile, 0, 64, 64, sm); sink += sm.rowsum[threadIdx.x & 63]; break;
+        case 5: gemv_tile<float, false>(wglobal, 0, 64, 64, sm); sink += sm.rowsum[threadIdx.x & 63]; break;
+        case 6:
+          warp_rows<float, 2, true>(tile, 16, RowGeom<float>(512), sm.xs, [&](int row, const float (&v)[2], int sl) {
+            if (sl == 0) { sm.rowsum[row] = v[0]; sm.rowsum[row + 1] = v[1]; }
+          });
+          __syncthreads();
+          sink += sm.rowsum[threadIdx.x & 15];
+          break;
+        case 7:
+          warp_rows<float, 2, true>(tile, 16, RowGeom<float>(512), sm.xs, [&](int row, const float (&v)[2], int sl) {
+            if (sl == 0) sink += v[0] + v[1];
+          });
+          break;
+        case 9:
+          warp_rows<float, 2, false>(wglobal, 16, RowGeom<float>(512), sm.xs, [&](int row, const float (&v)[2], int sl) {
+            if (sl == 0) { sm.rowsum[row] = v[0]; sm.rowsum[row + 1] = v[1]; }
+          });
+          __syncthreads();
+          sink += sm.rowsum[threadIdx.x & 15];
+          break;
+        default:
+          warp_rows<float, 1, true>(tile, 64, RowGeom<float>(64), sm.xs, [&](int row, const float (&v)[1], int sl) {
+            if (sl == 0) sm.rowsum[row] = v[0];
+          });
+          __syncthreads();
+          sink += sm.rowsum[threadIdx.x & 63];
+          break;
+      }
+    }
+    __syncthreads();
+    const long long c1 = clock64();
+    if (threadIdx.x == 0) out[(size_t)prim * gridDim.x + blockIdx.x] = (unsigned long long)((c1 - c0) / reps);
+  }
+  if (sink == 12345.f) out[0] = 0;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) k_barriers(StepArgs a, unsigned long long count, unsigned long long base) {
   GridSync gs{base, 0};
   for (unsigned long long i = 0; i < count; ++i)
@@ -184,7 +350,8 @@ struct Resources {
 int run_bench(int device, const std::string& mode, size_t count, int backoff, const char* csv_path, std::string* json) {
   const bool interactive = mode == "ping-pong" || mode == "gpu-ping";
   if (mode != "empty" && mode != "empty-graph" && mode != "copy" && !interactive && mode != "grid-barrier" &&
-      mode != "ll-exchange" && mode != "cluster-barrier") {
+      mode != "ll-exchange" && mode != "cluster-barrier" && mode != "bulk-stream" && mode != "load-stream" &&
+      mode != "primitives" && mode != "icache") {
     g_transport_error = "Unknown transport mode " + mode;
     return ST_ERR_INVALID;
   }
@@ -207,6 +374,111 @@ int run_bench(int device, const std::string& mode, size_t count, int backoff, co
   TB_CUDA(cudaEventCreate(&r.e1));
   std::ostringstream o;
   o.precision(9);
+  if (mode == "icache") {
+    const int grid = prop.multiProcessorCount;
+    unsigned long long* out = nullptr;
+    float* sink = nullptr;
+    TB_CUDA(cudaMalloc(&out, grid * sizeof(unsigned long long)));
+    TB_CUDA(cudaMalloc(&sink, kThreads * sizeof(float)));
+    const int reps = (int)std::min<size_t>(std::max<size_t>(count, 1), 10000);
+    o << "{\"mode\":\"icache\",\"ctas\":" << grid << ",\"threads\":" << kThreads << ",\"reps\":" << reps
+      << ",\"cycles_per_pass\":{";
+    auto run = [&](auto kernel, int n, bool first) -> int {
+      kernel<<<grid, kThreads, 0, r.stream>>>(reps, out, sink);
+      if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(r.stream) != cudaSuccess) return -1;
+      std::vector<unsigned long long> v(grid);
+      if (cudaMemcpy(v.data(), out, grid * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+      std::sort(v.begin(), v.end());
+      o << (first ? "" : ",") << "\"" << n * 16 / 1024 << "KB\":" << v[grid / 2];
+      return 0;
+    };
+    int bad = 0;
+    bad |= run(k_icache<512>, 512, true);
+    bad |= run(k_icache<1024>, 1024, false);
+    bad |= run(k_icache<2048>, 2048, false);
+    bad |= run(k_icache<4096>, 4096, false);
+    cudaFree(out);
+    cudaFree(sink);
+    if (bad) {
+      g_transport_error = "icache kernel failed";
+      return ST_ERR_CUDA;
+    }
+    o << "}}";
+    *json = o.str();
+    return ST_OK;
+  }
+  if (mode == "primitives") {
+    const int grid = prop.multiProcessorCount;
+    float* w = nullptr;
+    unsigned long long* out = nullptr;
+    TB_CUDA(cudaMalloc(&w, 16 * 512 * sizeof(float)));
+    TB_CUDA(cudaMalloc(&out, (size_t)kPrimitives * grid * sizeof(unsigned long long)));
+    TB_CUDA(cudaMemsetAsync(w, 0, 16 * 512 * sizeof(float), r.stream));
+    const size_t smem = ((sizeof(Smem) + 127) / 128) * 128 + 16 * 512 * sizeof(float);
+    TB_CUDA(cudaFuncSetAttribute(k_primitives, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const int reps = (int)std::min<size_t>(std::max<size_t>(count, 1), 100000);
+    k_primitives<<<grid, kThreads, smem, r.stream>>>(w, reps, out);
+    TB_CUDA(cudaGetLastError());
+    TB_CUDA(cudaStreamSynchronize(r.stream));
+    std::vector<unsigned long long> v((size_t)kPrimitives * grid);
+    TB_CUDA(cudaMemcpy(v.data(), out, v.size() * 8, cudaMemcpyDeviceToHost));
+    cudaFree(w);
+    cudaFree(out);
+    static const char* names[kPrimitives] = {"syncthreads", "block_sum", "gemv_smem_16x512", "gemv_global_16x512",
+                                             "gemv_smem_64x64", "gemv_global_64x64", "warp_rows_pairs_16x512",
+                                             "warp_rows_pairs_16x512_no_barrier", "warp_rows_64x64",
+                                             "warp_rows_pairs_16x512_global"};
+    o << "{\"mode\":\"primitives\",\"ctas\":" << grid << ",\"threads\":" << kThreads << ",\"reps\":" << reps
+      << ",\"cycles_median\":{";
+    for (int p = 0; p < kPrimitives; ++p) {
+      std::vector<unsigned long long> s(v.begin() + (size_t)p * grid, v.begin() + (size_t)(p + 1) * grid);
+      std::sort(s.begin(), s.end());
+      o << (p ? "," : "") << "\"" << names[p] << "\":" << s[grid / 2];
+    }
+    o << "}}";
+    *json = o.str();
+    return ST_OK;
+  }
+  if (mode == "bulk-stream" || mode == "load-stream") {
+    const int grid = prop.multiProcessorCount;
+    const size_t per = 1u << 20;
+    char* src = nullptr;
+    unsigned long long* cyc = nullptr;
+    float* sink = nullptr;
+    TB_CUDA(cudaMalloc(&src, per * grid));
+    TB_CUDA(cudaMalloc(&cyc, grid * sizeof(unsigned long long)));
+    TB_CUDA(cudaMalloc(&sink, grid * sizeof(float)));
+    TB_CUDA(cudaMemsetAsync(src, 1, per * grid, r.stream));
+    const int rounds = (int)std::min<size_t>(count, 1000);
+    const size_t smem = sizeof(StreamRing);
+    if (mode == "bulk-stream")
+      TB_CUDA(cudaFuncSetAttribute(k_bulk_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    auto launch = [&](int rr) {
+      if (mode == "bulk-stream") k_bulk_stream<<<grid, kThreads, smem, r.stream>>>(src, per, rr, cyc, sink);
+      else k_load_stream<<<grid, kThreads, 0, r.stream>>>(src, per, rr, sink);
+    };
+    launch(1);
+    TB_CUDA(cudaGetLastError());
+    TB_CUDA(cudaEventRecord(r.e0, r.stream));
+    launch(rounds);
+    TB_CUDA(cudaEventRecord(r.e1, r.stream));
+    TB_CUDA(cudaEventSynchronize(r.e1));
+    TB_CUDA(cudaGetLastError());
+    float ms = 0;
+    TB_CUDA(cudaEventElapsedTime(&ms, r.e0, r.e1));
+    std::vector<unsigned long long> cycles(grid, 0);
+    if (mode == "bulk-stream") TB_CUDA(cudaMemcpy(cycles.data(), cyc, grid * 8, cudaMemcpyDeviceToHost));
+    cudaFree(src);
+    cudaFree(cyc);
+    cudaFree(sink);
+    std::sort(cycles.begin(), cycles.end());
+    const double bytes = (double)per * grid * rounds;
+    o << "{\"mode\":\"" << mode << "\",\"ctas\":" << grid << ",\"mib_per_cta\":1,\"rounds\":" << rounds
+      << ",\"gb_per_s\":" << bytes / (ms * 1e-3) / 1e9 << ",\"issue_cycles_median\":" << cycles[grid / 2]
+      << ",\"issue_cycles_max\":" << cycles[grid - 1] << "}";
+    *json = o.str();
+    return ST_OK;
+  }
   if (mode == "ll-exchange" || mode == "cluster-barrier") {
     const int grid = mode == "ll-exchange" ? prop.multiProcessorCount : prop.multiProcessorCount / 8 * 8;
     float ms = 0;

@@ -49,37 +49,43 @@ def main() -> None:
         print(json.dumps(out))
 
 
-LAYER_MARKS = ["norm1", "qkv_rows", "qkv_shared", "attention", "partials_shared", "out_partial",
-               "grid_sync_A", "residual_heads", "norm2", "gate_up", "down_partial", "cluster_reduce",
-               "grid_sync_B", "residual_clusters"]
+# Tags of the device marks (TimelineTag in csrc/st_step.cuh); each mark is
+# clock64() << 8 | tag and charges the interval since the previous mark to its tag.
+TAGS = {1: "step_start", 2: "input", 3: "norm1", 4: "ring_wait", 5: "warp_gemv", 6: "qkv_rows", 7: "qkv_shared",
+        8: "kv_wait", 9: "merge_heads", 10: "logits_pv", 11: "cta_merge_broadcast", 12: "partials_shared",
+        13: "out_rows", 14: "sync_cluster_arrive", 15: "sync_grid_wait", 16: "residual_heads", 17: "norm2",
+        18: "gate_up_rows", 19: "down_partial", 20: "cluster_reduce", 21: "residual_clusters", 22: "step_end",
+        23: "ring_release_fill"}
 
 
 def timeline_breakdown(rt, events, config, us_per_step):
-    """Median duration of each phase (time since the previous mark) over the
-    steps, scaled so one step sums to the measured device time per step."""
+    """Per-step total of each tag's intervals (median over steps), scaled so one
+    step sums to the measured device time per step."""
     import numpy as np
-    marks = rt.device_timeline(events).astype(np.int64)
-    per_step = 2 + len(LAYER_MARKS) * config.layers
-    steps = len(marks) // per_step
-    names = ["step_start", "input"] + [f"{n}" for _ in range(config.layers) for n in LAYER_MARKS]
-    durations = {}
-    cycles_per_step = []
-    for s in range(steps):
-        m = marks[s * per_step:(s + 1) * per_step]
-        nxt = marks[(s + 1) * per_step] if (s + 1) * per_step < len(marks) else None
-        if nxt is not None:
-            cycles_per_step.append(nxt - m[0])
-        for i in range(1, per_step):
-            durations.setdefault(names[i], []).append(m[i] - m[i - 1])
-    scale = us_per_step / float(np.median(cycles_per_step)) if cycles_per_step else 1.0 / 1965.0
-    summary = {}
-    for name, vals in durations.items():
-        v = np.asarray(vals, dtype=np.float64)
-        per_layer = name in LAYER_MARKS
-        # layer marks appear config.layers times per step: report the per-step total
-        summary[name] = round(float(np.median(v.reshape(steps, -1).sum(1) if per_layer else v)) * scale, 3)
-    summary["other (end of step)"] = round(us_per_step - sum(summary.values()), 3)
-    return summary
+    raw = rt.device_timeline(events).astype(np.int64)
+    raw = raw[(raw & 0xFF) != 24]  # chunk issue times are not phase boundaries
+    tags = raw & 0xFF
+    clocks = raw >> 8
+    starts = np.flatnonzero(tags == 1)
+    per_step = []
+    for i in range(len(starts) - 1):
+        seg = slice(starts[i], starts[i + 1] + 1)
+        c, t = clocks[seg], tags[seg]
+        totals = {}
+        for k in range(1, len(c)):
+            name = TAGS.get(int(t[k]), f"tag{int(t[k])}")
+            if k == len(c) - 1:
+                name = "end_of_step"
+            totals[name] = totals.get(name, 0) + int(c[k] - c[k - 1])
+        per_step.append((int(c[-1] - c[0]), totals))
+    if not per_step:
+        return {}
+    cycles = float(np.median([p[0] for p in per_step]))
+    scale = us_per_step / cycles
+    names = sorted({n for _, t in per_step for n in t}, key=lambda n: -np.median([t.get(n, 0) for _, t in per_step]))
+    out = {n: round(float(np.median([t.get(n, 0) for _, t in per_step])) * scale, 3) for n in names}
+    out["implied_sm_mhz"] = round(cycles / us_per_step, 1)
+    return out
 
 
 if __name__ == "__main__":
