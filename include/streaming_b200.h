@@ -156,11 +156,16 @@ int st_device_trace(st_runtime* rt, const float* inputs, size_t count, float* sc
                     double* us_per_step);
 
 /* Diagnostic device timeline: like st_device_trace (FUSED/PERSISTENT device
- * loop), with CTA 0 recording clock64() at every phase boundary of every step
- * into marks[0..capacity); *used receives the number written. New; the
- * reference exposes no intra-step timing. */
+ * loop), with every warp of CTA 0 recording clock64() << 8 | tag at every phase
+ * boundary of every step; warp w (of 16) fills marks[w * capacity / 16 ..
+ * (w + 1) * capacity / 16) and unused entries stay 0. *used receives the number
+ * warp 0 wrote. New; the reference exposes no intra-step timing. */
 int st_device_timeline(st_runtime* rt, const float* inputs, size_t count, long long* marks, size_t capacity,
                        size_t* used);
+
+/* Same, recorded by CTA `cta` of the grid (0 <= cta < blocks in st_info). */
+int st_device_timeline_cta(st_runtime* rt, const float* inputs, size_t count, int cta, long long* marks,
+                           size_t capacity, size_t* used);
 
 /* Same, but `inputs` is a device pointer already resident in HBM and no score is
  * copied back; *kernel_launches receives the number of kernels launched. */

@@ -81,8 +81,10 @@ struct StepArgs {
   float* trace_attention;             // [S][d] merged attention, diagnostics only (null in timed paths)
   float* trace_qkv;                   // [S][3][d] rotated q, k and v, diagnostics only
   float* trace_act;                   // [S][F] SwiGLU output, diagnostics only
-  long long* timeline;                // CTA 0 clock64() at phase boundaries, diagnostics only
+  long long* timeline;                // clock64() of one CTA at phase boundaries, diagnostics only
   int timeline_capacity;
+  int timeline_cta;                   // the CTA that records the timeline
+  int l2_keep_layers;                 // layers whose weights are kept L2-resident (weight ring)
   int cluster_size;                   // CTAs per cluster the buffers were sized for
   int clusters;                       // clusters in the grid (sizes dpart)
 };

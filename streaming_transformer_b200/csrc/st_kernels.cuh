@@ -113,25 +113,28 @@ __global__ void __launch_bounds__(kThreads, 1) k2_fused(StepArgs a, unsigned lon
 }
 
 // Steps `count` preloaded events ([count][S][features], device memory) in one
-// launch; the kDiag variant also records the phase timeline. scores ([count][S]) may be null. The extra grid sync per event orders
-// CTA 0's position update before the next event reads the position.
+// launch; the kDiag variant also records the phase timeline. scores
+// ([count][S]) may be null.
 template <typename T, bool kRing, bool kDiag>
 __global__ void __launch_bounds__(kThreads, 1) k2_trace(StepArgs a, const float* inputs, unsigned long long count,
                                                        float* scores, unsigned long long base) {
   ST_SMEM2;
   if (!cluster_shape_ok(a)) return;
   ClusterGridSync gs{base, 0};
-  if (threadIdx.x == 0) sm.tl_n = 0;
+  if (threadIdx.x < kWarps) sm.tl_nw[threadIdx.x] = 0;
   __syncthreads();
   Ring rg;
   if (!ring_setup<T, kRing>(a, rg, rs, ring_buf, count)) return;
   const size_t stride = (size_t)a.streams * a.features;
-  for (unsigned long long e = 0; e < count; ++e) {
-    if (!forward2<T, StepCfg<kRing, kDiag>>(a, inputs + e * stride, gs, sm, rg, rs)) break;
-    if (scores && blockIdx.x == 0)
-      for (int s = threadIdx.x; s < a.streams; s += kThreads) scores[e * a.streams + s] = a.score[s];
-    if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok, nullptr, kRing ? &rg : nullptr, &rs)) break;
-  }
+  bool ok = true;
+  for (unsigned long long e = 0; e < count && ok; ++e)
+    ok = forward2<T, StepCfg<kRing, kDiag>>(a, inputs + e * stride, gs, sm, rg, rs, e,
+                                            scores ? scores + e * a.streams : nullptr, false);
+  // Every CTA derived its positions from the stored ones plus the event index,
+  // so they are stored once, after the last event (whose reads of them all
+  // precede its grid syncs).
+  if (ok && is_score_cta())
+    for (int s = threadIdx.x; s < a.streams; s += kThreads) a.position[s] = ld_cg_u64(a.position + s) + count;
   ring_drain(a, rg, rs);
 }
 
@@ -221,7 +224,9 @@ __global__ void __launch_bounds__(kThreads, 1) k2_persistent(StepArgs a, Persist
       // No CTA may see the next command before every CTA has read this one.
       if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok)) { ring_drain(a, rg, rs); persistent_exit<T>(a, p); return; }
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
+    // A step's score, hidden state and position come from the score CTA, so it
+    // publishes RUN completions; other commands end with a grid sync.
+    if ((command == kRun ? is_score_cta() : blockIdx.x == 0) && threadIdx.x == 0) {
       __threadfence_system();
       st_release_sys(&p.mailbox->completion, seq);
     }

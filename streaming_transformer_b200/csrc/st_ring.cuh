@@ -22,6 +22,12 @@
 // reclaims the bytes of chunks whose empty phase has completed whenever it
 // issues.
 //
+// Every step reads every weight once, and the fp32 models are about as large
+// as L2, so plain copies would flush L2 each step (code and the K/V cache
+// included). Chunks of the first a.l2_keep_layers layers are copied with an
+// L2 evict_last policy and stay resident from step to step; the rest use
+// evict_first and pass through without displacing them.
+//
 // The issuer is lane 0 of the CTA's last warp (kIssuer). A launch issues at
 // most `limit` chunks (fused and trace kernels: exactly
 // the chunks their steps consume; the resident kernel keeps prefetching the
@@ -67,9 +73,25 @@ __device__ __forceinline__ bool mbar_try_wait_for(unsigned long long* bar, unsig
       : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity), "r"(suspend_ns) : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ void bulk_copy(void* dst_smem, const void* src, unsigned bytes, unsigned long long* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               :: "r"(smem_addr(dst_smem)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
+// Bulk copy global -> this CTA's shared memory with an L2 eviction policy
+// (from createpolicy); completion on `bar`. No multicast.
+__device__ __forceinline__ void bulk_copy(void* dst_smem, const void* src, unsigned bytes, unsigned long long* bar,
+                                          unsigned long long policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      :: "r"(smem_addr(dst_smem)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy) : "memory");
+}
+// L2 policies for weight chunks: layers that should stay resident across
+// steps, and the rest, streamed once per step without displacing them.
+__device__ __forceinline__ unsigned long long policy_evict_last() {
+  unsigned long long p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ unsigned long long policy_evict_first() {
+  unsigned long long p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 __device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
@@ -204,7 +226,7 @@ __host__ __device__ inline bool ring_supported(const StepArgs& a, size_t elem, i
 struct RingChunk {
   const char* src;
   unsigned bytes;
-  unsigned pad;
+  unsigned keep;  // 1: L2 evict_last (the layer stays resident), 0: evict_first
 };
 
 // Per-thread ring state (uniform across the CTA).
@@ -229,7 +251,10 @@ struct alignas(128) RingSmem {
   unsigned long long released;           // chunks whose bytes have been reclaimed
   unsigned long long limit;              // chunks this launch may issue
   unsigned char* buf;                    // the ring bytes (128-byte aligned)
+  unsigned long long keep_policy;        // createpolicy L2::evict_last
+  unsigned long long stream_policy;      // createpolicy L2::evict_first
   unsigned capacity;                     // ring bytes
+  unsigned head_off;                     // head % capacity
   int nchunks;                           // chunks per step in `table`
   int next;                              // table index of the next chunk to issue
   RingChunk table[kMaxRingChunkTable];
@@ -240,17 +265,19 @@ struct alignas(128) RingSmem {
 __device__ inline bool build_chunk_table(const StepArgs& a, const Where& w, size_t elem, RingSmem& rs) {
   int n = 0;
   bool ok = true;
+  unsigned keep = 1u;
   auto add = [&](const Span& s) {
     if (s.rows <= 0) return;
     const int rpc = rows_per_chunk(s.row_bytes, s.unit);
     for (int r = 0; r < s.rows; r += rpc) {
       if (n >= kMaxRingChunkTable) { ok = false; return; }
       const int rows = min(rpc, s.rows - r);
-      rs.table[n++] = RingChunk{s.base + (size_t)r * s.row_bytes, (unsigned)(rows * s.row_bytes), 0u};
+      rs.table[n++] = RingChunk{s.base + (size_t)r * s.row_bytes, (unsigned)(rows * s.row_bytes), keep};
     }
   };
   add(span_of(a, w, kSpanIn, -1, 0, elem));
   for (int l = 0; l < a.layers; ++l) {
+    keep = l < a.l2_keep_layers ? 1u : 0u;
     if (w.id < a.heads) {
       add(span_of(a, w, kSpanNorm1, l, 0, elem));
       for (int h = w.id; h < a.heads; h += w.count) {
@@ -272,17 +299,17 @@ __device__ inline bool build_chunk_table(const StepArgs& a, const Where& w, size
 // arriving on its empty mbarrier (release semantics), and the test below
 // observes that arrival (acquire), so a copy into those bytes cannot race a
 // reader.
-static __device__ __noinline__ void ring_fill_slow(Ring& r, RingSmem& rs) {
+static __device__ __noinline__ void ring_fill_slow(Ring& r, RingSmem& rs, int max_issue) {
   while (rs.released < rs.issued &&
          mbar_test_wait(&rs.empty[rs.released % kRingChunks], (unsigned)((rs.released / kRingChunks) & 1ull))) {
     rs.tail = rs.end[rs.released % kRingChunks];
     rs.released += 1;
   }
-  while (rs.issued < rs.limit && rs.issued < rs.released + kRingChunks) {
+  for (int n = 0; n < max_issue && rs.issued < rs.limit && rs.issued < rs.released + kRingChunks; ++n) {
     const RingChunk c = rs.table[rs.next];
     const unsigned alloc = (c.bytes + 127u) & ~127u;
     unsigned long long pos = rs.head;
-    unsigned off = (unsigned)(pos % rs.capacity);
+    unsigned off = rs.head_off;  // == head % capacity, tracked to avoid a 64-bit modulo
     if (off + alloc > rs.capacity) {  // never split a chunk across the end
       pos += rs.capacity - off;
       off = 0;
@@ -292,18 +319,22 @@ static __device__ __noinline__ void ring_fill_slow(Ring& r, RingSmem& rs) {
     rs.off[slot] = off;
     rs.end[slot] = pos + alloc;
     rs.head = pos + alloc;
+    rs.head_off = off + alloc == rs.capacity ? 0u : off + alloc;
     rs.issued_at[slot] = clock64();
     mbar_expect_tx(&rs.full[slot], c.bytes);
-    bulk_copy(rs.buf + off, c.src, c.bytes, &rs.full[slot]);
+    bulk_copy(rs.buf + off, c.src, c.bytes, &rs.full[slot], c.keep ? rs.keep_policy : rs.stream_policy);
     rs.next = rs.next + 1 == rs.nchunks ? 0 : rs.next + 1;  // the next step repeats the table
     rs.issued += 1;
   }
 }
 
-// Out of line: only the issuer runs it, usually off the critical path.
-__device__ __forceinline__ void ring_fill(Ring& r, RingSmem& rs) {
-  if (threadIdx.x == kIssuer && r.enabled) ring_fill_slow(r, rs);
+// Out of line: only the issuer runs it. `max_issue` bounds the copies issued
+// in one call: one where the issuer's warp has work waiting (a release), all
+// that fit where the CTA is idle anyway (a grid barrier).
+__device__ __forceinline__ void ring_fill(Ring& r, RingSmem& rs, int max_issue = 1) {
+  if (threadIdx.x == kIssuer && r.enabled) ring_fill_slow(r, rs, max_issue);
 }
+constexpr int kFillAll = kRingChunks;
 
 // All threads: set up (mbarriers, chunk table, first issues). `buf` holds
 // `capacity` bytes (a multiple of 128, at least two chunks, so a chunk that
@@ -315,6 +346,9 @@ __device__ inline void ring_begin(const StepArgs& a, Ring& r, RingSmem& rs, unsi
   __shared__ int table_ok;
   if (threadIdx.x == kIssuer) {
     rs.head = rs.tail = rs.issued = rs.released = 0;
+    rs.head_off = 0;
+    rs.keep_policy = policy_evict_last();
+    rs.stream_policy = policy_evict_first();
     rs.limit = limit;
     rs.buf = buf;
     rs.capacity = capacity;
@@ -330,7 +364,7 @@ __device__ inline void ring_begin(const StepArgs& a, Ring& r, RingSmem& rs, unsi
   }
   __syncthreads();
   r.set_enabled(table_ok != 0);
-  ring_fill(r, rs);
+  ring_fill(r, rs, kFillAll);
 }
 
 // Wait (bounded) until the next chunk has landed; returns its bytes. The

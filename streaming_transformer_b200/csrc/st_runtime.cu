@@ -303,7 +303,7 @@ int launch_trace(st_runtime* rt, const StepArgs& a0, const float* inputs, unsign
   void* params[] = {&a, &inputs, &count, &scores, &base};
   ST_TRY(launch_ex(rt, timeline ? ST_TIMELINE_KERNEL(rt) : ST_LOOP_KERNEL(rt, trace), rt->grid, rt->cluster, true,
                    params));
-  rt->bar_base += count * (unsigned long long)(forward_barrier_count(rt) + 1) * rt->nclusters;
+  rt->bar_base += count * (unsigned long long)forward_barrier_count(rt) * rt->nclusters;
   return ST_OK;
 }
 
@@ -764,6 +764,15 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   a.cluster_size = rt->cluster;
   a.clusters = rt->nclusters;
   {
+    // Keep as many whole layers L2-resident as fit in 70% of L2 (the rest holds
+    // the K/V cache, activations and code); ST_L2_KEEP_LAYERS overrides.
+    const size_t dd = (size_t)m.width, ff = (size_t)m.ffn;
+    const size_t per_layer = (2 * dd + 4 * dd * dd + 3 * ff * dd) * rt->elem;
+    int keep = per_layer ? (int)std::min<size_t>(L, (size_t)(0.7 * (double)prop.l2CacheSize) / per_layer) : 0;
+    if (const char* env = std::getenv("ST_L2_KEEP_LAYERS")) keep = std::max(0, std::min(L, std::atoi(env)));
+    a.l2_keep_layers = keep;
+  }
+  {
     const char* env = std::getenv("ST_WEIGHT_RING");
     rt->ring = ring_supported(a, rt->elem, rt->cluster, rt->nclusters) && !(env && env[0] == '0');
   }
@@ -1072,7 +1081,13 @@ int st_device_trace(st_runtime* rt, const float* inputs, size_t count, float* sc
 
 int st_device_timeline(st_runtime* rt, const float* inputs, size_t count, long long* marks, size_t capacity,
                        size_t* used) {
+  return st_device_timeline_cta(rt, inputs, count, 0, marks, capacity, used);
+}
+
+int st_device_timeline_cta(st_runtime* rt, const float* inputs, size_t count, int cta, long long* marks,
+                           size_t capacity, size_t* used) {
   if (!rt || !inputs || !marks || count == 0 || capacity == 0) return ST_ERR_INVALID;
+  if (cta < 0 || cta >= rt->grid) return rt->fail(ST_ERR_INVALID, "timeline CTA %d outside the grid of %d", cta, rt->grid);
   if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
   if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
   if (rt->opt.backend == ST_BACKEND_PERSISTENT) ST_TRY(st_stop(rt));
@@ -1090,14 +1105,16 @@ int st_device_timeline(st_runtime* rt, const float* inputs, size_t count, long l
     a.score = rt->dev_score;
     a.timeline = tl;
     a.timeline_capacity = (int)std::min<size_t>(capacity, 1u << 30);
+    a.timeline_cta = cta;
     st = launch_trace(rt, a, dev, count, nullptr, true);
   }
   if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "timeline run");
   if (st == ST_OK) st = check_device_error(rt);
   if (st == ST_OK) st = rt->cuda(cudaMemcpy(marks, tl, capacity * sizeof(long long), cudaMemcpyDeviceToHost), "timeline download");
-  if (st == ST_OK && used) {
+  if (st == ST_OK && used) {  // warp 0's entries
+    const size_t per_warp = capacity / kWarps;
     size_t u = 0;
-    while (u < capacity && marks[u] != 0) ++u;
+    while (u < per_warp && marks[u] != 0) ++u;
     *used = u;
   }
   cudaFree(dev);
@@ -1142,7 +1159,7 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     << ",\"shared_bytes\":" << fa.sharedSizeBytes << ",\"dynamic_shared_bytes\":" << kSmem2
     << ",\"cluster\":" << rt->cluster << ",\"clusters\":" << rt->nclusters
     << ",\"cooperative_clusters\":" << (rt->coop_clusters ? "true" : "false")
-    << ",\"weight_ring\":" << (rt->ring ? "true" : "false")
+    << ",\"weight_ring\":" << (rt->ring ? "true" : "false") << ",\"l2_keep_layers\":" << rt->args.l2_keep_layers
     << ",\"attention_implementation\":\"one cluster per head, window split over the cluster, partials merged through DSMEM\""
     << ",\"matvec_implementation\":\"16-byte non-temporal loads; out- and down-projections K-split (per head, per ffn slice)\""
     << ",\"barriers_per_step\":" << forward_barrier_count(rt)

@@ -58,8 +58,6 @@ constexpr int kMaxWidth = 1024;
 constexpr int kMaxHeadDim = 1024;
 constexpr int kMaxWindow = 4096;
 constexpr int kMaxFfn = 4096;
-constexpr int kAttDims = 256;                 // head dims one attention pass covers
-constexpr int kAttPerLane = kAttDims / 32;
 constexpr int kKvBytes = 16 * 1024;           // K and V rows one CTA prefetches per head
 
 // Shared scratch of one step CTA (~110 KB; the weight ring takes the rest of
@@ -74,7 +72,7 @@ struct alignas(128) Smem2 {
   union {
     struct {
       float apart[kMaxCluster * (kMaxHeadDim + 2)];  // CTA attention partials per rank (DSMEM target)
-      float wpart[kWarps * (kAttDims + 2)];          // per-warp attention partials
+      float logits[kMaxWindow];                      // this CTA's logits, then softmax weights
       alignas(16) unsigned char kv[kKvBytes];        // this CTA's K rows, then V rows
     } at;
     struct {
@@ -87,8 +85,11 @@ struct alignas(128) Smem2 {
   float rope[kMaxHeadDim / 2];                   // RoPE frequencies, loaded once per launch
   float2 rope_cs[kMaxHeadDim / 2];               // cos, sin of t * frequency for the current stream
   unsigned long long t;                          // position of the stream being stepped
+  int slot, valid;                               // t % window and the retained slot count
+  float att[2];                                  // max logit and softmax sum of this CTA's slots
+  float rscale[kMaxCluster];                     // merge weight of each rank's attention partial
   int sync_ok;                                   // verdict of the last grid sync (DSMEM target)
-  int tl_n;                                      // timeline entries written by this CTA
+  int tl_nw[kWarps];                             // timeline entries written by each warp
 };
 
 // Dynamic shared memory of the step kernels: Smem2, the ring header, then the
@@ -109,20 +110,25 @@ enum TimelineTag : int {
   kTlGateUp, kTlDownPartial, kTlClusterReduce, kTlResidualClusters, kTlStepEnd, kTlRingFill, kTlIssueAt
 };
 
-// Phase-boundary mark (CTA 0, thread 0) when a timeline buffer is given:
-// clock64() << 8 | tag. Compiled only into the diagnostic kernel variants.
+// Phase-boundary mark, clock64() << 8 | tag, by lane 0 of every warp of CTA
+// a.timeline_cta when a timeline buffer is given; warp w fills its own
+// region [w * capacity / kWarps, (w + 1) * capacity / kWarps). Compiled only
+// into the diagnostic kernel variants.
+__device__ __forceinline__ void tl_put(const StepArgs& a, Smem2& sm, long long value) {
+  if (a.timeline && blockIdx.x == a.timeline_cta && (threadIdx.x & 31) == 0) {
+    const int w = threadIdx.x >> 5, per_warp = a.timeline_capacity / kWarps;
+    if (sm.tl_nw[w] < per_warp) a.timeline[(size_t)w * per_warp + sm.tl_nw[w]++] = value;
+  }
+}
 template <bool kDiag = true>
 __device__ __forceinline__ void tl_mark(const StepArgs& a, Smem2& sm, int tag) {
-  if constexpr (kDiag)
-    if (a.timeline && blockIdx.x == 0 && threadIdx.x == 0 && sm.tl_n < a.timeline_capacity)
-      a.timeline[sm.tl_n++] = (long long)((clock64() << 8) | (long long)tag);
+  if constexpr (kDiag) tl_put(a, sm, (long long)((clock64() << 8) | (long long)tag));
 }
 
 // Diagnostics: the issue time of the chunk just acquired, as a mark tagged
 // kTlIssueAt (not an interval; the host pairs it with the next mark).
 __device__ __forceinline__ void tl_mark_issue(const StepArgs& a, Smem2& sm, const RingSmem& rs, const Ring& rg) {
-  if (a.timeline && blockIdx.x == 0 && threadIdx.x == 0 && sm.tl_n < a.timeline_capacity)
-    a.timeline[sm.tl_n++] = (long long)((rs.issued_at[(rg.consumed) % kRingChunks] << 8) | (long long)kTlIssueAt);
+  tl_put(a, sm, (long long)((rs.issued_at[(rg.consumed) % kRingChunks] << 8) | (long long)kTlIssueAt));
 }
 
 // Compile-time shape of a step kernel: weights through the shared-memory ring
@@ -209,7 +215,7 @@ struct ClusterGridSync {
                        Ring* rg = nullptr, RingSmem* rs = nullptr) {
     cluster_sync();
     if (tl) tl_mark(a, *tl, kTlSyncArrive);
-    if (rg) ring_fill(*rg, *rs);
+    if (rg) ring_fill(*rg, *rs, kFillAll);
     const unsigned rank = cluster_rank();
     if (rank == 0 && threadIdx.x == kIssuer) {
       epoch += 1;
@@ -222,7 +228,7 @@ struct ClusterGridSync {
         unsigned int polls = 0;
         while (ld_acquire_gpu(a.bar_counter) < target) {
           if ((++polls & 63u) == 0) {
-            if (rg) ring_fill(*rg, *rs);
+            if (rg) ring_fill(*rg, *rs, kFillAll);
             if (ld_volatile_int(a.error) != 0) { good = 0; break; }
             const unsigned long long now = globaltimer();
             if (start == 0) start = now;
@@ -249,9 +255,12 @@ __device__ __forceinline__ bool cluster_shape_ok(const StepArgs& a) {
   return false;
 }
 
+// Contiguous share [lo, hi) of `units` for part `part` of `parts`. Model and
+// grid limits (units <= 4096, parts <= 1024) keep units * parts in 32 bits,
+// so this stays a 32-bit division (a 64-bit one is a long software routine).
 __device__ __forceinline__ void split(int units, int part, int parts, int& lo, int& hi) {
-  lo = (int)(((long long)units * part) / parts);
-  hi = (int)(((long long)units * (part + 1)) / parts);
+  lo = (int)(((unsigned)units * (unsigned)part) / (unsigned)parts);
+  hi = (int)(((unsigned)units * (unsigned)(part + 1)) / (unsigned)parts);
 }
 
 __device__ __forceinline__ int valid_length(unsigned long long t, int window) {
@@ -381,8 +390,12 @@ template <typename T, int U, bool kShared, typename Epi>
 __device__ __forceinline__ void warp_rows_x(const T* W, int n, const RowGeom<T>& g, const XRegs<T>& xr,
                                             const float* xs, Epi&& epi, int g0 = 0) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // Rows from the ring skip the issuer's warp, whose copies would hold up the
+  // barrier that ends the phase.
+  constexpr int kW = kShared ? kWarps - 1 : kWarps;
+  if (warp >= kW) return;
   const int sub = lane / g.lpr, sl = lane - sub * g.lpr;
-  const int groups = n / U, per_pass = kWarps * g.rpw;
+  const int groups = n / U, per_pass = kW * g.rpw;
   const int first = ((warp * g.rpw - g0) % per_pass + per_pass) % per_pass;
   for (int base = first; base < groups; base += per_pass) {
     const int gi = base + sub;
@@ -425,7 +438,7 @@ __device__ __forceinline__ void ring_rows(const StepArgs& a, Ring& rg, RingSmem&
 // right after barriers, when every warp has released what it consumed.
 template <class Cfg>
 __device__ __forceinline__ void ring_poll(Ring& rg, RingSmem& rs) {
-  if constexpr (Cfg::kRing) ring_fill(rg, rs);
+  if constexpr (Cfg::kRing) ring_fill(rg, rs, 2);
 }
 
 // Rows [0, rows) of a weight matrix: from the ring (kRing) or straight from
@@ -506,9 +519,16 @@ __device__ __forceinline__ void residual_from_clusters(const StepArgs& a, int s,
 }
 
 // ---------------------------------------------------------------- blocks
-// Position of stream s into sm.t (read by other threads after the next barrier).
-__device__ __forceinline__ void load_position(const StepArgs& a, int s, Smem2& sm) {
-  if (threadIdx.x == 0) sm.t = ld_cg_u64(a.position + s);
+// Position of stream s into sm.t (read by other threads after the next
+// barrier): the stored position plus `event`, the events this launch has
+// already stepped without storing their positions.
+__device__ __forceinline__ void load_position(const StepArgs& a, int s, Smem2& sm, unsigned long long event = 0) {
+  if (threadIdx.x == 0) {
+    const unsigned long long t = ld_cg_u64(a.position + s) + event;
+    sm.t = t;
+    sm.slot = (int)(t % (unsigned long long)a.window);
+    sm.valid = valid_length(t, a.window);
+  }
 }
 
 // RoPE rotation of the current position, angle = float(t) * frequency
@@ -570,86 +590,79 @@ __device__ __forceinline__ bool kv_prefetch(const T* keys, const T* values, int 
   return true;
 }
 
-// Attention of head h over this CTA's slots [j0, j1): every warp folds its
-// slots j0 + warp, j0 + warp + kWarps, ... into an online-softmax partial
-// (m, l, acc) (reference src/cpu/Cpu.cpp:97-110: logits q.k / sqrt(hd), softmax
-// over the retained slots, sum p v); the CTA merges its warps in warp order
-// and broadcasts (m, l, acc) into apart[rank] of every CTA of the cluster.
-// Head dims are covered kAttDims at a time (one pass for hd <= 256).
+// Attention of head h over this CTA's slots [j0, j1) (reference
+// src/cpu/Cpu.cpp:97-110: logits q.k / sqrt(hd), softmax over the retained
+// slots, sum p v): warps compute the logits (one slot per warp at a time),
+// warp 0 turns them into softmax weights against this CTA's max, and every
+// thread then computes one (rank, dim) value of the partial (m, l, acc),
+// storing it straight into apart[rank] of that rank's CTA. The partial is
+// computed once per destination rank, which costs a few FMAs and saves a
+// barrier.
 template <typename T, class Cfg>
 __device__ void attention_share(const StepArgs& a, int l, int s, int h, int j0, int j1, int slot, bool kv_smem,
                                 const ClusterPos& cp, Smem2& sm) {
-  const int hd = a.head_dim, W = a.window;
+  const int hd = a.head_dim, W = a.window, n = j1 - j0;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const size_t head_base = ((((size_t)s * a.layers + l) * a.heads + h) * (size_t)W) * hd;
   const T* Kg = (const T*)a.keys + head_base;
   const T* Vg = (const T*)a.values + head_base;
   const T* Ks = reinterpret_cast<const T*>(sm.u.at.kv);
-  const T* Vs = Ks + (size_t)(j1 - j0) * hd;
+  const T* Vs = Ks + (size_t)n * hd;
   const float* q = sm.qkv;
   const float* kcur = sm.qkv + hd;
   const float* vcur = sm.qkv + 2 * hd;
   const float root = sqrtf((float)hd);
-  float* wp = sm.u.at.wpart + warp * (kAttDims + 2);
-  float* mine = sm.u.at.apart + (size_t)cp.rank * (hd + 2);
-  for (int b = 0; b < hd; b += kAttDims) {
-    const int nb = min(kAttDims, hd - b);
-    float m = -INFINITY, lsum = 0.f, acc[kAttPerLane];
-#pragma unroll
-    for (int k = 0; k < kAttPerLane; ++k) acc[k] = 0.f;
-    for (int j = j0 + warp; j < j1; j += kWarps) {
-      const bool cur = j == slot;
-      const T* krow = kv_smem ? Ks + (size_t)(j - j0) * hd : Kg + (size_t)j * hd;
-      const T* vrow = kv_smem ? Vs + (size_t)(j - j0) * hd : Vg + (size_t)j * hd;
-      float dot = 0.f;
-      for (int i = lane; i < hd; i += 32) {
-        const float kv = cur ? kcur[i] : kv_smem ? Storage<T>::load(krow, i) : Storage<T>::load_cg(krow, i);
-        dot = fmaf(q[i], kv, dot);
-      }
-      dot = warp_sum(dot);
-      const float logit = dot / root;
-      const float mn = fmaxf(m, logit);
-      const float so = expf(m - mn), p = expf(logit - mn);
-      lsum = lsum * so + p;
-      m = mn;
-#pragma unroll
-      for (int k = 0; k < kAttPerLane; ++k) {
-        const int dd = lane + 32 * k;
-        if (dd < nb) {
-          const float v = cur ? vcur[b + dd] : kv_smem ? Storage<T>::load(vrow, b + dd) : Storage<T>::load_cg(vrow, b + dd);
-          acc[k] = fmaf(acc[k], so, p * v);
-        }
-      }
+  float* logits = sm.u.at.logits;
+  for (int j = j0 + warp; j < j1; j += kWarps) {
+    const T* krow = kv_smem ? Ks + (size_t)(j - j0) * hd : Kg + (size_t)j * hd;
+    float dot = 0.f;
+    if (j == slot) {
+      for (int i = lane; i < hd; i += 32) dot = fmaf(q[i], kcur[i], dot);
+    } else if (kv_smem) {
+      for (int i = lane; i < hd; i += 32) dot = fmaf(q[i], Storage<T>::load(krow, i), dot);
+    } else {
+      for (int i = lane; i < hd; i += 32) dot = fmaf(q[i], Storage<T>::load_cg(krow, i), dot);
     }
+    dot = warp_sum(dot);
+    if (lane == 0) logits[j - j0] = dot / root;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float m = -INFINITY;
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, logits[j]);
+    m = warp_max(m);
+    float sum = 0.f;
+    for (int j = lane; j < n; j += 32) {
+      const float p = expf(logits[j] - m);
+      logits[j] = p;
+      sum += p;
+    }
+    sum = warp_sum(sum);
     if (lane == 0) {
-      wp[0] = m;
-      wp[1] = lsum;
+      sm.att[0] = n > 0 ? m : -INFINITY;
+      sm.att[1] = n > 0 ? sum : 0.f;
     }
-#pragma unroll
-    for (int k = 0; k < kAttPerLane; ++k)
-      if (lane + 32 * k < nb) wp[2 + lane + 32 * k] = acc[k];
-    __syncthreads();
-    if (b == 0) tl_mark<Cfg::kDiag>(a, sm, kTlPv);
-    // CTA merge in warp order; item (rank k, value i) per thread, i = 0: m,
-    // 1: l, 2..: acc[b + i - 2]; every item recomputes the merge weights.
-    const int vals = nb + 2, items = vals * (int)cp.size;
-    for (int it = threadIdx.x; it < items; it += kThreads) {
-      const int k = it / vals, i = it - k * vals;
-      if (b > 0 && i < 2) continue;  // m and l were sent with the first pass
-      float M = -INFINITY;
-      for (int w = 0; w < kWarps; ++w) {
-        const float* pw = sm.u.at.wpart + w * (kAttDims + 2);
-        if (pw[1] > 0.f) M = fmaxf(M, pw[0]);
+  }
+  __syncthreads();
+  tl_mark<Cfg::kDiag>(a, sm, kTlPv);
+  float* mine = sm.u.at.apart + (size_t)cp.rank * (hd + 2);
+  const int vals = hd + 2, items = vals * (int)cp.size;
+  for (int it = threadIdx.x; it < items; it += kThreads) {
+    const int k = it / vals, i = it - k * vals;
+    float v;
+    if (i < 2) {
+      v = sm.att[i];
+    } else {
+      const int dd = i - 2;
+      v = 0.f;
+      for (int j = j0; j < j1; ++j) {
+        const float x = j == slot ? vcur[dd]
+                        : kv_smem ? Storage<T>::load(Vs + (size_t)(j - j0) * hd, dd)
+                                  : Storage<T>::load_cg(Vg + (size_t)j * hd, dd);
+        v = fmaf(logits[j - j0], x, v);
       }
-      float r = 0.f;
-      for (int w = 0; w < kWarps; ++w) {
-        const float* pw = sm.u.at.wpart + w * (kAttDims + 2);
-        if (pw[1] > 0.f) r = fmaf(pw[i == 1 ? 1 : i], expf(pw[0] - M), r);
-      }
-      const float v = i == 0 ? M : r;
-      dsmem_store(mine + (i < 2 ? i : b + i), (unsigned)k, v);
     }
-    if (b + kAttDims < hd) __syncthreads();  // wpart is rewritten by the next pass
+    dsmem_store(mine + i, (unsigned)k, v);
   }
 }
 
@@ -660,9 +673,7 @@ __device__ void attention_head(const StepArgs& a, int l, int s, int h, const Clu
                                RingSmem& rs) {
   const int d = a.width, hd = a.head_dim, W = a.window;
   const LayerPtrs& w = a.layer[l];
-  const unsigned long long t = sm.t;
-  const int slot = (int)(t % (unsigned long long)W);
-  const int valid = valid_length(t, W);
+  const int slot = sm.slot, valid = sm.valid;
   T* keys = (T*)a.keys + ((((size_t)s * a.layers + l) * a.heads + h) * (size_t)W) * hd;
   T* values = (T*)a.values + ((((size_t)s * a.layers + l) * a.heads + h) * (size_t)W) * hd;
   int j0, j1;
@@ -710,21 +721,28 @@ __device__ void attention_head(const StepArgs& a, int l, int s, int h, const Clu
   tl_mark<Cfg::kDiag>(a, sm, kTlAttention);
   cluster_sync();
   tl_mark<Cfg::kDiag>(a, sm, kTlPartialsShared);
-  // merge the cluster's partials in rank order -> attn_h (cast) in sm.g.xs[0..hd)
-  for (int i = threadIdx.x; i < hd; i += kThreads) {
+  // merge the cluster's partials in rank order -> attn_h (cast) in sm.g.xs[0..hd):
+  // the first warp computes each rank's weight exp(m_k - M) (0 for an empty
+  // share) once, then every dim folds the ranks in order.
+  if (threadIdx.x < 32) {
     float M = -INFINITY;
     for (unsigned k = 0; k < cp.size; ++k) {
       const float* pk = sm.u.at.apart + (size_t)k * (hd + 2);
       if (pk[1] > 0.f) M = fmaxf(M, pk[0]);
     }
+    if (threadIdx.x < cp.size) {
+      const float* pk = sm.u.at.apart + (size_t)threadIdx.x * (hd + 2);
+      sm.rscale[threadIdx.x] = pk[1] > 0.f ? expf(pk[0] - M) : 0.f;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < hd; i += kThreads) {
     float L = 0.f, acc = 0.f;
     for (unsigned k = 0; k < cp.size; ++k) {
       const float* pk = sm.u.at.apart + (size_t)k * (hd + 2);
-      if (pk[1] > 0.f) {
-        const float scale = expf(pk[0] - M);
-        L = fmaf(pk[1], scale, L);
-        acc = fmaf(pk[2 + i], scale, acc);
-      }
+      const float scale = sm.rscale[k];
+      L = fmaf(pk[1], scale, L);
+      acc = fmaf(pk[2 + i], scale, acc);
     }
     sm.g.xs[i] = Storage<T>::round(acc / L);
     if constexpr (Cfg::kDiag)
@@ -838,17 +856,26 @@ __device__ void block_ffn(const StepArgs& a, int l, int s, const ClusterPos& cp,
   tl_mark<Cfg::kDiag>(a, sm, kTlClusterReduce);
 }
 
-// Final RMSNorm + score head (no cast) for stream s from sm.xres; CTA 0 only.
+// Final RMSNorm + score head (no cast) for stream s from sm.xres, into
+// a.score[s] and, when given, score_out[s]; one CTA.
 template <typename T>
-__device__ void block_score(const StepArgs& a, int s, Smem2& sm) {
+__device__ void block_score(const StepArgs& a, int s, Smem2& sm, float* score_out = nullptr) {
   norm_vec<T>(sm.xres, (const T*)a.final_norm, a.width, a.epsilon, sm, sm.g.xs);
   float acc = 0.f;
   for (int i = threadIdx.x; i < a.width; i += kThreads)
     acc = fmaf(Storage<T>::load((const T*)a.score_w, i), sm.g.xs[i], acc);
   const float total = block_sum(acc, sm.g);
-  if (threadIdx.x == 0) a.score[s] = total;
+  if (threadIdx.x == 0) {
+    a.score[s] = total;
+    if (score_out) score_out[s] = total;
+  }
   __syncthreads();
 }
+
+// The CTA that writes hidden state, scores and positions in the device-loop
+// kernels: the last one, whose cluster has no attention head at full size and
+// so has slack while the attention clusters work.
+__device__ __forceinline__ bool is_score_cta() { return blockIdx.x == gridDim.x - 1; }
 
 // hidden[s][l] and the residual buffer a.x from x (thread i writes element i,
 // i + kThreads, ...).
@@ -862,17 +889,21 @@ __device__ __forceinline__ void write_hidden(const StepArgs& a, int s, int l, co
 }
 
 // Whole step inside one cluster launch; `input` is [S][features]. Every CTA
-// keeps x and x' in shared memory; streams run one after another.
+// keeps x and x' in shared memory; streams run one after another. `event`
+// counts the events this launch stepped before (their positions are not yet
+// stored); `score_out` ([S], may be null) receives the scores too; with
+// `advance` the positions are stored incremented.
 template <typename T, class Cfg>
 __device__ bool forward2(const StepArgs& a, const float* input, ClusterGridSync& gs, Smem2& sm, Ring& rg,
-                         RingSmem& rs) {
+                         RingSmem& rs, unsigned long long event = 0, float* score_out = nullptr,
+                         bool advance = true) {
   const ClusterPos cp = ClusterPos::get();
   for (int s = 0; s < a.streams; ++s) {
-    // CTA 0 may still read its x for the previous stream's score while the
-    // next input projection writes x through DSMEM.
-    if (s > 0) cluster_sync();
+    // The score CTA may still read its x for the previous stream or event
+    // while the next input projection writes x through DSMEM.
+    if (s > 0 || event > 0) cluster_sync();
     tl_mark<Cfg::kDiag>(a, sm, kTlStepStart);
-    load_position(a, s, sm);
+    load_position(a, s, sm, event);
     step_input<T, Cfg>(a, s, input, cp, sm, rg, rs);
     tl_mark<Cfg::kDiag>(a, sm, kTlInput);
     for (int l = 0; l < a.layers; ++l) {
@@ -891,11 +922,11 @@ __device__ bool forward2(const StepArgs& a, const float* input, ClusterGridSync&
       if (!gs.sync(a, a.bar_timeout_ns, &sm.sync_ok, Cfg::kDiag ? &sm : nullptr, Cfg::kRing ? &rg : nullptr, &rs)) return false;
       residual_from_clusters<T>(a, s, (int)cp.count, sm);
       tl_mark<Cfg::kDiag>(a, sm, kTlResidualClusters);
-      if (blockIdx.x == 0) write_hidden(a, s, l, sm.xres);
+      if (is_score_cta()) write_hidden(a, s, l, sm.xres);
     }
-    if (blockIdx.x == 0) block_score<T>(a, s, sm);
+    if (is_score_cta()) block_score<T>(a, s, sm, score_out);
   }
-  if (blockIdx.x == 0)
+  if (advance && is_score_cta())
     for (int s = threadIdx.x; s < a.streams; s += kThreads) a.position[s] = ld_cg_u64(a.position + s) + 1;
   return true;
 }

@@ -20,7 +20,9 @@
 //                 waiting on the slot mbarriers) or with 16-byte vector loads;
 //                 reports GB/s and thread 0's cycles inside the issue
 //   icache        cycles per pass over 8-64 KB of straight-line code (512
-//                 threads per SM): instruction fetch cost of the step's code
+//                 threads per SM), and cycles per call over 8-128 distinct
+//                 ~1 KB out-of-line functions: instruction fetch cost and the
+//                 instruction cache capacity the step's per-layer code must fit
 //   primitives    SM cycles per call of the step's building blocks, every CTA
 //                 (one per SM) calling each one `count` times back to back:
 //                 __syncthreads, block_sum, gemv_tile on 16 x 512 and 64 x 64
@@ -39,6 +41,7 @@
 #include <sstream>
 #include <string>
 #include <thread>
+#include <utility>
 #include <vector>
 
 #include "../../include/streaming_b200.h"
@@ -160,11 +163,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_bulk_stream(const char* src, si
   __syncthreads();
   unsigned long long issued = 0, spent = 0;
   const size_t chunks = bytes_per_cta / kStreamSlotBytes;
+  const unsigned long long policy = policy_evict_first();
   auto issue = [&]() {
     const int slot = (int)(issued % kStreamSlots);
     const long long c0 = clock64();
     mbar_expect_tx(&rs.full[slot], kStreamSlotBytes);
-    bulk_copy(rs.slot[slot], base + (issued % chunks) * kStreamSlotBytes, kStreamSlotBytes, &rs.full[slot]);
+    bulk_copy(rs.slot[slot], base + (issued % chunks) * kStreamSlotBytes, kStreamSlotBytes, &rs.full[slot], policy);
     spent += (unsigned long long)(clock64() - c0);
     ++issued;
   };
@@ -232,6 +236,35 @@ __global__ void __launch_bounds__(kThreads, 1) k_icache(int reps, unsigned long 
   const long long c1 = clock64();
   if (threadIdx.x == 0) out[blockIdx.x] = (unsigned long long)((c1 - c0) / reps);
   if (a + b + c + d == 12345.f) sink[threadIdx.x] = a;
+}
+
+// Capacity probe: a pass calls N distinct out-of-line functions of ~64
+// instructions each (non-sequential code, so prefetching cannot hide misses);
+// the cycles per call against N (x ~1 KB) show when the code stops fitting.
+template <int K>
+__device__ __noinline__ float icache_fn(float x) {
+#pragma unroll
+  for (int i = 0; i < 60; ++i) asm volatile("fma.rn.f32 %0, %0, 0f3F800054, 0f3F000000;" : "+f"(x));
+  return x + (float)K;
+}
+
+// Calls in a scrambled order (37 K mod N), so consecutive calls land far apart.
+template <int N, int... K>
+__device__ __forceinline__ float icache_calls(float x, std::integer_sequence<int, K...>) {
+  ((x = icache_fn<(K * 37) % N>(x)), ...);
+  return x;
+}
+
+template <int N>
+__global__ void __launch_bounds__(kThreads, 1) k_icache_calls(int reps, unsigned long long* out, float* sink) {
+  float x = threadIdx.x;
+  __syncthreads();
+  const long long c0 = clock64();
+  for (int r = 0; r < reps; ++r) x = icache_calls<N>(x, std::make_integer_sequence<int, N>{});
+  __syncthreads();
+  const long long c1 = clock64();
+  if (threadIdx.x == 0) out[blockIdx.x] = (unsigned long long)((c1 - c0) / reps / N);
+  if (x == 12345.f) sink[threadIdx.x] = x;
 }
 
 constexpr int kPrimitives = 10;
@@ -397,6 +430,22 @@ int run_bench(int device, const std::string& mode, size_t count, int backoff, co
     bad |= run(k_icache<1024>, 1024, false);
     bad |= run(k_icache<2048>, 2048, false);
     bad |= run(k_icache<4096>, 4096, false);
+    o << "},\"cycles_per_call\":{";
+    auto run_calls = [&](auto kernel, int n, bool first) -> int {
+      kernel<<<grid, kThreads, 0, r.stream>>>(reps, out, sink);
+      if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(r.stream) != cudaSuccess) return -1;
+      std::vector<unsigned long long> v(grid);
+      if (cudaMemcpy(v.data(), out, grid * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+      std::sort(v.begin(), v.end());
+      o << (first ? "" : ",") << "\"" << n << "fn\":" << v[grid / 2];
+      return 0;
+    };
+    bad |= run_calls(k_icache_calls<8>, 8, true);
+    bad |= run_calls(k_icache_calls<16>, 16, false);
+    bad |= run_calls(k_icache_calls<32>, 32, false);
+    bad |= run_calls(k_icache_calls<64>, 64, false);
+    bad |= run_calls(k_icache_calls<128>, 128, false);
+    bad |= run_calls(k_icache_calls<256>, 256, false);
     cudaFree(out);
     cudaFree(sink);
     if (bad) {

@@ -52,7 +52,7 @@ def main() -> None:
 # Tags of the device marks (TimelineTag in csrc/st_step.cuh); each mark is
 # clock64() << 8 | tag and charges the interval since the previous mark to its tag.
 TAGS = {1: "step_start", 2: "input", 3: "norm1", 4: "ring_wait", 5: "warp_gemv", 6: "qkv_rows", 7: "qkv_shared",
-        8: "kv_wait", 9: "merge_heads", 10: "logits_pv", 11: "cta_merge_broadcast", 12: "partials_shared",
+        8: "kv_wait", 9: "merge_heads", 10: "logits_softmax", 11: "pv_broadcast", 12: "partials_shared",
         13: "out_rows", 14: "sync_cluster_arrive", 15: "sync_grid_wait", 16: "residual_heads", 17: "norm2",
         18: "gate_up_rows", 19: "down_partial", 20: "cluster_reduce", 21: "residual_clusters", 22: "step_end",
         23: "ring_release_fill"}

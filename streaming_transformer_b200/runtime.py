@@ -118,6 +118,7 @@ def library() -> ctypes.CDLL:
             "st_trace_step": (I, [P, F, F, TRACE_FN, P]),
             "st_device_trace": (I, [P, F, S, F, ctypes.POINTER(ctypes.c_double)]),
             "st_device_timeline": (I, [P, F, S, ctypes.POINTER(ctypes.c_longlong), S, ctypes.POINTER(S)]),
+            "st_device_timeline_cta": (I, [P, F, S, I, ctypes.POINTER(ctypes.c_longlong), S, ctypes.POINTER(S)]),
             "st_device_trace_resident": (I, [P, ctypes.c_void_p, S, ctypes.POINTER(ctypes.c_double),
                                              ctypes.POINTER(U64)]),
             "st_info": (I, [P, ctypes.c_char_p, S, ctypes.POINTER(S)]),
@@ -309,17 +310,23 @@ class Runtime:
             return us.value, (scores[:, 0] if self.streams == 1 else scores)
         return us.value
 
-    def device_timeline(self, events, capacity: int = 1 << 16) -> np.ndarray:
-        """Diagnostic: CTA 0's clock64() at every phase boundary of a device-loop
-        run over ``events`` (see st_device_timeline); returns the marks."""
+    def device_timeline(self, events, capacity: int = 1 << 18, cta: int = 0, warp: int | None = 0) -> np.ndarray:
+        """Diagnostic: clock64() << 8 | tag at every phase boundary of a device-loop
+        run over ``events``, recorded by every warp of one CTA (see
+        st_device_timeline_cta). Returns warp ``warp``'s marks, or all warps'
+        as a [16, capacity // 16] array (zero padded) when ``warp`` is None."""
         e = np.ascontiguousarray(events, dtype=np.float32)
         count = e.shape[0]
         marks = np.zeros(capacity, dtype=np.int64)
         used = ctypes.c_size_t(0)
-        _check(library().st_device_timeline(self._h, _fptr(e), count,
-                                            marks.ctypes.data_as(ctypes.POINTER(ctypes.c_longlong)),
-                                            capacity, ctypes.byref(used)), self._h)
-        return marks[: used.value]
+        _check(library().st_device_timeline_cta(self._h, _fptr(e), count, int(cta),
+                                                marks.ctypes.data_as(ctypes.POINTER(ctypes.c_longlong)),
+                                                capacity, ctypes.byref(used)), self._h)
+        per_warp = marks.reshape(16, capacity // 16)
+        if warp is None:
+            return per_warp
+        row = per_warp[warp]
+        return row[: int(np.count_nonzero(row))]
 
     def device_trace_resident(self, device_ptr: int, count: int) -> tuple[float, int]:
         """Device-only timing with the trace already in device memory (pointer from
