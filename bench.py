@@ -283,7 +283,8 @@ def run_b200(args):
                 "p99_us": metrics.nearest_rank(e2e_lat, 0.99),
                 "path": "Runtime.step -> st_step, persistent mailbox, mapped pinned input/score, host clock"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "kernel": f"k_trace ({mode})",
+                     "traffic": traffic, "kernel": f"k2_trace ({mode}, weight ring)" if info.get("weight_ring")
+                     else f"k2_trace ({mode}, direct loads)",
                      "algorithmic_bytes_per_step": alg / K, "peak_source": peak_src,
                      "traffic_source": traffic_src},
         "gpu_launches": launches,
