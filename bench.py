@@ -207,25 +207,40 @@ def run_reference(args):
     return 0
 
 
+def combine_ranks(values, dist=None, group=None):
+    """Max over ranks of each host-side timing (a CPU tensor over the host
+    group); identity on one process."""
+    import torch
+    t = torch.tensor(list(values), dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return [float(x) for x in t]
+
+
 def run_b200(args):
     import torch
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
-    dist = None
+    dist = host = None
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        # Host-side coordination (barriers, max over ranks) runs over gloo: an
+        # NCCL barrier synchronizes the whole device, which would wait for the
+        # resident persistent worker of the e2e phase until its idle budget
+        # ends it. The step path itself has no collective (replicas).
+        host = dist.new_group(backend="gloo", timeout=timedelta(seconds=120))
 
     def barrier(device_wide=True):
         # While the persistent worker is resident a device-wide synchronize
-        # would wait for that kernel (until its idle budget ends it), so the
-        # e2e phase synchronizes torch's own stream only.
-        if dist:
-            dist.barrier()
+        # would wait for that kernel, so the e2e phase synchronizes torch's own
+        # stream only.
         if device_wide:
             torch.cuda.synchronize()
         else:
             torch.cuda.current_stream().synchronize()
+        if dist:
+            dist.barrier(group=host)
 
     config, mode = workload(args)
     model = synthetic.make_model(config, mode, seed=42)
@@ -258,12 +273,9 @@ def run_b200(args):
         finally:
             rt.close()
     elapsed_s = us * K / 1e6
-    e2e_steps_s = K / e2e_wall
-    t = torch.tensor([elapsed_s, e2e_wall], dtype=torch.float64, device="cuda")
+    max_elapsed, max_e2e = combine_ranks([elapsed_s, e2e_wall], dist, host)
     if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.destroy_process_group()
-    max_elapsed, max_e2e = float(t[0]), float(t[1])
     if rank != 0:
         return 0
     value = world * K / max_elapsed
