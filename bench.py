@@ -60,6 +60,8 @@ def parse_args():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--config", default="c2-main-fp32", choices=sorted(synthetic.CONFIGS))
     p.add_argument("--window", type=int, default=0, help="override the window (C3 sweep)")
+    p.add_argument("--streams", type=int, default=1,
+                   help="independent streams per GPU (C4/C5-A: the total is streams x GPUs, partitioned by rank)")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
@@ -72,16 +74,19 @@ def workload(args):
     return config, mode
 
 
-def config_json(args, config, mode, working_set):
+def config_json(args, config, mode, working_set, world=1):
+    s = max(1, args.streams)
+    per_gpu = "single stream per GPU" if s == 1 else f"{s} streams per GPU"
     return {
-        "workload": f"{args.config}: {mode} single stream per GPU, d{config.width} L{config.layers} "
+        "workload": f"{args.config}: {mode} {per_gpu}, d{config.width} L{config.layers} "
                     f"H{config.heads} hd{config.head_dim} F{config.ffn} W{config.window}, "
                     f"{config.features} features",
         "model": "local-causal pre-RMSNorm transformer (streaming step)",
-        "streams_per_gpu": 1,
-        "global_batch": 1,
+        "streams_per_gpu": s,
+        "global_batch": s * world,
         "seq_len": config.window,
-        "parallelism": "replicas (independent streams, no collective)",
+        "parallelism": "streams partitioned across GPUs (independent, no collective)" if s > 1
+                       else "replicas (independent streams, no collective)",
         "data": "seeded N(0,0.02) weights, unit norm gains, N(0,1) events",
         "l2": ("working set %.1f MB > 126 MB L2, no flush" % (working_set / 1e6)) if working_set > L2_BYTES
               else ("working set %.1f MB fits in L2; no flush between steps (streaming state carries "
@@ -195,11 +200,13 @@ def run_reference(args):
     ws = metrics.weight_bytes(config, mode) + 2 * config.layers * config.width * config.window * metrics.ELEM_BYTES[mode]
     sample = (f"{n} consecutive events from reset of the {args.config} trace, C restatement of the reference "
               f"CPU step (reference Eigen src/cpu/Cpu.cpp needs Eigen3, absent), {threads} threads, {dt:.1f} s")
+    if args.streams > 1:
+        sample += "; streams are independent, so stream-steps/s is the single-stream rate"
     line = {
         "impl": "reference", "metric": METRIC, "value": steps_per_s, "unit": "steps/s", "n_gpus": args.gpus,
         "steps": n, "warmup": 0, "ms_per_step": 1000.0 / steps_per_s, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": mode, "data": "synthetic",
-        "config": config_json(args, config, mode, ws),
+        "config": config_json(args, config, mode, ws, world),
         "cpu_baseline": {"value": steps_per_s, "unit": "steps/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": steps_per_s, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -245,20 +252,24 @@ def run_b200(args):
     config, mode = workload(args)
     model = synthetic.make_model(config, mode, seed=42)
     K, W = max(1, args.steps), max(3, args.warmup)
-    events = synthetic.make_events(K + W, config.features, seed=123 + rank)
+    S = max(1, args.streams)
+    # stream g = rank * S + s has its own seeded trace
+    events = np.stack([synthetic.make_events(K + W, config.features, seed=123 + rank * S + s) for s in range(S)],
+                      axis=1)  # [K + W, S, features]
     e2e_lat = []
     with ClockSampler(local) as clocks:
-        rt = Runtime(model, RuntimeOptions(backend=Backend.PERSISTENT, blocks=0, device=local))
+        rt = Runtime(model, RuntimeOptions(backend=Backend.PERSISTENT, blocks=0, device=local), streams=S)
+        step = (lambda e: rt.step(e[0])) if S == 1 else rt.step_batch
         try:
-            # ---- e2e through the public API: host event in, host score out
+            # ---- e2e through the public API: host events in, host scores out
             for e in events[:W]:
-                rt.step(e)
+                step(e)
             rt.reset()
             barrier(device_wide=False)
             t_start = time.perf_counter()
             for e in events[W:W + K]:
                 t0 = time.perf_counter_ns()
-                rt.step(e)
+                step(e)
                 e2e_lat.append((time.perf_counter_ns() - t0) / 1000.0)
             e2e_wall = time.perf_counter() - t_start
             barrier(device_wide=False)
@@ -267,7 +278,7 @@ def run_b200(args):
             torch.cuda.synchronize()
             rt.device_trace_resident(dev_events.data_ptr(), W)       # warm-up (untimed)
             barrier()
-            us, launches = rt.device_trace_resident(dev_events[W:].data_ptr(), K)
+            us, launches = rt.device_trace_resident(dev_events[W:].data_ptr(), K)  # us per round of S streams
             barrier()
             info = rt.info()
         finally:
@@ -278,20 +289,20 @@ def run_b200(args):
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    value = world * K / max_elapsed
+    value = world * S * K / max_elapsed
     peak, peak_src = measured_peak()
-    alg = metrics.trace_bytes(config, mode, K)
+    alg = metrics.trace_bytes(config, mode, K, streams=S)
     achieved = alg / K / (us * 1e-6) / 1e9
     traffic, traffic_src = measured_traffic(args.config)
-    ws = metrics.weight_bytes(config, mode) + 2 * config.layers * config.width * config.window * metrics.ELEM_BYTES[mode]
+    ws = metrics.weight_bytes(config, mode) + S * 2 * config.layers * config.width * config.window * metrics.ELEM_BYTES[mode]
     line = {
         "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": max_elapsed * 1000.0 / K, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": mode, "data": "synthetic",
-        "config": config_json(args, config, mode, ws),
+        "config": config_json(args, config, mode, ws, world),
         "p50_us_per_step_device": us,
-        "e2e": {"value": world * K / max_e2e, "unit": "steps/s", "h2d_bytes_per_step": 4 * config.features,
-                "d2h_bytes_per_step": 4, "p50_us": metrics.nearest_rank(e2e_lat, 0.5),
+        "e2e": {"value": world * S * K / max_e2e, "unit": "steps/s", "h2d_bytes_per_step": 4 * config.features * S,
+                "d2h_bytes_per_step": 4 * S, "p50_us": metrics.nearest_rank(e2e_lat, 0.5),
                 "p99_us": metrics.nearest_rank(e2e_lat, 0.99),
                 "path": "Runtime.step -> st_step, persistent mailbox, mapped pinned input/score, host clock"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -306,7 +317,7 @@ def run_b200(args):
                     "barriers_per_step": info.get("barriers_per_step")},
     }
     if world == 1 and not args.no_cpu_baseline:
-        sps, n, dt = time_cpu_oracle(model, events, 1, args.cpu_seconds, K)
+        sps, n, dt = time_cpu_oracle(model, events[:, 0], 1, args.cpu_seconds, K)
         line["cpu_baseline"] = {
             "value": sps, "unit": "steps/s", "cores": 1, "kind": "port",
             "sample": f"{n} events from reset, C restatement of the reference CPU step, 1 thread, {dt:.1f} s"}

@@ -57,8 +57,8 @@ struct PersistArgs {
   __syncthreads()
 
 // Ring setup shared by the step kernels (kRing variants only; the host chose
-// them after ring_supported). `steps` bounds the chunks issued (0: unbounded,
-// resident kernel). Returns false, with the error word set, when the chunk
+// them after ring_supported). `steps` bounds the chunks issued: steps x
+// streams x chunks per step (0: unbounded, resident kernel). Returns false, with the error word set, when the chunk
 // table could not be built -- the whole grid then leaves before any barrier.
 template <typename T, bool kRing>
 __device__ bool ring_setup(const StepArgs& a, Ring& rg, RingSmem& rs, unsigned char* buf, unsigned long long steps) {
@@ -67,7 +67,9 @@ __device__ bool ring_setup(const StepArgs& a, Ring& rg, RingSmem& rs, unsigned c
   if constexpr (!kRing) return true;
   const ClusterPos cp = ClusterPos::get();
   const Where w{(int)cp.rank, (int)cp.size, (int)cp.id, (int)cp.count};
-  const unsigned long long limit = steps ? steps * chunks_per_step(a, w, sizeof(T)) : ~0ull;
+  // every stream of every step walks the chunk list once
+  const unsigned long long limit =
+      steps ? steps * (unsigned long long)a.streams * chunks_per_step(a, w, sizeof(T)) : ~0ull;
   ring_begin(a, rg, rs, buf, kRingCapacity, w, sizeof(T), limit, true);
   if (!rg.enabled && threadIdx.x == 0) set_error(a, kRingTable);
   return rg.enabled;

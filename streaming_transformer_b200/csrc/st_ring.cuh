@@ -255,6 +255,7 @@ struct alignas(128) RingSmem {
   unsigned long long stream_policy;      // createpolicy L2::evict_first
   unsigned capacity;                     // ring bytes
   unsigned head_off;                     // head % capacity
+  int failed;                            // a wait timed out; acquires no longer wait
   int nchunks;                           // chunks per step in `table`
   int next;                              // table index of the next chunk to issue
   RingChunk table[kMaxRingChunkTable];
@@ -347,12 +348,14 @@ __device__ inline void ring_begin(const StepArgs& a, Ring& r, RingSmem& rs, unsi
   if (threadIdx.x == kIssuer) {
     rs.head = rs.tail = rs.issued = rs.released = 0;
     rs.head_off = 0;
+    rs.failed = 0;
     rs.keep_policy = policy_evict_last();
     rs.stream_policy = policy_evict_first();
     rs.limit = limit;
     rs.buf = buf;
     rs.capacity = capacity;
     rs.next = 0;
+    for (int i = 0; i < kRingChunks; ++i) rs.off[i] = 0;
     table_ok = enabled && capacity >= 2u * kChunkBytes && build_chunk_table(a, w, elem, rs);
     if (table_ok) {
       for (int i = 0; i < kRingChunks; ++i) {
@@ -383,13 +386,21 @@ static __device__ __noinline__ bool ring_wait_slow(Ring& r, RingSmem& rs, int sl
   }
 }
 
+// After a timed-out wait the slot may never have been issued in this launch
+// (its offset is whatever the previous use left), so the ring is marked
+// failed (later acquires stop waiting; the error word ends the launch at its
+// next grid barrier) and every acquire from then on returns the start of the
+// ring, which holds a full chunk. A completed wait returns the offset the
+// issuer stored for the chunk, which never crosses the end of the ring.
 __device__ __forceinline__ const unsigned char* ring_acquire(const StepArgs& a, Ring& r, RingSmem& rs) {
   const int slot = (int)(r.consumed % kRingChunks);
   const unsigned parity = (unsigned)((r.consumed / kRingChunks) & 1ull);
-  if (!mbar_try_wait(&rs.full[slot], parity) && !ring_wait_slow(r, rs, slot, parity, a.bar_timeout_ns) &&
-      threadIdx.x == kIssuer)
-    set_error(a, kBarrierTimeout);
-  return rs.buf + rs.off[slot];
+  if (!mbar_try_wait(&rs.full[slot], parity) && !*reinterpret_cast<volatile int*>(&rs.failed) &&
+      !ring_wait_slow(r, rs, slot, parity, a.bar_timeout_ns)) {
+    rs.failed = 1;
+    if (threadIdx.x == kIssuer) set_error(a, kBarrierTimeout);
+  }
+  return rs.buf + (*reinterpret_cast<volatile int*>(&rs.failed) ? 0u : rs.off[slot]);
 }
 
 // Every thread of a warp, after the warp's last read of the chunk: one
