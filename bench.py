@@ -258,7 +258,10 @@ def run_b200(args):
                       axis=1)  # [K + W, S, features]
     e2e_lat = []
     with ClockSampler(local) as clocks:
-        rt = Runtime(model, RuntimeOptions(backend=Backend.PERSISTENT, blocks=0, device=local), streams=S)
+        # One stream: the persistent mailbox (lowest latency). Several streams:
+        # FUSED, one batched-round launch per st_step_batch call.
+        backend = Backend.PERSISTENT if S == 1 else Backend.FUSED
+        rt = Runtime(model, RuntimeOptions(backend=backend, blocks=0, device=local), streams=S)
         step = (lambda e: rt.step(e[0])) if S == 1 else rt.step_batch
         try:
             # ---- e2e through the public API: host events in, host scores out
@@ -293,7 +296,7 @@ def run_b200(args):
     peak, peak_src = measured_peak()
     alg = metrics.trace_bytes(config, mode, K, streams=S)
     achieved = alg / K / (us * 1e-6) / 1e9
-    traffic, traffic_src = measured_traffic(args.config)
+    traffic, traffic_src = measured_traffic(args.config) if not info.get("batched") else (None, None)
     ws = metrics.weight_bytes(config, mode) + S * 2 * config.layers * config.width * config.window * metrics.ELEM_BYTES[mode]
     line = {
         "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -304,17 +307,22 @@ def run_b200(args):
         "e2e": {"value": world * S * K / max_e2e, "unit": "steps/s", "h2d_bytes_per_step": 4 * config.features * S,
                 "d2h_bytes_per_step": 4 * S, "p50_us": metrics.nearest_rank(e2e_lat, 0.5),
                 "p99_us": metrics.nearest_rank(e2e_lat, 0.99),
-                "path": "Runtime.step -> st_step, persistent mailbox, mapped pinned input/score, host clock"},
+                "path": ("Runtime.step -> st_step, persistent mailbox, mapped pinned input/score, host clock"
+                         if S == 1 else "Runtime.step_batch -> st_step_batch, one batched-round launch (FUSED), "
+                         "pinned copies of the S inputs and scores, host clock")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "kernel": f"k2_trace ({mode}, weight ring)" if info.get("weight_ring")
-                     else f"k2_trace ({mode}, direct loads)",
+                     "traffic": traffic,
+                     "kernel": (f"k3_rounds ({mode}, batched round of {S} streams)" if info.get("batched")
+                                else f"k2_trace ({mode}, weight ring)" if info.get("weight_ring")
+                                else f"k2_trace ({mode}, direct loads)"),
                      "algorithmic_bytes_per_step": alg / K, "peak_source": peak_src,
                      "traffic_source": traffic_src},
         "gpu_launches": launches,
         "clocks": clocks.summary(),
         "runtime": {"blocks": info.get("blocks"), "threads": info.get("threads"),
                     "registers_per_thread": info.get("registers_per_thread"),
-                    "barriers_per_step": info.get("barriers_per_step")},
+                    "barriers_per_step": info.get("barriers_per_step"), "batched": info.get("batched"),
+                    "batched_grid": info.get("batched_grid"), "batched_splits": info.get("batched_splits")},
     }
     if world == 1 and not args.no_cpu_baseline:
         sps, n, dt = time_cpu_oracle(model, events[:, 0], 1, args.cpu_seconds, K)

@@ -163,7 +163,10 @@ int st_device_trace(st_runtime* rt, const float* inputs, size_t count, float* sc
 int st_device_timeline(st_runtime* rt, const float* inputs, size_t count, long long* marks, size_t capacity,
                        size_t* used);
 
-/* Same, recorded by CTA `cta` of the grid (0 <= cta < blocks in st_info). */
+/* Same, recorded by CTA `cta` of the grid (0 <= cta < blocks in st_info, or
+ * < batched_grid when st_info reports "batched": then thread 0 of that CTA
+ * records the end of every phase of the batched round, tags 40-48, and every
+ * grid-barrier exit, tag 49, in warp 0's row). */
 int st_device_timeline_cta(st_runtime* rt, const float* inputs, size_t count, int cta, long long* marks,
                            size_t capacity, size_t* used);
 

@@ -1,0 +1,751 @@
+// st_batch.cuh -- the batched round: one step of every stream in one pass over
+// the weights.
+//
+// With S independent streams the per-stream GEMVs of the step become skinny
+// GEMMs (rows = weight rows, columns = streams), so every weight byte is read
+// once per round instead of once per stream. A round is a sequence of phases
+// over the whole grid (one CTA per SM, 512 threads), separated by grid
+// barriers:
+//
+//   P0   per stream: x = cast(W_in e), z = norm1_0(x)               (CTA per stream)
+//   per layer l:
+//   G1   Pq[k][s][m]  = sum_{k-split} Wqkv[m] . z[s]                (warp units)
+//   A    per (stream, head): q, k, v = cast(sum_k Pq), RoPE, cast, K/V slot
+//        insert, window attention (each warp a slice of the slots, online
+//        softmax, merged in warp order), a = cast(out)               (CTA per unit)
+//   G2   Po = W_out . a                                             (warp units)
+//   R2   per stream: x' = cast(x + cast(sum_k Po)), z = norm2(x')    (CTA per stream)
+//   G3   Pg = W_gateup . z                                          (warp units)
+//   R3   act = cast(silu(cast(sum_k Pg[2f])) cast(sum_k Pg[2f+1]))  (elementwise)
+//   G4   Pd = W_down . act                                          (warp units)
+//   R1   per stream: x = cast(x' + cast(sum_k Pd)), hidden[l] = x, then norm1
+//        of layer l+1 or, after the last layer, the final norm and score
+//
+// The math and cast points are the reference step's (reference
+// src/cpu/Cpu.cpp:59-141); only the summation order of the dot products
+// differs from the one-stream path. Every K-split partial is written to its
+// own slot and summed in split order, so a round is deterministic.
+//
+// GEMM warp unit: 64 weight rows (two per lane) x 32 streams over one K
+// range; the lane keeps its two rows' weights in registers for 8 columns at a
+// time and the streams' inputs arrive as uniform (broadcast) 16-byte loads,
+// so each weight element feeds 32 FMAs. Data written inside the launch by
+// other CTAs (inputs, partials, residuals) is read through L2 (ld.cg); only
+// weights take the read-only path.
+#pragma once
+
+#include "st_step.cuh"
+#include "st_umma.cuh"
+
+namespace st {
+
+constexpr int kBatchStreams = 32;     // streams per GEMM warp unit
+constexpr int kBatchRows = 64;        // weight rows per GEMM warp unit (two per lane)
+constexpr int kBatchMaxHeadDim = 256; // attention unit: head_dim <= 256 (4 dim pairs per lane)
+
+// How the GEMM reads W[m][k] from the weight slab.
+enum BatchView : int {
+  kViewRows = 0,      // W[m * K + k] (q/k/v fused [3d, d], gate/up interleaved [2F, d])
+  kViewOutHeads = 1,  // out projection stored per head [H][d][hd]: W[(k / hd) * d * hd + m * hd + k % hd]
+  kViewColumns = 2    // W_down stored transposed [F][d]: W[k * M + m]
+};
+
+// Attention units run four at a time per CTA, one per group of four warps.
+constexpr int kAttGroups = 4;
+constexpr int kAttWarps = kWarps / kAttGroups;
+constexpr int kAttThreads = kAttWarps * 32;
+
+struct AttSmem {
+  float q[kBatchMaxHeadDim];                      // rotated, cast q, k, v of the unit
+  float k[kBatchMaxHeadDim];
+  float v[kBatchMaxHeadDim];
+  float part_m[kAttWarps];                        // per-warp softmax partials
+  float part_l[kAttWarps];
+  float part_acc[kAttWarps][kBatchMaxHeadDim];
+};
+
+struct BatchSmem {
+  float red[kWarps];                              // block reductions (16-byte aligned)
+  union {
+    AttSmem att[kAttGroups];                      // attention phase
+    float zt[kWarps][kBatchStreams * 8];          // GEMM phases: each warp's stream-input tile
+    float xs[kMaxCols];                           // row phases: per-stream input vector
+  } u;
+  int tl_n;                                       // timeline marks recorded (diagnostics)
+  // tensor-core GEMM pipeline (kTc rounds)
+  unsigned long long tc_full[8];                  // stage landed (bulk-copy bytes)
+  unsigned long long tc_empty[8];                 // stage consumed (MMA commit)
+  unsigned long long tc_tfull;                    // unit's accumulator complete (MMA commit)
+  unsigned long long tc_tempty;                   // unit's accumulator read (4 epilogue warps)
+  unsigned long long tc_done;                     // every MMA issued has completed (teardown)
+  unsigned tc_tmem;                               // tensor-memory base address
+};
+constexpr int kTcMaxStages = 8;
+constexpr int kTcProducer = kThreads - 32;        // lane 0 of the last warp: bulk copies
+constexpr int kTcIssuer = kThreads - 64;          // lane 0 of the next-to-last warp: MMAs
+constexpr unsigned kTcTileBytes = kUmmaM * kTileK * 2;  // one 128 x 64 16-bit A tile
+constexpr int kTcMaxN = 256;                      // streams per MMA (N)
+
+// Diagnostics: thread 0 of the timeline CTA records clock64() << 8 | tag at
+// every phase end and barrier exit (warp 0's row of the timeline buffer).
+enum BatchTag : int {
+  kBtlInput = 40, kBtlQkv = 41, kBtlAttention = 42, kBtlOut = 43, kBtlResidual2 = 44, kBtlGateUp = 45,
+  kBtlSwiglu = 46, kBtlDown = 47, kBtlResidual1 = 48, kBtlSync = 49
+};
+__device__ __forceinline__ void btl(const StepArgs& a, BatchSmem& sm, int tag) {
+  if (a.timeline && blockIdx.x == a.timeline_cta && threadIdx.x == 0 && sm.tl_n < a.timeline_capacity / kWarps)
+    a.timeline[sm.tl_n++] = (long long)((clock64() << 8) | (long long)tag);
+}
+
+// Round barriers per launch step: one after P0, eight per layer, none after
+// the last R1 (the next round's P0 of a stream runs on the CTA that did its R1).
+__host__ __device__ inline int round_barriers(int layers) { return 8 * layers; }
+
+// True when the batched round supports this model (host and device).
+__host__ __device__ inline bool batch_supported(int width, int heads, int ffn, int features) {
+  const int hd = heads > 0 ? width / heads : 0;
+  return width <= kMaxCols && features <= kMaxCols && hd % 8 == 0 && hd >= 8 && hd <= kBatchMaxHeadDim &&
+         width % 8 == 0 && ffn % 8 == 0;
+}
+
+__device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+// Stores element (stream s, column k) of the next GEMM's input: fp32 [S][K]
+// for the CUDA-core GEMM, or the storage type in the MMA's tiled B layout
+// for the tensor cores: one tile of all `spad` streams x 64 columns per K
+// chunk, so the B operand of streams [s0, s0 + N) in chunk c is one contiguous
+// run of N x 128 bytes.
+template <typename T, bool kTc>
+__device__ __forceinline__ void put_z(const StepArgs& a, int s, int k, int K, float v) {
+  if constexpr (kTc) Storage<T>::store((T*)a.bz16, umma_tile_offset((size_t)s, (size_t)k, (size_t)a.spad, (size_t)K / kTileK), v);
+  else a.bz[(size_t)s * K + k] = v;
+}
+
+// Two consecutive cache elements (K/V rows are 16-byte aligned, dim even).
+template <typename T> __device__ __forceinline__ float2 load2_cg(const T* p);
+template <> __device__ __forceinline__ float2 load2_cg<float>(const float* p) {
+  return __ldcg(reinterpret_cast<const float2*>(p));
+}
+template <> __device__ __forceinline__ float2 load2_cg<__half>(const __half* p) {
+  const unsigned u = __ldcg(reinterpret_cast<const unsigned*>(p));
+  return __half22float2(*reinterpret_cast<const __half2*>(&u));
+}
+template <> __device__ __forceinline__ float2 load2_cg<__nv_bfloat16>(const __nv_bfloat16* p) {
+  const unsigned u = __ldcg(reinterpret_cast<const unsigned*>(p));
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
+// Raw (not yet widened) weights of a lane's two rows for 8 columns. (Loading
+// them a step ahead as well spills at 128 registers; the warps of the SM hide
+// their latency instead.)
+template <typename T> struct RawBits { using U = unsigned short; };
+template <> struct RawBits<float> { using U = float; };
+__device__ __forceinline__ float widen(float v, float*) { return v; }
+__device__ __forceinline__ float widen(unsigned short v, __nv_bfloat16*) { return __uint_as_float((unsigned)v << 16); }
+__device__ __forceinline__ float widen(unsigned short v, __half*) { return __half2float(__ushort_as_half(v)); }
+
+template <typename T, int kView>
+struct WeightPair {
+  static constexpr int kVecs = sizeof(T) == 4 ? 2 : 1;  // 16-byte vectors per 8 columns
+  uint4 vec[2][kVecs];                                // kViewRows / kViewOutHeads
+  typename RawBits<T>::U col[2][8];                   // kViewColumns
+
+  __device__ __forceinline__ const T* row_ptr(const T* W, int M, int K, int hd, int m, int k) const {
+    return kView == kViewRows ? W + (size_t)m * K + k : W + ((size_t)(k / hd) * M + m) * hd + (k % hd);
+  }
+  __device__ __forceinline__ void load(const T* W, int M, int K, int hd, const int (&m)[2], int k,
+                                       const bool (&ok)[2]) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      if constexpr (kView == kViewColumns) {
+        const typename RawBits<T>::U* p = reinterpret_cast<const typename RawBits<T>::U*>(W) + (size_t)k * M + m[r];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) col[r][u] = ok[r] ? __ldg(p + (size_t)u * M) : (typename RawBits<T>::U)0;
+      } else {
+        const uint4* p = reinterpret_cast<const uint4*>(row_ptr(W, M, K, hd, m[r], k));
+#pragma unroll
+        for (int v = 0; v < kVecs; ++v) vec[r][v] = ok[r] ? __ldg(p + v) : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+  }
+  __device__ __forceinline__ void widen_to(float (&w)[2][8]) const {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      if constexpr (kView == kViewColumns) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) w[r][u] = widen(col[r][u], (T*)nullptr);
+      } else {
+#pragma unroll
+        for (int v = 0; v < kVecs; ++v) Storage<T>::unpack(vec[r][v], w[r] + v * Storage<T>::kVec);
+      }
+    }
+  }
+};
+
+// One warp unit: rows [m0, m0 + 64) x streams [s0, s0 + 32) over K range
+// [k0, k1) into P[ks][s][m] (P holds S x M floats per split). Lane i loads
+// stream s0+i's 8 inputs one step ahead (one coalesced load per step) and
+// stores them into the warp's shared tile; the FMAs read the tile with
+// broadcast loads.
+template <typename T, int kView>
+__device__ __forceinline__ void gemm_unit(const T* W, int M, int K, int hd, const float* Z, int S, float* P,
+                                          int m0, int k0, int k1, int s0, int ks, float* zt) {
+  const int lane = threadIdx.x & 31;
+  const int m[2] = {m0 + lane, m0 + 32 + lane};
+  const bool ok[2] = {m[0] < M, m[1] < M};
+  const int ns = min(kBatchStreams, S - s0);
+  const bool zl = lane < ns;
+  const float* zrow = Z + (size_t)(s0 + (zl ? lane : 0)) * K;
+  float acc0[kBatchStreams], acc1[kBatchStreams];
+#pragma unroll
+  for (int s = 0; s < kBatchStreams; ++s) acc0[s] = acc1[s] = 0.f;
+  float4 za = make_float4(0.f, 0.f, 0.f, 0.f), zc = za;
+  if (zl) {
+    za = ldcg4(zrow + k0);
+    zc = ldcg4(zrow + k0 + 4);
+  }
+  WeightPair<T, kView> wp;
+#pragma unroll 1
+  for (int k = k0; k < k1; k += 8) {
+    __syncwarp();  // every lane has finished reading the previous tile
+    reinterpret_cast<float4*>(zt + lane * 8)[0] = za;
+    reinterpret_cast<float4*>(zt + lane * 8)[1] = zc;
+    float w[2][8];
+    wp.load(W, M, K, hd, m, k, ok);
+    wp.widen_to(w);
+    __syncwarp();
+    if (k + 8 < k1 && zl) {
+      za = ldcg4(zrow + k + 8);
+      zc = ldcg4(zrow + k + 12);
+    }
+#pragma unroll
+    for (int s = 0; s < kBatchStreams; ++s) {
+      if (s < ns) {
+        const float4 a = reinterpret_cast<const float4*>(zt + s * 8)[0];
+        const float4 b = reinterpret_cast<const float4*>(zt + s * 8)[1];
+        const float zz[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          acc0[s] = fmaf(w[0][u], zz[u], acc0[s]);
+          acc1[s] = fmaf(w[1][u], zz[u], acc1[s]);
+        }
+      }
+    }
+  }
+  float* out = P + ((size_t)ks * S + s0) * M;
+#pragma unroll
+  for (int s = 0; s < kBatchStreams; ++s) {
+    if (s < ns) {
+      if (ok[0]) out[(size_t)s * M + m[0]] = acc0[s];
+      if (ok[1]) out[(size_t)s * M + m[1]] = acc1[s];
+    }
+  }
+}
+
+// P[ks][s][m] = sum over split ks's K range of W[m][k] Z[s][k], every unit
+// dealt to the grid's warps in turn.
+template <typename T, int kView>
+__device__ void gemm_phase(const StepArgs& a, BatchSmem& sm, const T* W, int M, int K, int ksplit, const float* Z,
+                           float* P) {
+  const int S = a.streams;
+  const int mblocks = (M + kBatchRows - 1) / kBatchRows, sgroups = (S + kBatchStreams - 1) / kBatchStreams;
+  const int kchunks = K / 8;
+  const int units = mblocks * ksplit * sgroups;
+  const int nwarps = (int)gridDim.x * kWarps;
+  for (int u = (int)blockIdx.x * kWarps + (int)(threadIdx.x >> 5); u < units; u += nwarps) {
+    const int mb = u % mblocks, rest = u / mblocks;
+    const int ks = rest % ksplit, sg = rest / ksplit;
+    int c0, c1;
+    split(kchunks, ks, ksplit, c0, c1);
+    gemm_unit<T, kView>(W, M, K, a.head_dim, Z, S, P, mb * kBatchRows, c0 * 8, c1 * 8, sg * kBatchStreams, ks,
+                        sm.u.zt[threadIdx.x >> 5]);
+  }
+}
+
+// Sum of the K-split partials of one output in split order; the loads of a
+// group of eight are issued together so they overlap in flight.
+__device__ __forceinline__ float sum_splits(const float* P, int ksplit, size_t stride) {
+  float v = 0.f;
+  for (int k0 = 0; k0 < ksplit; k0 += 8) {
+    float t[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) t[u] = k0 + u < ksplit ? __ldcg(P + (size_t)(k0 + u) * stride) : 0.f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (k0 + u < ksplit) v += t[u];
+  }
+  return v;
+}
+
+// Thread i of the CTA handles elements i and i + kThreads of a d-vector.
+constexpr int kRowPer = kMaxCols / kThreads;
+
+// RMSNorm of the CTA's row values xv of stream s (reference
+// src/cpu/Cpu.cpp:43-57) into the next GEMM input (cast), or, with `score_w`,
+// the final norm followed by the score head (no cast). Ends with a barrier.
+template <typename T, bool kTc>
+__device__ __forceinline__ void row_norm(const StepArgs& a, BatchSmem& sm, int s, const float (&xv)[kRowPer],
+                                         float ss, const T* gain, const T* score_w, float* score, float* score_out) {
+  const int d = a.width;
+  const float total = block_reduce_sum(ss, sm.red);
+  const float scale = 1.0f / sqrtf(total / (float)d + a.epsilon);
+  float acc = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowPer; ++c) {
+    const int i = (int)threadIdx.x + c * kThreads;
+    if (i < d) {
+      const float zi = Storage<T>::round(xv[c] * scale * Storage<T>::load(gain, i));
+      if (score_w) acc = fmaf(Storage<T>::load(score_w, i), zi, acc);
+      else put_z<T, kTc>(a, s, i, d, zi);
+    }
+  }
+  __syncthreads();  // the reduction slot is reused below and by the next unit
+  if (score_w) {
+    const float total_score = block_reduce_sum(acc, sm.red);
+    if (threadIdx.x == 0) {
+      *score = total_score;
+      if (score_out) *score_out = total_score;
+    }
+    __syncthreads();
+  }
+}
+
+// P0: x = cast(W_in e) for stream s (reference src/cpu/Cpu.cpp:64-66), then norm1 of layer 0.
+template <typename T, bool kTc>
+__device__ void row_input(const StepArgs& a, BatchSmem& sm, int s, const float* input) {
+  const int d = a.width, nf = a.features;
+  for (int i = threadIdx.x; i < nf; i += kThreads) sm.u.xs[i] = __ldcv(input + (size_t)s * nf + i);
+  __syncthreads();
+  const T* Win = (const T*)a.input_w;
+  float xv[kRowPer];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowPer; ++c) {
+    const int i = (int)threadIdx.x + c * kThreads;
+    xv[c] = 0.f;
+    if (i < d) {
+      float acc = 0.f;
+      for (int f = 0; f < nf; ++f) acc = fmaf(Storage<T>::load(Win, (size_t)i * nf + f), sm.u.xs[f], acc);
+      const float x = Storage<T>::round(acc);
+      a.bx[(size_t)s * d + i] = x;
+      xv[c] = x;
+      ss += x * x;
+    }
+  }
+  row_norm<T, kTc>(a, sm, s, xv, ss, (const T*)a.layer[0].norm1, nullptr, nullptr, nullptr);
+}
+
+// R1 / R2: out = cast(base + cast(sum_k P)) for stream s, then the next norm
+// (gain) into z, or the final norm and score when `final_`.
+template <typename T, bool kTc>
+__device__ void row_residual(const StepArgs& a, BatchSmem& sm, int s, const float* base, float* out, const float* P,
+                             int ksplit, float* hidden, const T* gain, bool final_, float* score_out) {
+  const int d = a.width;
+  const size_t stride = (size_t)a.streams * d;
+  float xv[kRowPer];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowPer; ++c) {
+    const int i = (int)threadIdx.x + c * kThreads;
+    xv[c] = 0.f;
+    if (i < d) {
+      const float t = Storage<T>::round(sum_splits(P + (size_t)s * d + i, ksplit, stride));
+      const float x = Storage<T>::round(__ldcg(base + (size_t)s * d + i) + t);
+      out[(size_t)s * d + i] = x;
+      if (hidden) hidden[i] = x;
+      xv[c] = x;
+      ss += x * x;
+    }
+  }
+  if (final_)
+    row_norm<T, kTc>(a, sm, s, xv, ss, (const T*)a.final_norm, (const T*)a.score_w, a.score + s, score_out);
+  else
+    row_norm<T, kTc>(a, sm, s, xv, ss, gain, nullptr, nullptr, nullptr);
+}
+
+// R3: act[s][f] = cast(silu(g) u) with g, u the cast gate/up sums
+// (reference src/cpu/Cpu.cpp:121-127), every element of every stream.
+template <typename T, bool kTc>
+__device__ void swiglu_phase(const StepArgs& a, int ksplit) {
+  const int F = a.ffn, S = a.streams;
+  const size_t n = (size_t)S * F, stride = (size_t)S * 2 * F;
+  for (size_t e = (size_t)blockIdx.x * kThreads + threadIdx.x; e < n; e += (size_t)gridDim.x * kThreads) {
+    const size_t s = e / F, f = e - s * F;
+    const float* P = a.bpart + s * 2 * F + 2 * f;
+    const float g = Storage<T>::round(sum_splits(P, ksplit, stride));
+    const float u = Storage<T>::round(sum_splits(P + 1, ksplit, stride));
+    put_z<T, kTc>(a, (int)s, (int)f, F, Storage<T>::round((g / (1.0f + expf(-g))) * u));
+  }
+}
+
+// q . K_j over head_dim, K row from the cache (16-byte loads through L2).
+template <typename T>
+__device__ __forceinline__ float dot_cache_row(const T* krow, const float* q, int hd) {
+  constexpr int V = Storage<T>::kVec;
+  float acc = 0.f;
+  for (int e = 0; e < hd; e += V) {
+    float f[V];
+    Storage<T>::unpack(__ldcg(reinterpret_cast<const uint4*>(krow + e)), f);
+#pragma unroll
+    for (int u = 0; u < V; ++u) acc = fmaf(q[e + u], f[u], acc);
+  }
+  return acc;
+}
+
+// Barrier of one attention group (named barrier 1 + group, kAttThreads threads).
+__device__ __forceinline__ void group_sync(int group) {
+  asm volatile("bar.sync %0, %1;" ::"r"(group + 1), "r"(kAttThreads) : "memory");
+}
+
+// A: stream s, head h of layer l (reference src/cpu/Cpu.cpp:72-111), run by
+// one group of kAttWarps warps (`gt` = thread index within the group).
+template <typename T, bool kTc>
+__device__ void attention_unit(const StepArgs& a, AttSmem& sm, int group, int l, int s, int h,
+                               unsigned long long event, int ksplit) {
+  const int hd = a.head_dim, W = a.window, d = a.width, M = 3 * d, S = a.streams;
+  const int gt = (int)threadIdx.x - group * kAttThreads;
+  const int lane = gt & 31, warp = gt >> 5;
+  const unsigned long long t = __ldcg(a.position + s) + event;
+  const int slot = (int)(t % (unsigned long long)W);
+  const int valid = valid_length(t, W);
+  const size_t head_base = ((((size_t)s * a.layers + l) * a.heads + h) * (size_t)W) * hd;
+  T* keys = (T*)a.keys + head_base;
+  T* values = (T*)a.values + head_base;
+  // q, k, v of head h: sums of the split partials, cast, RoPE on q and k in
+  // adjacent pairs with angle float(t) * 10000^(-i/hd), cast (reference
+  // src/cpu/Cpu.cpp:76-89), and the K/V insert at slot t % W.
+  const float* P = a.bpart + (size_t)s * M + (size_t)h * 3 * hd;
+  const size_t stride = (size_t)S * M;
+  const float tf = (float)t;
+  for (int p = gt; p < 3 * hd / 2; p += kAttThreads) {
+    const int row = 2 * p, which = row / hd, dim = row - which * hd;
+    float v0 = Storage<T>::round(sum_splits(P + row, ksplit, stride));
+    float v1 = Storage<T>::round(sum_splits(P + row + 1, ksplit, stride));
+    if (which < 2) {
+      const float angle = tf * a.rope_freq[dim >> 1];
+      const float c = cosf(angle), sn = sinf(angle);
+      const float r0 = v0 * c - v1 * sn;
+      const float r1 = v0 * sn + v1 * c;
+      v0 = Storage<T>::round(r0);
+      v1 = Storage<T>::round(r1);
+    }
+    float* dst = which == 0 ? sm.q : which == 1 ? sm.k : sm.v;
+    dst[dim] = v0;
+    dst[dim + 1] = v1;
+    if (which > 0) {
+      T* ring = which == 1 ? keys : values;
+      Storage<T>::store(ring, (size_t)slot * hd + dim, v0);
+      Storage<T>::store(ring, (size_t)slot * hd + dim + 1, v1);
+    }
+  }
+  group_sync(group);
+  // Each warp: slots [j0, j1), one slot per lane per pass, online softmax;
+  // the current slot's key and value come from shared memory.
+  int j0, j1;
+  split(valid, warp, kAttWarps, j0, j1);
+  const float root = sqrtf((float)hd);
+  const int pairs = hd / 2;
+  constexpr int kPairRegs = kBatchMaxHeadDim / 64;
+  float m = -INFINITY, lsum = 0.f;
+  float acc[kPairRegs][2];
+#pragma unroll
+  for (int c = 0; c < kPairRegs; ++c) acc[c][0] = acc[c][1] = 0.f;
+  for (int c0 = j0; c0 < j1; c0 += 32) {
+    const int j = c0 + lane;
+    float lg = -INFINITY;
+    if (j < j1) {
+      float dot = 0.f;
+      if (j == slot) {
+        for (int i = 0; i < hd; ++i) dot = fmaf(sm.q[i], sm.k[i], dot);
+      } else {
+        dot = dot_cache_row<T>(keys + (size_t)j * hd, sm.q, hd);
+      }
+      lg = dot / root;
+    }
+    const float mn = fmaxf(m, warp_max(lg));
+    const float sc = expf(m - mn);
+    const float p = j < j1 ? expf(lg - mn) : 0.f;
+    lsum = lsum * sc + warp_sum(p);
+#pragma unroll
+    for (int c = 0; c < kPairRegs; ++c) {
+      acc[c][0] *= sc;
+      acc[c][1] *= sc;
+    }
+    const int n = min(32, j1 - c0);
+#pragma unroll 8
+    for (int jj = 0; jj < n; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, p, jj);
+      const int row = c0 + jj;
+#pragma unroll
+      for (int c = 0; c < kPairRegs; ++c) {
+        const int pi = lane + 32 * c;
+        if (pi < pairs) {
+          const float2 v = row == slot ? make_float2(sm.v[2 * pi], sm.v[2 * pi + 1])
+                                       : load2_cg<T>(values + (size_t)row * hd + 2 * pi);
+          acc[c][0] = fmaf(pj, v.x, acc[c][0]);
+          acc[c][1] = fmaf(pj, v.y, acc[c][1]);
+        }
+      }
+    }
+    m = mn;
+  }
+  if (lane == 0) {
+    sm.part_m[warp] = m;
+    sm.part_l[warp] = lsum;
+  }
+#pragma unroll
+  for (int c = 0; c < kPairRegs; ++c) {
+    const int pi = lane + 32 * c;
+    if (pi < pairs) {
+      sm.part_acc[warp][2 * pi] = acc[c][0];
+      sm.part_acc[warp][2 * pi + 1] = acc[c][1];
+    }
+  }
+  group_sync(group);
+  // merge the warps' partials in warp order, cast (reference src/cpu/Cpu.cpp:105-111)
+  for (int i = gt; i < hd; i += kAttThreads) {
+    float mx = -INFINITY;
+    for (int w = 0; w < kAttWarps; ++w)
+      if (sm.part_l[w] > 0.f) mx = fmaxf(mx, sm.part_m[w]);
+    float L = 0.f, o = 0.f;
+    for (int w = 0; w < kAttWarps; ++w) {
+      if (sm.part_l[w] > 0.f) {
+        const float e = expf(sm.part_m[w] - mx);
+        L = fmaf(sm.part_l[w], e, L);
+        o = fmaf(sm.part_acc[w][i], e, o);
+      }
+    }
+    put_z<T, kTc>(a, s, h * hd + i, d, Storage<T>::round(o / L));
+  }
+  group_sync(group);  // the next unit of this group overwrites q, k, v and the partials
+}
+
+// The attention phase: units (stream, head) dealt to the grid's groups in turn.
+template <typename T, bool kTc>
+__device__ void attention_phase(const StepArgs& a, BatchSmem& sm, int l, unsigned long long event) {
+  const int group = (int)threadIdx.x / kAttThreads;
+  const int units = a.streams * a.heads;
+  for (int u = (int)blockIdx.x * kAttGroups + group; u < units; u += (int)gridDim.x * kAttGroups)
+    attention_unit<T, kTc>(a, sm.u.att[group], group, l, u / a.heads, u % a.heads, event, a.bsplit[0]);
+}
+
+// ---------------------------------------------------------------- tensor-core GEMM phase
+// Per-thread pipeline counters of the roles below; they persist across the
+// GEMM phases, layers and rounds of one launch (every role thread walks the
+// same unit sequence).
+struct TcRoles {
+  unsigned long long issued = 0;    // producer: chunks issued
+  unsigned long long consumed = 0;  // MMA issuer: chunks consumed
+  unsigned long long units = 0;     // every thread: units walked
+  bool failed = false;
+};
+
+// P[ks][s][m] = sum over split ks's K chunks of W[m][k] z[s][k] on the tensor
+// cores. A unit is (128-row tile, K split, group of up to 256 streams): the
+// producer thread copies each 64-column chunk's A tile (16 KB of pre-tiled
+// weights) and B tile (the streams' inputs, N x 128 bytes) into a stage with
+// one mbarrier completion; the issuer thread runs four 128 x N x 16 MMAs per
+// chunk into the unit's tensor-memory accumulator and frees the stage with a
+// commit; warps 0-3 read the accumulator (32 rows each) and store the
+// partials. Every wait is bounded; a timeout sets the error word.
+template <typename T>
+__device__ void tc_gemm_phase(const StepArgs& a, BatchSmem& sm, unsigned char* stages, TcRoles& tr, const T* Wt,
+                              int M, int K, int ksplit, float* P) {
+  const int S = a.streams, spad = a.spad;
+  const int mtiles = (M + kUmmaM - 1) / kUmmaM, kchunks = K / kTileK;
+  const int sgroups = (spad + kTcMaxN - 1) / kTcMaxN;
+  const int units = mtiles * ksplit * sgroups;
+  const int warp = (int)threadIdx.x >> 5, lane = (int)threadIdx.x & 31;
+  const T* Bt = (const T*)a.bz16;
+  const unsigned long long tmo = a.bar_timeout_ns;
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const int mt = u % mtiles, rest = u / mtiles, ks = rest % ksplit, sg = rest / ksplit;
+    int c0, c1;
+    split(kchunks, ks, ksplit, c0, c1);
+    const int s0 = sg * kTcMaxN, n = min(kTcMaxN, spad - s0);
+    if (threadIdx.x == kTcProducer) {
+      const unsigned long long wpol = policy_evict_first(), zpol = policy_evict_last();
+      for (int kc = c0; kc < c1 && !tr.failed; ++kc) {
+        const int st = (int)(tr.issued % (unsigned long long)a.tc_stages);
+        const unsigned long long r = tr.issued / (unsigned long long)a.tc_stages;
+        if (r > 0 && !mbar_wait_bounded(&sm.tc_empty[st], (unsigned)((r - 1) & 1ull), tmo)) {
+          tr.failed = true;
+          set_error(a, kBarrierTimeout);
+          break;
+        }
+        unsigned char* sa = stages + (size_t)st * a.tc_stage_bytes;
+        mbar_expect_tx(&sm.tc_full[st], kTcTileBytes + (unsigned)n * kCoreBytes);
+        bulk_copy(sa, Wt + ((size_t)mt * kchunks + kc) * (kUmmaM * kTileK), kTcTileBytes, &sm.tc_full[st], wpol);
+        bulk_copy(sa + kTcTileBytes, Bt + ((size_t)kc * spad + s0) * kTileK, (unsigned)n * kCoreBytes,
+                  &sm.tc_full[st], zpol);
+        tr.issued += 1;
+      }
+    } else if (threadIdx.x == kTcIssuer) {
+      if (!tr.failed && tr.units > 0 && !mbar_wait_bounded(&sm.tc_tempty, (unsigned)((tr.units - 1) & 1ull), tmo)) {
+        tr.failed = true;
+        set_error(a, kBarrierTimeout);
+      }
+      tc_fence_after();
+      const unsigned idesc = umma_idesc<T>(kUmmaM, n);
+      for (int kc = c0; kc < c1 && !tr.failed; ++kc) {
+        const int st = (int)(tr.consumed % (unsigned long long)a.tc_stages);
+        const unsigned long long r = tr.consumed / (unsigned long long)a.tc_stages;
+        if (!mbar_wait_bounded(&sm.tc_full[st], (unsigned)(r & 1ull), tmo)) {
+          tr.failed = true;
+          set_error(a, kBarrierTimeout);
+          break;
+        }
+        tc_fence_after();
+        const unsigned char* sa = stages + (size_t)st * a.tc_stage_bytes;
+#pragma unroll
+        for (int kk = 0; kk < kTileK / kUmmaK; ++kk)
+          umma_f16(sm.tc_tmem, umma_desc(sa + kk * 2 * kCoreBytes), umma_desc(sa + kTcTileBytes + kk * 2 * kCoreBytes),
+                   idesc, (kc > c0 || kk > 0) ? 1u : 0u);
+        umma_commit(&sm.tc_empty[st]);
+        tr.consumed += 1;
+      }
+      umma_commit(&sm.tc_tfull);
+    } else if (warp < 4) {
+      bool ok = !tr.failed && mbar_wait_bounded(&sm.tc_tfull, (unsigned)(tr.units & 1ull), tmo);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        const int m = mt * kUmmaM + warp * 32 + lane;
+        float* out = P + ((size_t)ks * S + s0) * M;
+        const int live = min(n, S - s0);
+        for (int c = 0; c < n; c += 16) {
+          float v[16];
+          tmem_ld16(sm.tc_tmem + ((unsigned)(warp * 32) << 16) + (unsigned)c, v);
+          if (m < M)
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (c + j < live) out[(size_t)(c + j) * M + m] = v[j];
+        }
+        tc_fence_before();
+      } else if (lane == 0 && !tr.failed) {
+        set_error(a, kBarrierTimeout);
+      }
+      if (!ok) tr.failed = true;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.tc_tempty);
+    }
+    tr.units += 1;
+  }
+}
+
+// Kernel start (kTc): mbarriers, tensor-memory allocation (warp 0).
+__device__ inline void tc_setup(const StepArgs& a, BatchSmem& sm) {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.tc_stages; ++i) {
+      mbar_init(&sm.tc_full[i], 1);
+      mbar_init(&sm.tc_empty[i], 1);
+    }
+    mbar_init(&sm.tc_tfull, 1);
+    mbar_init(&sm.tc_tempty, 4);
+    mbar_init(&sm.tc_done, 1);
+    fence_mbar_init();
+  }
+  if (threadIdx.x < 32) {
+    tmem_alloc(&sm.tc_tmem, a.tc_ncols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+}
+
+// Kernel end (kTc), reached on every path: every MMA issued has completed,
+// every bulk copy issued has landed, then warp 0 frees the tensor memory.
+__device__ inline void tc_teardown(const StepArgs& a, BatchSmem& sm, const TcRoles& tr) {
+  __syncthreads();
+  if (threadIdx.x == kTcIssuer) {
+    umma_commit(&sm.tc_done);
+    if (!mbar_wait_bounded(&sm.tc_done, 0u, a.bar_timeout_ns)) set_error(a, kBarrierTimeout);
+  }
+  if (threadIdx.x == kTcProducer) {
+    const unsigned long long n = tr.issued, stages = (unsigned long long)a.tc_stages;
+    for (unsigned long long c = n > stages ? n - stages : 0; c < n; ++c)
+      if (!mbar_wait_bounded(&sm.tc_full[c % stages], (unsigned)((c / stages) & 1ull), a.bar_timeout_ns)) {
+        set_error(a, kBarrierTimeout);
+        break;
+      }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x < 32) tmem_dealloc(sm.tc_tmem, a.tc_ncols);
+}
+
+// One GEMM phase on the CUDA cores or the tensor cores.
+template <typename T, bool kTc, int kView>
+__device__ __forceinline__ void gemm_any(const StepArgs& a, BatchSmem& sm, unsigned char* stages, TcRoles& tr,
+                                         const void* W, const void* Wt, int M, int K, int ksplit) {
+  if constexpr (kTc) tc_gemm_phase<T>(a, sm, stages, tr, (const T*)Wt, M, K, ksplit, a.bpart);
+  else gemm_phase<T, kView>(a, sm, (const T*)W, M, K, ksplit, a.bz, a.bpart);
+}
+
+// One round (event `event` of this launch) for every stream. `input` is
+// [S][features]; scores go to a.score and, when given, score_out[S].
+template <typename T, bool kTc>
+__device__ bool round_batched(const StepArgs& a, BatchSmem& sm, unsigned char* stages, TcRoles& tr, GridSync& gs,
+                              const float* input, unsigned long long event, float* score_out) {
+  const int S = a.streams, d = a.width, F = a.ffn, L = a.layers;
+  auto sync = [&](int tag) {
+    btl(a, sm, tag);
+    const bool ok = gs.sync(a, a.bar_timeout_ns);
+    btl(a, sm, kBtlSync);
+    return ok;
+  };
+  for (int s = blockIdx.x; s < S; s += gridDim.x) row_input<T, kTc>(a, sm, s, input);
+  if (!sync(kBtlInput)) return false;
+  for (int l = 0; l < L; ++l) {
+    const LayerPtrs& w = a.layer[l];
+    gemm_any<T, kTc, kViewRows>(a, sm, stages, tr, w.qkv, a.tqkv[l], 3 * d, d, a.bsplit[0]);
+    if (!sync(kBtlQkv)) return false;
+    attention_phase<T, kTc>(a, sm, l, event);
+    if (!sync(kBtlAttention)) return false;
+    gemm_any<T, kTc, kViewOutHeads>(a, sm, stages, tr, w.out, a.tout[l], d, d, a.bsplit[1]);
+    if (!sync(kBtlOut)) return false;
+    for (int s = blockIdx.x; s < S; s += gridDim.x)
+      row_residual<T, kTc>(a, sm, s, a.bx, a.bx2, a.bpart, a.bsplit[1], nullptr, (const T*)w.norm2, false, nullptr);
+    if (!sync(kBtlResidual2)) return false;
+    gemm_any<T, kTc, kViewRows>(a, sm, stages, tr, w.gateup, a.tgateup[l], 2 * F, d, a.bsplit[2]);
+    if (!sync(kBtlGateUp)) return false;
+    swiglu_phase<T, kTc>(a, a.bsplit[2]);
+    if (!sync(kBtlSwiglu)) return false;
+    gemm_any<T, kTc, kViewColumns>(a, sm, stages, tr, w.down, a.tdown[l], d, F, a.bsplit[3]);
+    if (!sync(kBtlDown)) return false;
+    const bool last = l + 1 == L;
+    for (int s = blockIdx.x; s < S; s += gridDim.x)
+      row_residual<T, kTc>(a, sm, s, a.bx2, a.bx, a.bpart, a.bsplit[3], a.hidden + ((size_t)s * L + l) * d,
+                           last ? nullptr : (const T*)a.layer[l + 1].norm1, last, score_out ? score_out + s : nullptr);
+    if (last) btl(a, sm, kBtlResidual1);
+    else if (!sync(kBtlResidual1)) return false;
+  }
+  return true;
+}
+
+// `count` rounds over inputs [count][S][features] (scores [count][S] when
+// given); positions advance by `count` at the end, each stream's by the CTA
+// that ran its last R1. kTc: the GEMM phases run on the tensor cores, with
+// the pipeline stages in dynamic shared memory.
+template <typename T, bool kTc>
+__device__ void batched_rounds(const StepArgs& a, const float* inputs, unsigned long long count, float* scores,
+                               unsigned long long base) {
+  __shared__ BatchSmem sm;
+  extern __shared__ __align__(1024) unsigned char tc_stage_smem[];
+  if (threadIdx.x == 0) sm.tl_n = 0;
+  TcRoles tr;
+  if constexpr (kTc) tc_setup(a, sm);
+  GridSync gs{base, 0};
+  const size_t stride = (size_t)a.streams * a.features;
+  bool ok = true;
+  for (unsigned long long e = 0; e < count && ok; ++e)
+    ok = round_batched<T, kTc>(a, sm, tc_stage_smem, tr, gs, inputs + e * stride, e,
+                               scores ? scores + e * a.streams : nullptr);
+  if (ok && threadIdx.x == 0)
+    for (int s = blockIdx.x; s < a.streams; s += gridDim.x) a.position[s] = __ldcg(a.position + s) + count;
+  if constexpr (kTc) tc_teardown(a, sm, tr);
+}
+
+}  // namespace st

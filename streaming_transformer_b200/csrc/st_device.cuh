@@ -87,6 +87,22 @@ struct StepArgs {
   int l2_keep_layers;                 // layers whose weights are kept L2-resident (weight ring)
   int cluster_size;                   // CTAs per cluster the buffers were sized for
   int clusters;                       // clusters in the grid (sizes dpart)
+  // batched round (all streams per pass over the weights)
+  float* bx;                          // [S][d] residual x
+  float* bx2;                         // [S][d] residual x'
+  float* bz;                          // [S][K] input of the next GEMM phase (K = d or F)
+  float* bpart;                       // [split][S][rows] K-split partials of the last GEMM phase
+  int bsplit[4];                      // K-splits of the q/k/v, out, gate/up and down GEMMs
+  // batched round on the tensor cores (16-bit modes)
+  const void* tqkv[kMaxLayers];       // weights pre-tiled for the MMA (128-row x 64-column core-matrix tiles)
+  const void* tout[kMaxLayers];
+  const void* tgateup[kMaxLayers];
+  const void* tdown[kMaxLayers];
+  void* bz16;                         // next GEMM input, storage type, tiled [K/64][spad/8][8][8][8]
+  int spad;                           // streams rounded up to 16 (MMA N granularity)
+  int tc_stages;                      // shared-memory stages of the MMA pipeline
+  unsigned tc_stage_bytes;            // bytes per stage: A tile 16 KB + B tile (<= 256 streams x 128 B)
+  unsigned tc_ncols;                  // tensor-memory columns allocated (power of two >= 32)
 };
 
 // ---------------------------------------------------------------- storage types

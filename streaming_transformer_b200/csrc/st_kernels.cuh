@@ -10,6 +10,7 @@
 // src/cuda/Runtime.cu:16-132).
 #pragma once
 
+#include "st_batch.cuh"
 #include "st_step.cuh"
 
 namespace st {
@@ -239,6 +240,16 @@ __global__ void __launch_bounds__(kThreads, 1) k2_persistent(StepArgs a, Persist
   gs.sync(a, a.bar_timeout_ns, &sm.sync_ok);
   ring_drain(a, rg, rs);
   persistent_exit<T>(a, p);
+}
+
+// Batched rounds (st_batch.cuh): one CTA per SM, no clusters, `count` events
+// of every stream, inputs [count][S][features] in device memory, scores
+// [count][S] when given; kTc runs the GEMM phases on the tensor cores (16-bit
+// modes). Steps of a batched runtime launch it with count 1.
+template <typename T, bool kTc>
+__global__ void __launch_bounds__(kThreads, 1) k3_rounds(StepArgs a, const float* inputs, unsigned long long count,
+                                                        float* scores, unsigned long long base) {
+  batched_rounds<T, kTc>(a, inputs, count, scores, base);
 }
 
 }  // namespace st

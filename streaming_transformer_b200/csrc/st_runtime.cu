@@ -29,6 +29,7 @@
 #include <sstream>
 #include <string>
 #include <thread>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/streaming_b200.h"
@@ -53,6 +54,10 @@ struct TensorSlot {
   int rows, cols;     // logical tensor shape (1-D tensors: rows = 1)
   int kind, p0, p1;   // LayoutKind and its parameters
   int index;          // presence flag index
+  // Tensor-core copy (batched round, 16-bit modes): the GEMM matrix this
+  // tensor belongs to, pre-tiled for the MMA; tiled_rows = 0 when none.
+  size_t tiled_offset = 0;
+  int tiled_rows = 0, tiled_cols = 0;
 };
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -107,6 +112,22 @@ __global__ void k_convert(const float* src, T* dst, int rows, int cols, int kind
   }
 }
 
+// The tensor-core copy of one checkpoint tensor: element (r, c) goes to row m,
+// column k of its GEMM matrix (q/k/v fused head-major [3d, d], out [d, d],
+// gate/up interleaved [2F, d], down [d, F]) in the MMA's tiled layout
+// (umma_tile_offset, 128-row tiles).
+template <typename T>
+__global__ void k_convert_tiled(const float* src, T* dst, int rows, int cols, int kind, int p0, int p1, int gemm_cols) {
+  const size_t n = (size_t)rows * cols;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / cols, c = i - r * cols;
+    size_t m = r;
+    if (kind == kQkvHead) m = ((r / p1) * 3 + p0) * p1 + r % p1;
+    else if (kind == kPlain) m = r * p0 + p1;
+    Storage<T>::store(dst, umma_tile_offset(m, c, kUmmaM, (size_t)gemm_cols / kTileK), src[i]);
+  }
+}
+
 }  // namespace
 
 struct st_runtime {
@@ -127,6 +148,16 @@ struct st_runtime {
   // (st_ring.cuh) when the configuration allows it (ring_supported); the
   // environment variable ST_WEIGHT_RING=0 selects the direct-load variants.
   bool ring = false;
+  // Several streams step together through the batched round (st_batch.cuh):
+  // one CTA per SM, every weight read once per round for all streams. Chosen
+  // for 4 or more streams when the model allows it; ST_BATCHED=0/1 overrides.
+  bool batched = false;
+  bool tc = false;        // batched GEMM phases on the tensor cores (16-bit modes)
+  int bgrid = 0;
+  int bsplit[4] = {1, 1, 1, 1};
+  size_t tc_smem = 0;     // dynamic shared memory of the tensor-core rounds kernel
+  char* tweights = nullptr;
+  size_t tweights_bytes = 0;
   size_t elem = 4;
   cudaStream_t stream = nullptr;
   cudaStream_t aux = nullptr;
@@ -210,6 +241,10 @@ struct Kernels {
     return ring ? (const void*)k2_persistent<T, true> : (const void*)k2_persistent<T, false>;
   }
   static const void* convert() { return (const void*)k_convert<T>; }
+  static const void* rounds(bool tc) {
+    if constexpr (std::is_same<T, float>::value) return (const void*)k3_rounds<T, false>;  // fp32: CUDA cores only
+    else return tc ? (const void*)k3_rounds<T, true> : (const void*)k3_rounds<T, false>;
+  }
 };
 
 #define ST_KERNEL(rt, name) \
@@ -226,6 +261,11 @@ struct Kernels {
                                      : Kernels<float>::trace((rt)->ring, true))
 
 const void* persistent_fn(const st_runtime* rt) { return ST_LOOP_KERNEL(rt, persistent); }
+const void* rounds_fn(const st_runtime* rt) {
+  if (rt->desc.mode == ST_MODE_FP16) return Kernels<__half>::rounds(rt->tc);
+  if (rt->desc.mode == ST_MODE_BF16) return Kernels<__nv_bfloat16>::rounds(rt->tc);
+  return Kernels<float>::rounds(false);
+}
 
 // Launch with this runtime's cluster shape. `cooperative` requests the
 // co-residency guarantee when coop_clusters is set (off: see st_runtime).
@@ -307,6 +347,18 @@ int launch_trace(st_runtime* rt, const StepArgs& a0, const float* inputs, unsign
   return ST_OK;
 }
 
+// `count` batched rounds over inputs [count][S][features] (device memory);
+// scores [count][S] may be null (a.score always holds the last round's).
+int launch_rounds(st_runtime* rt, const StepArgs& a0, const float* inputs, unsigned long long count, float* scores) {
+  StepArgs a = a0;
+  unsigned long long base = rt->bar_base;
+  void* params[] = {&a, &inputs, &count, &scores, &base};
+  ST_CUDA(rt, cudaLaunchKernel(rounds_fn(rt), dim3(rt->bgrid), dim3(kThreads), params, rt->tc_smem, rt->stream));
+  rt->launches += 1;
+  rt->bar_base += count * (unsigned long long)round_barriers(rt->desc.layers) * (unsigned long long)rt->bgrid;
+  return ST_OK;
+}
+
 // Host-side check of the error word mirrored into mapped memory.
 int check_device_error(st_runtime* rt) {
   const int e = __atomic_load_n(&rt->mb_h->error, __ATOMIC_ACQUIRE);
@@ -323,7 +375,7 @@ int check_device_error(st_runtime* rt) {
 int preload(st_runtime* rt) {
   const void* fns[] = {ST_KERNEL(rt, input), ST_KERNEL(rt, attention), ST_KERNEL(rt, ffn), ST_KERNEL(rt, final_),
                        ST_KERNEL(rt, reset), ST_LOOP_KERNEL(rt, fused), ST_LOOP_KERNEL(rt, trace), ST_LOOP_KERNEL(rt, persistent),
-                       ST_TIMELINE_KERNEL(rt), ST_KERNEL(rt, convert)};
+                       ST_TIMELINE_KERNEL(rt), ST_KERNEL(rt, convert), rounds_fn(rt)};
   for (const void* f : fns) {
     cudaFuncAttributes fa{};
     ST_CUDA(rt, cudaFuncGetAttributes(&fa, f));
@@ -430,7 +482,9 @@ int run_step_nonpersistent(st_runtime* rt) {
   const size_t out_bytes = (size_t)rt->desc.streams * sizeof(float);
   if (!rt->opt.mapped)
     ST_CUDA(rt, cudaMemcpyAsync(rt->dev_input, rt->in_h, in_bytes, cudaMemcpyHostToDevice, rt->stream));
-  if (rt->opt.backend == ST_BACKEND_GRAPH) {
+  if (rt->batched) {
+    ST_TRY(launch_rounds(rt, rt->args, rt->args.input, 1, nullptr));
+  } else if (rt->opt.backend == ST_BACKEND_GRAPH) {
     ST_CUDA(rt, cudaGraphLaunch(rt->graph_exec, rt->stream));
     rt->launches += sequence_launches(rt);
   } else if (rt->opt.backend == ST_BACKEND_FUSED) {
@@ -699,6 +753,71 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   const size_t part_at = take(S * m.heads * (size_t)nch * (hd + 2) * 4);
   const size_t act_at = take(S * F * 4), score_at = take(S * 4), input_at = take(S * m.features * 4);
   const size_t pout_at = take(S * m.heads * (size_t)d * 4), dpart_at = take(S * (size_t)rt->nclusters * d * 4);
+  // batched round: selection, grid (one CTA per SM) and K-splits. On the
+  // tensor cores (16-bit modes, d and F multiples of 64; ST_TC=0 disables) a
+  // GEMM unit is a 128-row tile x K split x up to 256 streams, and each phase
+  // gets about one unit per CTA. On the CUDA cores a unit is 64 rows x 32
+  // streams, about one per warp, with at most 16 splits. Splits never exceed
+  // one per 64 columns, and partials stay within 64 MB.
+  {
+    const char* env = std::getenv("ST_BATCHED");
+    bool want = S >= 4;
+    if (env && env[0] == '0') want = false;
+    if (env && env[0] == '1') want = true;
+    rt->batched = want && S >= 2 && batch_supported(d, m.heads, F, m.features);
+    const char* tenv = std::getenv("ST_TC");
+    rt->tc = rt->batched && m.mode != ST_MODE_FP32 && d % kTileK == 0 && F % kTileK == 0 && !(tenv && tenv[0] == '0');
+  }
+  const size_t spad = (S + 15) / 16 * 16;
+  size_t bpart_floats = 0;
+  if (rt->batched) {
+    rt->bgrid = rt->sms;
+    const size_t nmax = std::min<size_t>(spad, kTcMaxN);
+    if (rt->tc) {
+      const size_t stage = kTcTileBytes + nmax * kCoreBytes;
+      const int stages = (int)std::min<size_t>(kTcMaxStages, ((size_t)192 << 10) / stage);
+      rt->args.tc_stages = stages;
+      rt->args.tc_stage_bytes = (unsigned)stage;
+      rt->tc_smem = (size_t)stages * stage;
+      unsigned ncols = 32;
+      while (ncols < nmax) ncols *= 2;
+      rt->args.tc_ncols = ncols;
+      if (rt->cuda(cudaFuncSetAttribute(rounds_fn(rt), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rt->tc_smem),
+                   "cudaFuncSetAttribute rounds") != ST_OK)
+        return bail(ST_ERR_CUDA);
+    }
+    int occ = 0;
+    if (rt->cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, rounds_fn(rt), kThreads, rt->tc_smem),
+                 "cudaOccupancyMaxActiveBlocksPerMultiprocessor") != ST_OK)
+      return bail(ST_ERR_CUDA);
+    if (occ < 1) {
+      rt->fail(ST_ERR_UNSUPPORTED, "batched round kernel does not fit on an SM");
+      return bail(ST_ERR_UNSUPPORTED);
+    }
+    auto pick = [&](size_t M, size_t K) {
+      size_t units1, target;
+      if (rt->tc) {
+        units1 = ((M + kUmmaM - 1) / kUmmaM) * ((spad + kTcMaxN - 1) / kTcMaxN);
+        target = (size_t)rt->bgrid;
+      } else {
+        units1 = ((M + kBatchRows - 1) / kBatchRows) * ((S + kBatchStreams - 1) / kBatchStreams);
+        target = (size_t)rt->bgrid * kWarps;
+      }
+      size_t ks = (target + units1 - 1) / units1;
+      ks = std::min(ks, std::min(K / 64, (size_t)16));
+      while (ks > 1 && ks * S * M * 4 > ((size_t)64 << 20)) --ks;
+      ks = std::max(ks, (size_t)1);
+      bpart_floats = std::max(bpart_floats, ks * S * M);
+      return (int)ks;
+    };
+    rt->bsplit[0] = pick(3 * (size_t)d, d);
+    rt->bsplit[1] = pick(d, d);
+    rt->bsplit[2] = pick(2 * (size_t)F, d);
+    rt->bsplit[3] = pick(d, F);
+  }
+  const size_t bx_at = take(rt->batched ? S * d * 4 : 0), bx2_at = take(rt->batched ? S * d * 4 : 0);
+  const size_t bz_at = take(rt->batched && !rt->tc ? S * (size_t)std::max(d, F) * 4 : 0), bpart_at = take(bpart_floats * 4);
+  const size_t bz16_at = take(rt->tc ? spad * (size_t)std::max(d, F) * 2 : 0);
   const size_t bar_at = take(sizeof(unsigned long long)), err_at = take(sizeof(int));
   const size_t rope_at = take((hd / 2) * sizeof(float)), ctl_at = take(sizeof(Control));
   rt->scratch_bytes = co;
@@ -763,6 +882,54 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   a.bar_timeout_ns = 2ull * 1000000000ull;
   a.cluster_size = rt->cluster;
   a.clusters = rt->nclusters;
+  if (rt->batched) {
+    a.bx = (float*)(rt->scratch + bx_at);
+    a.bx2 = (float*)(rt->scratch + bx2_at);
+    a.bz = (float*)(rt->scratch + bz_at);
+    a.bpart = (float*)(rt->scratch + bpart_at);
+    for (int i = 0; i < 4; ++i) a.bsplit[i] = rt->bsplit[i];
+    a.spad = (int)spad;
+  }
+  if (rt->tc) {
+    // The tensor-core copy of the layer matrices, rows padded to 128 (zeros).
+    a.bz16 = rt->scratch + bz16_at;
+    auto pad = [](size_t rows) { return (rows + kUmmaM - 1) / kUmmaM * kUmmaM; };
+    size_t to = 0;
+    auto matrix = [&](size_t rows, size_t cols) {
+      const size_t at = to;
+      to = align_up(to + pad(rows) * cols * 2, 256);
+      return at;
+    };
+    std::vector<size_t> tq(L), tout(L), tgu(L), tdn(L);
+    for (int l = 0; l < L; ++l) {
+      tq[l] = matrix(3 * (size_t)d, d);
+      tout[l] = matrix(d, d);
+      tgu[l] = matrix(2 * (size_t)F, d);
+      tdn[l] = matrix(d, F);
+    }
+    rt->tweights_bytes = to;
+    if (rt->cuda(cudaMalloc(&rt->tweights, to), "cudaMalloc tiled weights") != ST_OK ||
+        rt->cuda(cudaMemsetAsync(rt->tweights, 0, to, rt->stream), "cudaMemset tiled weights") != ST_OK)
+      return bail(ST_ERR_CUDA);
+    for (int l = 0; l < L; ++l) {
+      a.tqkv[l] = rt->tweights + tq[l];
+      a.tout[l] = rt->tweights + tout[l];
+      a.tgateup[l] = rt->tweights + tgu[l];
+      a.tdown[l] = rt->tweights + tdn[l];
+      const std::string p = "layers." + std::to_string(l) + ".";
+      auto set = [&](const char* name, size_t at, int rows, int cols) {
+        TensorSlot& ts = rt->slots[p + name];
+        ts.tiled_offset = at;
+        ts.tiled_rows = rows;
+        ts.tiled_cols = cols;
+      };
+      for (const char* n : {"q", "k", "v"}) set(n, tq[l], 3 * d, d);
+      set("out", tout[l], d, d);
+      set("gate", tgu[l], 2 * F, d);
+      set("up", tgu[l], 2 * F, d);
+      set("down", tdn[l], d, F);
+    }
+  }
   {
     // Keep as many whole layers L2-resident as fit in 70% of L2 (the rest holds
     // the K/V cache, activations and code); ST_L2_KEEP_LAYERS overrides.
@@ -800,6 +967,13 @@ int st_set_tensor(st_runtime* rt, const char* name, const float* data, size_t co
     if (rt->desc.mode == ST_MODE_FP16) k_convert<__half><<<blocks, 256, 0, rt->stream>>>(tmp, (__half*)dst, s.rows, s.cols, s.kind, s.p0, s.p1);
     else if (rt->desc.mode == ST_MODE_BF16) k_convert<__nv_bfloat16><<<blocks, 256, 0, rt->stream>>>(tmp, (__nv_bfloat16*)dst, s.rows, s.cols, s.kind, s.p0, s.p1);
     else k_convert<float><<<blocks, 256, 0, rt->stream>>>(tmp, (float*)dst, s.rows, s.cols, s.kind, s.p0, s.p1);
+    if (rt->tc && s.tiled_rows) {
+      void* tdst = rt->tweights + s.tiled_offset;
+      if (rt->desc.mode == ST_MODE_FP16)
+        k_convert_tiled<__half><<<blocks, 256, 0, rt->stream>>>(tmp, (__half*)tdst, s.rows, s.cols, s.kind, s.p0, s.p1, s.tiled_cols);
+      else
+        k_convert_tiled<__nv_bfloat16><<<blocks, 256, 0, rt->stream>>>(tmp, (__nv_bfloat16*)tdst, s.rows, s.cols, s.kind, s.p0, s.p1, s.tiled_cols);
+    }
     st = rt->cuda(cudaGetLastError(), "convert launch");
     if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "convert");
   }
@@ -1033,7 +1207,9 @@ static int device_trace_impl(st_runtime* rt, const float* dev_inputs, size_t cou
   a.score = rt->dev_score;
   ST_TRY(launch_reset(rt, 0, S));
   ST_CUDA(rt, cudaEventRecord(rt->ev_start, rt->stream));
-  if (rt->opt.backend == ST_BACKEND_FUSED || rt->opt.backend == ST_BACKEND_PERSISTENT) {
+  if (rt->batched) {
+    ST_TRY(launch_rounds(rt, a, dev_inputs, count, dev_scores));
+  } else if (rt->opt.backend == ST_BACKEND_FUSED || rt->opt.backend == ST_BACKEND_PERSISTENT) {
     ST_TRY(launch_trace(rt, a, dev_inputs, count, dev_scores));
   } else {
     const bool graph = rt->opt.backend == ST_BACKEND_GRAPH && !rt->opt.mapped;
@@ -1087,7 +1263,8 @@ int st_device_timeline(st_runtime* rt, const float* inputs, size_t count, long l
 int st_device_timeline_cta(st_runtime* rt, const float* inputs, size_t count, int cta, long long* marks,
                            size_t capacity, size_t* used) {
   if (!rt || !inputs || !marks || count == 0 || capacity == 0) return ST_ERR_INVALID;
-  if (cta < 0 || cta >= rt->grid) return rt->fail(ST_ERR_INVALID, "timeline CTA %d outside the grid of %d", cta, rt->grid);
+  const int grid = rt->batched ? rt->bgrid : rt->grid;
+  if (cta < 0 || cta >= grid) return rt->fail(ST_ERR_INVALID, "timeline CTA %d outside the grid of %d", cta, grid);
   if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
   if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
   if (rt->opt.backend == ST_BACKEND_PERSISTENT) ST_TRY(st_stop(rt));
@@ -1106,7 +1283,7 @@ int st_device_timeline_cta(st_runtime* rt, const float* inputs, size_t count, in
     a.timeline = tl;
     a.timeline_capacity = (int)std::min<size_t>(capacity, 1u << 30);
     a.timeline_cta = cta;
-    st = launch_trace(rt, a, dev, count, nullptr, true);
+    st = rt->batched ? launch_rounds(rt, a, dev, count, nullptr) : launch_trace(rt, a, dev, count, nullptr, true);
   }
   if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "timeline run");
   if (st == ST_OK) st = check_device_error(rt);
@@ -1167,7 +1344,13 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     << ",\"poll_policy\":\"" << (rt->opt.backoff ? "bounded-device-backoff-host-yield" : "tight") << "\""
     << ",\"workspace_storage\":\"FP32 with explicit rounding to the storage type\""
     << ",\"weights_and_kv_storage\":\"" << modes[rt->desc.mode] << "\""
-    << ",\"streams\":" << rt->desc.streams << ",\"weights_bytes\":" << rt->weights_bytes
+    << ",\"streams\":" << rt->desc.streams << ",\"batched\":" << (rt->batched ? "true" : "false")
+    << ",\"batched_tensor_cores\":" << (rt->tc ? "true" : "false") << ",\"tc_stages\":" << rt->args.tc_stages
+    << ",\"tc_stage_bytes\":" << rt->args.tc_stage_bytes << ",\"tc_tmem_columns\":" << rt->args.tc_ncols
+    << ",\"tiled_weights_bytes\":" << rt->tweights_bytes
+    << ",\"batched_grid\":" << rt->bgrid << ",\"batched_splits\":[" << rt->bsplit[0] << "," << rt->bsplit[1] << ","
+    << rt->bsplit[2] << "," << rt->bsplit[3] << "],\"batched_barriers_per_round\":"
+    << (rt->batched ? round_barriers(rt->desc.layers) : 0) << ",\"weights_bytes\":" << rt->weights_bytes
     << ",\"state_bytes\":" << rt->state_bytes << ",\"scratch_bytes\":" << rt->scratch_bytes << "}";
   return copy_json(o.str(), json, capacity, needed);
 }
@@ -1193,6 +1376,7 @@ void st_destroy(st_runtime* rt) {
   if (rt->stream) cudaStreamDestroy(rt->stream);
   if (rt->aux) cudaStreamDestroy(rt->aux);
   cudaFree(rt->weights);
+  cudaFree(rt->tweights);
   cudaFree(rt->state);
   cudaFree(rt->scratch);
   if (rt->mb_h) cudaFreeHost(rt->mb_h);
