@@ -54,11 +54,27 @@ def _run(cmd: list[str], log: Path | None = None) -> None:
 
 
 def build_cuda(force: bool = False) -> Path:
-    sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "streaming_b200.h"]
-    if force or _stale(CUDA_LIB, sources):
+    units = sorted(CSRC.glob("*.cu"))
+    headers = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [INCLUDE / "streaming_b200.h"]
+    if force or _stale(CUDA_LIB, units + headers):
         LIB.mkdir(exist_ok=True)
-        _run([NVCC, *NVCC_FLAGS, "-shared", "-o", str(CUDA_LIB), *[str(s) for s in sorted(CSRC.glob("*.cu"))]],
-             LIB / "ptxas.log")
+        objs = [LIB / (u.stem + ".o") for u in units]
+        # Translation units compile in parallel (the flow kernels are the
+        # longest); every object is rebuilt because they share the headers.
+        procs = [subprocess.Popen([NVCC, *NVCC_FLAGS, "-c", "-o", str(o), str(u)], stdout=subprocess.PIPE,
+                                  stderr=subprocess.STDOUT, text=True) for u, o in zip(units, objs)]
+        logs, failed = [], False
+        for u, p in zip(units, procs):
+            out, _ = p.communicate()
+            logs.append(f"== {u.name}\n{out}")
+            failed |= p.returncode != 0
+        (LIB / "ptxas.log").write_text("\n".join(logs))
+        if failed:
+            sys.stderr.write("\n".join(logs))
+            raise RuntimeError("build failed: nvcc -c ...")
+        _run([NVCC, *GENCODE, "-shared", "-o", str(CUDA_LIB), *[str(o) for o in objs]])
+        for o in objs:
+            o.unlink()
     return CUDA_LIB
 
 

@@ -87,6 +87,12 @@ struct StepArgs {
   int l2_keep_layers;                 // layers whose weights are kept L2-resident (weight ring)
   int cluster_size;                   // CTAs per cluster the buffers were sized for
   int clusters;                       // clusters in the grid (sizes dpart)
+  // single-stream flow kernel (st_flow.cuh)
+  unsigned long long* ll_heads;       // [2][H][d] tagged out-projection partials per head
+  unsigned long long* ll_clusters;    // [2][clusters][d] tagged down-projection partials per cluster
+  unsigned long long* flow_epoch;     // tag base for the next launch
+  unsigned long long* flow_ctl;       // persistent: tagged command word
+  unsigned long long* flow_seq;       // persistent: mailbox sequence of the command
   // batched round (all streams per pass over the weights)
   float* bx;                          // [S][d] residual x
   float* bx2;                         // [S][d] residual x'

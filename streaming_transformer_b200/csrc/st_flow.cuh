@@ -1,0 +1,1069 @@
+// st_flow.cuh -- the single-stream step at the benchmark shapes, with no grid
+// barrier on the step path.
+//
+// Shapes: width D in {256, 512, 1024} (a template parameter), head_dim 64,
+// 32 features, one stream; the host picks this kernel when the model has them
+// (flow_supported) and the generic kernels of st_step.cuh otherwise. The
+// arithmetic and cast points are the reference step's (reference
+// src/cpu/Cpu.cpp:59-141); only the association of the fp32 sums differs.
+//
+// Grid: NC clusters of CS CTAs (CS = 8, or 4 when 8-CTA clusters are fewer
+// than the heads), 512 threads, one CTA per SM, all co-resident. Cluster c
+// owns heads c, c + NC, ...; rank r of every cluster owns segment r of the
+// width, [r n, (r + 1) n) with n = D / CS. Per layer:
+//
+//   attention (clusters that own a head; per head h)
+//     z = norm1(x)                    every CTA, the gain from the ring
+//     q, k, v rows of head h          row pairs split over the cluster, RoPE and
+//                                     casts in the warp epilogue, broadcast into
+//                                     every rank through DSMEM; k, v to slot t % W
+//     cluster barrier
+//     attention over [0, valid)       slots split over the cluster, an online
+//                                     softmax per warp, warps merged per CTA, the
+//                                     CTA partial broadcast through DSMEM
+//     cluster barrier; merge -> o_h (cast)
+//     out-projection rows of segment r (K-split by head): P[h][seg r] published
+//   exchange 1 (every CTA)            rank r gathers P[*][seg r] of every head,
+//                                     x'[seg r] = cast(x + cast(sum_h P[h])),
+//                                     broadcast to the cluster with its sum of
+//                                     squares; cluster barrier
+//   FFN (every CTA)                   z = norm2(x'); gate/up row pairs of this CTA's
+//                                     ffn slice -> SwiGLU; down-projection K-split
+//                                     over the slice -> partial d-vector;
+//                                     reduce-scatter in the cluster (DSMEM, barrier);
+//                                     rank r publishes D[c][seg r]
+//   exchange 2 (every CTA)            rank r gathers D[*][seg r] of every cluster,
+//                                     x[seg r] = cast(x' + cast(sum_c D[c])),
+//                                     broadcast; cluster barrier
+//
+// Publishing is by tagged records: an 8-byte store of {fp32 value, 32-bit tag}
+// (single-copy atomic), the tag unique to (step, layer). A consumer polls the
+// records of its segment until every tag matches, so the wait and the data
+// arrive in one L2 round trip instead of a grid barrier followed by a read.
+// The record buffers alternate by layer parity; no CTA can lag a producer by
+// two layers (every exchange needs every cluster's previous contribution), so
+// a record is never overwritten before all its readers have read it. Tags
+// continue across launches from a device word (flow_epoch), so records left
+// by an earlier launch or step never match.
+//
+// Weights: every CTA streams its fixed per-step span sequence (st_ring.cuh's
+// span_of assignment: IN, then per layer NORM1 and QKV/OUT of each owned head,
+// NORM2, GATEUP, DOWN) through a shared-memory ring of chunks of at most
+// 64 KB, copied by cp.async.bulk (global -> this CTA's shared memory, no
+// multicast) with mbarrier completion. One issuer thread (lane 0 of warp 15)
+// issues whenever released bytes allow, including while its CTA polls records.
+// A chunk is shared by all 16 warps: warp passes are dealt round robin, every
+// warp arrives on the chunk's empty mbarrier when done (or at once when it has
+// no pass in it). The first l2_keep_layers layers are copied with an
+// L2::evict_last policy, the rest evict_first.
+//
+// Every wait is bounded (bar_timeout_ns) and sets the device error word.
+// Verdicts are made cluster-uniform at each exchange (every rank broadcasts
+// its own), so a failing cluster leaves together after a cluster barrier and
+// no CTA exits while a peer may still write into its shared memory.
+#pragma once
+
+#include "st_kernels.cuh"
+
+namespace st {
+
+constexpr int kFlowHd = 64;
+constexpr int kFlowFeatures = 32;
+constexpr int kFlowMaxCluster = 8;
+constexpr int kFlowSlots = 8;                  // ring chunks in flight (one mbarrier pair each)
+constexpr unsigned kFlowChunkMax = 64u * 1024u;
+constexpr int kFlowMaxChunks = 320;            // chunks per step one CTA may consume
+constexpr int kFlowKvBytes = 16 * 1024;        // K and V rows one CTA prefetches per head
+constexpr int kFlowMaxD = 1024;
+constexpr int kFlowMaxAct = 512;               // SwiGLU outputs per CTA
+constexpr int kFlowIssuer = kThreads - 32;     // lane 0 of the last warp
+
+enum FlowMode : int { kFlowTrace = 0, kFlowPersistent = 1 };
+enum FlowCommand : int { kFlowExit = 15 };
+
+// Launch parameters of k4_flow beyond StepArgs.
+struct FlowLaunch {
+  int mode;                         // kFlowTrace or kFlowPersistent
+  const float* inputs;              // trace: [count][features] (device)
+  unsigned long long count;         // trace: events
+  float* scores;                    // trace: [count] or null
+  PersistArgs p;                    // persistent: mailbox protocol
+  const float* mapped_input;        // persistent: device alias of the mapped event
+  unsigned long long bar_base;      // value of a.bar_counter at launch
+};
+
+// ---------------------------------------------------------------- chunking
+// Rows one warp pass covers for a span: U rows per epilogue group (2 for the
+// q/k/v, out and gate/up spans, whose epilogues take row pairs) times the
+// groups a warp covers at once when a row is shorter than 32 vectors. Norm
+// and down spans are read by the whole CTA, row by row.
+__host__ __device__ inline int flow_pass_rows(int kind, int row_bytes) {
+  if (kind == kSpanNorm1 || kind == kSpanNorm2 || kind == kSpanDown) return 1;
+  const int u = (kind == kSpanQkv || kind == kSpanGateUp || kind == kSpanOut) ? 2 : 1;
+  const int nv = row_bytes / 16;
+  const int lpr = nv < 32 ? nv : 32;
+  return u * (32 / lpr);
+}
+
+struct FlowSplit {
+  int chunks, rows_per_chunk;
+};
+
+// A span is cut into the fewest chunks of at most kFlowChunkMax bytes whose
+// row counts are whole warp passes and as equal as possible.
+__host__ __device__ inline FlowSplit flow_split(const Span& s, int kind) {
+  if (s.rows <= 0) return {0, 0};
+  const int pr = flow_pass_rows(kind, s.row_bytes);
+  const int units = (s.rows + pr - 1) / pr;
+  int per = (int)(kFlowChunkMax / (unsigned)(pr * s.row_bytes));
+  if (per < 1) per = 1;
+  const int chunks = (units + per - 1) / per;
+  const int upc = (units + chunks - 1) / chunks;
+  return {chunks, upc * pr};
+}
+
+// Chunks one step consumes for CTA position w (the issuer's table order).
+__host__ __device__ inline int flow_chunks_per_step(const StepArgs& a, const Where& w, size_t elem) {
+  int n = 0;
+  auto count = [&](int kind, int l, int h) { n += flow_split(span_of(a, w, kind, l, h, elem), kind).chunks; };
+  count(kSpanIn, -1, 0);
+  for (int l = 0; l < a.layers; ++l) {
+    if (w.id < a.heads) {
+      count(kSpanNorm1, l, 0);
+      for (int h = w.id; h < a.heads; h += w.count) {
+        count(kSpanQkv, l, h);
+        count(kSpanOut, l, h);
+      }
+    }
+    count(kSpanNorm2, l, 0);
+    count(kSpanGateUp, l, 0);
+    count(kSpanDown, l, 0);
+  }
+  return n;
+}
+
+// ---------------------------------------------------------------- shared memory
+struct FlowChunk {
+  const char* src;
+  unsigned bytes;
+  unsigned keep;  // 1: L2 evict_last, 0: evict_first
+};
+
+struct alignas(128) FlowRing {
+  unsigned long long full[kFlowSlots];   // completion of chunk c at c % kFlowSlots
+  unsigned long long empty[kFlowSlots];  // release of chunk c (one arrival per warp)
+  unsigned off[kFlowSlots];              // buffer offset of that chunk
+  unsigned long long end[kFlowSlots];    // allocation position just past it
+  unsigned long long head, tail, issued, released, limit;
+  unsigned long long keep_policy, stream_policy;
+  unsigned char* buf;
+  unsigned capacity, head_off;
+  int next, nchunks, failed, ok;
+  FlowChunk table[kFlowMaxChunks];
+};
+
+// Every DSMEM target sits at the same offset in every CTA of the cluster.
+struct alignas(128) FlowSmem {
+  float x[kFlowMaxD];                    // residual entering the layer (DSMEM target)
+  float x2[kFlowMaxD];                   // residual after attention (DSMEM target)
+  float z[kFlowMaxD];                    // norm output, GEMV input
+  float dred[kFlowMaxD];                 // down partials from every rank, [CS][n] (DSMEM target)
+  float seg[kFlowMaxD];                  // this rank's segment values before publishing
+  float fnorm[kFlowMaxD];                // final norm gain (score CTA)
+  float fscore[kFlowMaxD];               // score weights (score CTA)
+  float qkv[3 * kFlowHd];                // q, k, v of the current head (DSMEM target)
+  float apart[kFlowMaxCluster][kFlowHd + 2];  // CTA attention partials per rank (DSMEM target)
+  float wpart[kWarps][kFlowHd + 2];      // warp attention partials
+  float o[kFlowHd];                      // merged attention output (cast)
+  float act[kFlowMaxAct];                // this CTA's SwiGLU slice
+  float ssx[kFlowMaxCluster][8];         // sum of squares of x per rank and warp (DSMEM target)
+  float ssx2[kFlowMaxCluster][8];        // same for x' (DSMEM target)
+  int okv[4][kFlowMaxCluster];           // verdict per rank, one row per publishing site (DSMEM target)
+  float2 rope_cs[kFlowHd / 2];           // cos, sin of t * frequency
+  float rope[kFlowHd / 2];               // frequencies 10000^(-2i/hd)
+  float ev[kFlowFeatures];               // the event
+  float warp_scratch[kWarps];
+  unsigned long long cmd;                // persistent: the dispatched command
+  union {
+    alignas(16) unsigned char kv[kFlowKvBytes];   // K rows then V rows of this CTA's slots
+    float red[kFlowKvBytes / 4];                   // gather / down group partials
+  } u;
+};
+
+constexpr size_t kFlowRingOffset = (sizeof(FlowSmem) + sizeof(FlowRing) + 127) / 128 * 128;
+constexpr size_t kFlowSmemBytes = kSmemLimit - kStaticSmemReserve;
+constexpr unsigned kFlowRingCapacity = (unsigned)((kFlowSmemBytes - kFlowRingOffset) / 128 * 128);
+static_assert(kFlowRingCapacity >= 2 * kFlowChunkMax, "the flow ring needs room for two chunks");
+
+// ---------------------------------------------------------------- tagged records
+__device__ __forceinline__ unsigned long long ll_pack(float v, unsigned tag) {
+  return ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+}
+__device__ __forceinline__ void ll_store2(unsigned long long* p, float v0, float v1, unsigned tag) {
+  asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(ll_pack(v0, tag)), "l"(ll_pack(v1, tag))
+               : "memory");
+}
+__device__ __forceinline__ void ll_load2(const unsigned long long* p, unsigned long long& r0, unsigned long long& r1) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(r0), "=l"(r1) : "l"(p) : "memory");
+}
+__device__ __forceinline__ unsigned ll_tag(unsigned long long r) { return (unsigned)(r >> 32); }
+__device__ __forceinline__ float ll_value(unsigned long long r) { return __uint_as_float((unsigned)r); }
+
+__device__ __forceinline__ void dsmem_store2(float* local, unsigned rank, float v0, float v1) {
+  const unsigned addr = (unsigned)__cvta_generic_to_shared(local);
+  unsigned remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(remote), "f"(v0), "f"(v1) : "memory");
+}
+__device__ __forceinline__ void dsmem_store4(float* local, unsigned rank, float4 v) {
+  const unsigned addr = (unsigned)__cvta_generic_to_shared(local);
+  unsigned remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(remote), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+// ---------------------------------------------------------------- ring
+// The issuer: reclaim released chunks, then issue while a slot and enough
+// free bytes are available and the launch limit allows.
+static __device__ __noinline__ void flow_fill_slow(FlowRing& fr) {
+  while (fr.released < fr.issued &&
+         mbar_test_wait(&fr.empty[fr.released % kFlowSlots], (unsigned)((fr.released / kFlowSlots) & 1ull))) {
+    fr.tail = fr.end[fr.released % kFlowSlots];
+    fr.released += 1;
+  }
+  while (fr.issued < fr.limit && fr.issued < fr.released + kFlowSlots) {
+    const FlowChunk c = fr.table[fr.next];
+    const unsigned alloc = (c.bytes + 127u) & ~127u;
+    unsigned long long pos = fr.head;
+    unsigned off = fr.head_off;
+    if (off + alloc > fr.capacity) {  // never split a chunk across the end
+      pos += fr.capacity - off;
+      off = 0;
+    }
+    if (pos + alloc - fr.tail > fr.capacity) return;
+    const int slot = (int)(fr.issued % kFlowSlots);
+    fr.off[slot] = off;
+    fr.end[slot] = pos + alloc;
+    fr.head = pos + alloc;
+    fr.head_off = off + alloc == fr.capacity ? 0u : off + alloc;
+    mbar_expect_tx(&fr.full[slot], c.bytes);
+    bulk_copy(fr.buf + off, c.src, c.bytes, &fr.full[slot], c.keep ? fr.keep_policy : fr.stream_policy);
+    fr.next = fr.next + 1 == fr.nchunks ? 0 : fr.next + 1;
+    fr.issued += 1;
+  }
+}
+__device__ __forceinline__ void flow_fill(FlowRing& fr) {
+  if (threadIdx.x == kFlowIssuer) flow_fill_slow(fr);
+}
+
+// Per-thread consumer position (uniform across the CTA).
+struct FlowCur {
+  unsigned long long consumed;
+};
+
+static __device__ __noinline__ bool flow_wait_slow(FlowRing& fr, int slot, unsigned parity,
+                                                   unsigned long long timeout_ns) {
+  const bool issuer = threadIdx.x == kFlowIssuer;
+  const unsigned long long start = globaltimer();
+  while (true) {
+    flow_fill(fr);
+    if (mbar_try_wait_for(&fr.full[slot], parity, issuer ? 200u : 20000u)) return true;
+    if (globaltimer() - start > timeout_ns) return false;
+  }
+}
+
+// Wait (bounded) for the next chunk; returns its bytes. After a failed wait
+// the ring is marked failed and every later acquire returns the start of the
+// buffer without waiting (the error word ends the launch at its next exchange).
+__device__ __forceinline__ const unsigned char* flow_acquire(const StepArgs& a, FlowRing& fr, const FlowCur& cur) {
+  const int slot = (int)(cur.consumed % kFlowSlots);
+  const unsigned parity = (unsigned)((cur.consumed / kFlowSlots) & 1ull);
+  if (!mbar_try_wait(&fr.full[slot], parity) && !*reinterpret_cast<volatile int*>(&fr.failed) &&
+      !flow_wait_slow(fr, slot, parity, a.bar_timeout_ns)) {
+    fr.failed = 1;
+    set_error(a, kBarrierTimeout);
+  }
+  return fr.buf + (*reinterpret_cast<volatile int*>(&fr.failed) ? 0u : fr.off[slot]);
+}
+
+// Every thread of a warp, after the warp's last read of the chunk (or without
+// reading it): one arrival per warp on its empty mbarrier.
+__device__ __forceinline__ void flow_release(FlowRing& fr, FlowCur& cur) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&fr.empty[cur.consumed % kFlowSlots]);
+  cur.consumed += 1;
+  flow_fill(fr);
+}
+
+// Wait for every issued copy (bounded) before the CTA leaves.
+__device__ inline void flow_drain(const StepArgs& a, FlowRing& fr, const FlowCur& cur) {
+  if (threadIdx.x == kFlowIssuer && fr.ok) {
+    for (unsigned long long c = cur.consumed; c < fr.issued; ++c) {
+      const int slot = (int)(c % kFlowSlots);
+      const unsigned parity = (unsigned)((c / kFlowSlots) & 1ull);
+      const unsigned long long start = globaltimer();
+      while (!mbar_try_wait(&fr.full[slot], parity))
+        if (globaltimer() - start > a.bar_timeout_ns) break;
+    }
+  }
+  __syncthreads();
+}
+
+// All threads: the chunk table (issuer), mbarriers, first issues. `limit`
+// bounds the chunks issued (0: unbounded). Returns false when the table does
+// not fit (the host checks this before choosing the kernel).
+__device__ inline bool flow_ring_begin(const StepArgs& a, FlowRing& fr, unsigned char* buf, const Where& w,
+                                       size_t elem, unsigned long long steps) {
+  if (threadIdx.x == kFlowIssuer) {
+    fr.head = fr.tail = fr.issued = fr.released = 0;
+    fr.head_off = 0;
+    fr.failed = 0;
+    fr.keep_policy = policy_evict_last();
+    fr.stream_policy = policy_evict_first();
+    fr.buf = buf;
+    fr.capacity = kFlowRingCapacity;
+    fr.next = 0;
+    int n = 0;
+    bool ok = true;
+    unsigned keep = 1u;
+    auto add = [&](int kind, int l, int h) {
+      const Span s = span_of(a, w, kind, l, h, elem);
+      const FlowSplit sp = flow_split(s, kind);
+      for (int c = 0; c < sp.chunks; ++c) {
+        if (n >= kFlowMaxChunks) { ok = false; return; }
+        const int r0 = c * sp.rows_per_chunk;
+        const int rows = min(sp.rows_per_chunk, s.rows - r0);
+        fr.table[n++] = FlowChunk{s.base + (size_t)r0 * s.row_bytes, (unsigned)(rows * s.row_bytes), keep};
+      }
+    };
+    add(kSpanIn, -1, 0);
+    for (int l = 0; l < a.layers; ++l) {
+      keep = l < a.l2_keep_layers ? 1u : 0u;
+      if (w.id < a.heads) {
+        add(kSpanNorm1, l, 0);
+        for (int h = w.id; h < a.heads; h += w.count) {
+          add(kSpanQkv, l, h);
+          add(kSpanOut, l, h);
+        }
+      }
+      add(kSpanNorm2, l, 0);
+      add(kSpanGateUp, l, 0);
+      add(kSpanDown, l, 0);
+    }
+    fr.nchunks = n;
+    fr.limit = steps ? steps * (unsigned long long)n : ~0ull;
+    fr.ok = ok && n > 0;
+    if (fr.ok) {
+      for (int i = 0; i < kFlowSlots; ++i) {
+        mbar_init(&fr.full[i], 1);
+        mbar_init(&fr.empty[i], kWarps);
+      }
+      fence_mbar_init();
+    }
+  }
+  __syncthreads();
+  const bool ok = fr.ok != 0;
+  if (ok) flow_fill(fr);
+  return ok;
+}
+
+// ---------------------------------------------------------------- warp GEMV
+// Geometry of rows of K elements of T: 16-byte vectors, LPR lanes per row,
+// VPL vectors per lane, RPP row groups per warp pass.
+template <typename T, int K>
+struct FlowRow {
+  static constexpr int V = Storage<T>::kVec;
+  static constexpr int NV = K / V;
+  static constexpr int LPR = NV < 32 ? NV : 32;
+  static constexpr int VPL = NV / LPR;
+  static constexpr int RPP = 32 / LPR;
+  static_assert(K % V == 0 && (NV & (NV - 1)) == 0 && NV >= 2, "rows must be a power-of-two number of vectors");
+};
+
+// The lane's share of a GEMV input vector (shared memory), in registers.
+template <typename T, int K>
+struct FlowX {
+  using R = FlowRow<T, K>;
+  float v[R::VPL * R::V];
+  __device__ __forceinline__ void load(const float* xs) {
+    const int sl = (threadIdx.x & 31) % R::LPR;
+#pragma unroll
+    for (int k = 0; k < R::VPL; ++k)
+#pragma unroll
+      for (int e = 0; e < R::V; e += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(xs + (sl + R::LPR * k) * R::V + e);
+        v[k * R::V + e] = q.x;
+        v[k * R::V + e + 1] = q.y;
+        v[k * R::V + e + 2] = q.z;
+        v[k * R::V + e + 3] = q.w;
+      }
+  }
+};
+
+// Per-lane partial dot products of U consecutive rows (stride K) with x.
+template <typename T, int K, int U>
+__device__ __forceinline__ void flow_dot(const T* row, int sl, const FlowX<T, K>& x, float (&acc)[U]) {
+  using R = FlowRow<T, K>;
+  constexpr int B = 4;  // vectors per row in flight
+#pragma unroll
+  for (int u = 0; u < U; ++u) acc[u] = 0.f;
+#pragma unroll
+  for (int k0 = 0; k0 < R::VPL; k0 += B) {
+    uint4 w[U][B];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+        if (k0 + b < R::VPL) w[u][b] = ld_shared_v4(row + (size_t)u * K + (size_t)(sl + R::LPR * (k0 + b)) * R::V);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+        if (k0 + b < R::VPL) acc[u] += dot_regs<T>(w[u][b], x.v + (k0 + b) * R::V);
+  }
+}
+
+// Rows of span s from the ring, U rows per group; epi(row, v[U]) runs on lane
+// 0 of each valid group (row relative to the span). Passes of RPP groups are
+// dealt to warps round robin across the span's chunks; a warp without a pass
+// in a chunk releases it without waiting (except the issuer's warp).
+template <typename T, int K, int U, class Epi>
+__device__ __forceinline__ void flow_rows(const StepArgs& a, FlowRing& fr, FlowCur& cur, const Span& s, int kind,
+                                          const FlowX<T, K>& x, Epi&& epi) {
+  using R = FlowRow<T, K>;
+  const FlowSplit sp = flow_split(s, kind);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane / R::LPR, sl = lane - sub * R::LPR;
+  constexpr int pr = U * R::RPP;
+  int pass0 = 0;
+  for (int c = 0; c < sp.chunks; ++c) {
+    const int r0 = c * sp.rows_per_chunk;
+    const int n = min(sp.rows_per_chunk, s.rows - r0);
+    const int passes = (n + pr - 1) / pr;
+    const int first = (warp - pass0 % kWarps + kWarps) % kWarps;
+    // The issuer's warp waits for every chunk (issuing while it waits), so it
+    // never runs ahead to a barrier while other warps need a chunk it has
+    // yet to issue.
+    if (first < passes || warp == (kFlowIssuer >> 5)) {
+      const T* base = (const T*)flow_acquire(a, fr, cur);
+      for (int p = first; p < passes; p += kWarps) {
+        const int row = p * pr + sub * U;
+        const bool valid = row < n;
+        float acc[U];
+        flow_dot<T, K, U>(base + (size_t)(valid ? row : 0) * K, sl, x, acc);
+        if constexpr (U == 2) {
+          // Halve the shuffles: the upper half-group keeps row 1, the lower row 0.
+          constexpr int H = R::LPR / 2;
+          const bool hi = (sl & H) != 0;
+          const float send = hi ? acc[0] : acc[1];
+          float r = (hi ? acc[1] : acc[0]) + __shfl_xor_sync(0xffffffffu, send, H);
+#pragma unroll
+          for (int o = H / 2; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+          const float r1 = __shfl_down_sync(0xffffffffu, r, H);
+          if (valid && sl == 0) {
+            const float v[2] = {r, r1};
+            epi(r0 + row, v);
+          }
+        } else {
+          float r = acc[0];
+#pragma unroll
+          for (int o = R::LPR / 2; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+          if (valid && sl == 0) {
+            const float v[1] = {r};
+            epi(r0 + row, v);
+          }
+        }
+      }
+    }
+    flow_release(fr, cur);
+    pass0 += passes;
+  }
+}
+
+// A one-row span (a norm gain) read by every thread: g(i) for i < D.
+template <typename T, class Fn>
+__device__ __forceinline__ void flow_gain(const StepArgs& a, FlowRing& fr, FlowCur& cur, Fn&& fn) {
+  const T* g = (const T*)flow_acquire(a, fr, cur);
+  fn(g);
+  flow_release(fr, cur);
+}
+
+// ---------------------------------------------------------------- exchanges
+// Sum over sources src < nsrc of the records rec[src * D + seg0 + i], i < n,
+// into sm.seg[i] (threads i < n after the final barrier), sources added in
+// index order. Thread t polls element pair t % (n/2) for sources congruent to
+// t / (n/2) modulo G = 1024 / n, eight sources per round trip. Returns false
+// (error word set) when a wait ran out or another CTA failed.
+template <int D>
+__device__ __forceinline__ bool flow_gather(const StepArgs& a, FlowRing& fr, const unsigned long long* rec, int nsrc,
+                                            int seg0, int n, unsigned tag, FlowSmem& sm) {
+  const int np = n >> 1, G = kThreads / np;
+  const int e = (int)threadIdx.x % np, g = (int)threadIdx.x / np;
+  float s0 = 0.f, s1 = 0.f;
+  bool ok = true;
+  unsigned long long start = 0;
+  unsigned polls = 0;
+  for (int src0 = g; src0 < nsrc && ok; src0 += 8 * G) {
+    unsigned long long r[8][2];
+    while (true) {
+      bool ready = true;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int src = src0 + k * G;
+        if (src < nsrc) {
+          ll_load2(rec + (size_t)src * D + seg0 + 2 * e, r[k][0], r[k][1]);
+        } else {
+          r[k][0] = r[k][1] = ll_pack(0.f, tag);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ready = ready && ll_tag(r[k][0]) == tag && ll_tag(r[k][1]) == tag;
+      if (ready) break;
+      flow_fill(fr);
+      if ((++polls & 31u) == 0) {
+        if (ld_volatile_int(a.error) != 0) { ok = false; break; }
+        const unsigned long long now = globaltimer();
+        if (start == 0) start = now;
+        else if (now - start > a.bar_timeout_ns) { set_error(a, kBarrierTimeout); ok = false; break; }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      s0 += ll_value(r[k][0]);
+      s1 += ll_value(r[k][1]);
+    }
+  }
+  sm.u.red[g * n + 2 * e] = s0;
+  sm.u.red[g * n + 2 * e + 1] = s1;
+  ok = __syncthreads_and(ok) != 0;
+  if ((int)threadIdx.x < n) {
+    float t = 0.f;
+    for (int k = 0; k < G; ++k) t += sm.u.red[k * n + threadIdx.x];
+    sm.seg[threadIdx.x] = t;
+  }
+  __syncthreads();
+  return ok;
+}
+
+// Publish this rank's segment: dst[seg0 + i] = sm.seg[i] (i < n) into every
+// rank of the cluster, with the segment's sum of squares (per warp) and this
+// CTA's verdict; ends with a cluster barrier. Returns the cluster's verdict.
+// A rank reads its row of verdicts right after the barrier; each publishing
+// site has its own row, and between two publishes at one site every rank
+// passes another cluster barrier, so a row is never rewritten while read.
+enum FlowSite : int { kSiteSetup = 0, kSiteIn = 1, kSiteX2 = 2, kSiteX = 3 };
+__device__ __forceinline__ bool flow_publish(float* dst, float (*ss)[8], int seg0, int n, unsigned rank,
+                                             unsigned cs, bool ok, int site, FlowSmem& sm) {
+  const int np = n >> 1;
+  const int t = (int)threadIdx.x;
+  float q = 0.f;
+  if (t < np) {
+    const float v0 = sm.seg[2 * t], v1 = sm.seg[2 * t + 1];
+    for (unsigned k = 0; k < cs; ++k) dsmem_store2(dst + seg0 + 2 * t, k, v0, v1);
+    q = v0 * v0 + v1 * v1;
+  }
+  if (t < ((np + 31) & ~31)) {
+    q = warp_sum(q);
+    if ((t & 31) == 0)
+      for (unsigned k = 0; k < cs; ++k) dsmem_store(&ss[rank][t >> 5], k, q);
+  }
+  if (t < (int)cs) dsmem_store_u32(&sm.okv[site][rank], (unsigned)t, ok ? 1 : 0);
+  cluster_sync();
+  bool all = true;
+  for (unsigned k = 0; k < cs; ++k) all = all && (*reinterpret_cast<volatile int*>(&sm.okv[site][k]) != 0);
+  return all;
+}
+
+// 1 / sqrt(mean(x^2) + eps) from the published per-rank, per-warp sums.
+__device__ __forceinline__ float flow_norm_scale(const float (*ss)[8], unsigned cs, int n, int d, float eps) {
+  const int nw = ((n >> 1) + 31) >> 5;
+  float t = 0.f;
+  for (unsigned r = 0; r < cs; ++r)
+    for (int w = 0; w < nw; ++w) t += ss[r][w];
+  return 1.0f / sqrtf(t / (float)d + eps);
+}
+
+// ---------------------------------------------------------------- step context
+struct FlowCtx {
+  unsigned rank, cs, id, nc;
+  int n, seg0;
+  bool heads_here, score_cluster;
+  unsigned long long epoch;  // tag base of this launch
+  unsigned long long steps;  // steps this launch has run
+};
+
+// ---------------------------------------------------------------- attention
+// One head h of layer l: q/k/v rows, attention over the retained slots and
+// the out-projection rows of this rank's segment, published as P[h].
+// Returns false when a ring wait failed (nothing to undo; the error word ends
+// the launch at the next exchange).
+template <typename T, int D>
+__device__ __forceinline__ void flow_head(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSmem& sm,
+                                          const FlowCtx& cx, int l, int h, unsigned long long t, unsigned tag,
+                                          bool first_head) {
+  constexpr int hd = kFlowHd;
+  const int W = a.window;
+  const int slot = (int)(t % (unsigned long long)W);
+  const int valid = t + 1 < (unsigned long long)W ? (int)(t + 1) : W;
+  const Where wh{(int)cx.rank, (int)cx.cs, (int)cx.id, (int)cx.nc};
+  const size_t head_base = (((size_t)l * a.heads + h) * (size_t)W) * hd;
+  T* keys = (T*)a.keys + head_base;
+  T* values = (T*)a.values + head_base;
+  int j0, j1;
+  split(valid, (int)cx.rank, (int)cx.cs, j0, j1);
+  // K and V rows of this CTA's slots into shared memory (the slot this step
+  // overwrites comes from sm.qkv instead).
+  const int nj = j1 - j0;
+  const bool kv_smem = 2 * nj * hd * (int)sizeof(T) <= kFlowKvBytes;
+  if (kv_smem) {
+    constexpr int vpr = hd * (int)sizeof(T) / 16;
+    const int vecs = nj * vpr;
+    for (int i = threadIdx.x; i < 2 * vecs; i += kThreads) {
+      const bool is_v = i >= vecs;
+      const int k = is_v ? i - vecs : i;
+      if (j0 + k / vpr == slot) continue;
+      const char* src = (const char*)(is_v ? values : keys) + (size_t)j0 * hd * sizeof(T) + (size_t)k * 16;
+      cp_async16(sm.u.kv + (size_t)i * 16, src);
+    }
+    cp_async_commit();
+  }
+  if (first_head) {
+    const float scale = flow_norm_scale(sm.ssx, cx.cs, cx.n, D, a.epsilon);
+    flow_gain<T>(a, fr, cur, [&](const T* g) {
+      for (int i = threadIdx.x; i < D; i += kThreads) sm.z[i] = Storage<T>::round(sm.x[i] * scale * Storage<T>::load(g, i));
+    });
+    __syncthreads();
+  }
+  // q, k, v row pairs of this rank
+  {
+    int lo, hi;
+    split(3 * hd / 2, (int)cx.rank, (int)cx.cs, lo, hi);
+    FlowX<T, D> xr;
+    xr.load(sm.z);
+    flow_rows<T, D, 2>(a, fr, cur, span_of(a, wh, kSpanQkv, l, h, sizeof(T)), kSpanQkv, xr,
+                       [&](int r, const float (&v)[2]) {
+                         const int row = 2 * lo + r;
+                         const int which = row / hd, dim = row - which * hd;
+                         float v0 = Storage<T>::round(v[0]);
+                         float v1 = Storage<T>::round(v[1]);
+                         if (which < 2) {
+                           const float2 c = sm.rope_cs[dim >> 1];
+                           const float r0v = v0 * c.x - v1 * c.y;
+                           const float r1v = v0 * c.y + v1 * c.x;
+                           v0 = Storage<T>::round(r0v);
+                           v1 = Storage<T>::round(r1v);
+                         }
+                         for (unsigned k = 0; k < cx.cs; ++k) dsmem_store2(&sm.qkv[row], k, v0, v1);
+                         if (which > 0) {
+                           T* ring = which == 1 ? keys : values;
+                           const size_t at = (size_t)slot * hd + dim;
+                           Storage<T>::store(ring, at, v0);
+                           Storage<T>::store(ring, at + 1, v1);
+                         }
+                       });
+  }
+  if (kv_smem) cp_async_wait_all();
+  cluster_sync();
+  // attention over this CTA's slots: an online softmax per warp
+  {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const T* Ks = reinterpret_cast<const T*>(sm.u.kv);
+    const T* Vs = Ks + (size_t)nj * hd;
+    const float2 q = *reinterpret_cast<const float2*>(&sm.qkv[2 * lane]);
+    const float root = sqrtf((float)hd);
+    float m = -INFINITY, lsum = 0.f, acc0 = 0.f, acc1 = 0.f;
+    for (int j = j0 + warp; j < j1; j += kWarps) {
+      float k0, k1, v0, v1;
+      if (j == slot) {
+        k0 = sm.qkv[hd + 2 * lane];
+        k1 = sm.qkv[hd + 2 * lane + 1];
+        v0 = sm.qkv[2 * hd + 2 * lane];
+        v1 = sm.qkv[2 * hd + 2 * lane + 1];
+      } else if (kv_smem) {
+        k0 = Storage<T>::load(Ks + (size_t)(j - j0) * hd, 2 * lane);
+        k1 = Storage<T>::load(Ks + (size_t)(j - j0) * hd, 2 * lane + 1);
+        v0 = Storage<T>::load(Vs + (size_t)(j - j0) * hd, 2 * lane);
+        v1 = Storage<T>::load(Vs + (size_t)(j - j0) * hd, 2 * lane + 1);
+      } else {
+        k0 = Storage<T>::load_cg(keys + (size_t)j * hd, 2 * lane);
+        k1 = Storage<T>::load_cg(keys + (size_t)j * hd, 2 * lane + 1);
+        v0 = Storage<T>::load_cg(values + (size_t)j * hd, 2 * lane);
+        v1 = Storage<T>::load_cg(values + (size_t)j * hd, 2 * lane + 1);
+      }
+      const float s = warp_sum(fmaf(q.y, k1, q.x * k0)) / root;
+      const float mn = fmaxf(m, s);
+      const float c = expf(m - mn);
+      const float p = expf(s - mn);
+      lsum = fmaf(lsum, c, p);
+      acc0 = fmaf(acc0, c, p * v0);
+      acc1 = fmaf(acc1, c, p * v1);
+      m = mn;
+    }
+    sm.wpart[warp][2 + 2 * lane] = acc0;
+    sm.wpart[warp][3 + 2 * lane] = acc1;
+    if (lane == 0) {
+      sm.wpart[warp][0] = m;
+      sm.wpart[warp][1] = lsum;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    // warps 0 and 1: this CTA's partial (M, L, A[dim]) from the 16 warp partials
+    const int lane = threadIdx.x & 31, dim = threadIdx.x;
+    const float mk = lane < kWarps ? sm.wpart[lane][0] : -INFINITY;
+    const float lk = lane < kWarps ? sm.wpart[lane][1] : 0.f;
+    const float M = warp_max(lk > 0.f ? mk : -INFINITY);
+    const float sk = lk > 0.f ? expf(mk - M) : 0.f;
+    const float L = warp_sum(lk * sk);
+    float A = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) A = fmaf(sm.wpart[k][2 + dim], __shfl_sync(0xffffffffu, sk, k), A);
+    for (unsigned r = 0; r < cx.cs; ++r) dsmem_store(&sm.apart[cx.rank][2 + dim], r, A);
+    if (threadIdx.x < cx.cs) dsmem_store2(&sm.apart[cx.rank][0], threadIdx.x, M, L);
+  }
+  cluster_sync();
+  if (threadIdx.x < 64) {
+    // merge the cluster's partials in rank order -> o (cast)
+    const int lane = threadIdx.x & 31, dim = threadIdx.x;
+    const float mr = lane < (int)cx.cs ? sm.apart[lane][0] : -INFINITY;
+    const float lr = lane < (int)cx.cs ? sm.apart[lane][1] : 0.f;
+    const float M = warp_max(lr > 0.f ? mr : -INFINITY);
+    const float sr = lr > 0.f ? expf(mr - M) : 0.f;
+    const float L = warp_sum(lr * sr);
+    float A = 0.f;
+    for (unsigned r = 0; r < cx.cs; ++r) A = fmaf(sm.apart[r][2 + dim], __shfl_sync(0xffffffffu, sr, r), A);
+    sm.o[dim] = Storage<T>::round(A / L);
+  }
+  __syncthreads();
+  // out-projection rows of this rank's segment, published as P[h]
+  {
+    FlowX<T, hd> xr;
+    xr.load(sm.o);
+    unsigned long long* P = a.ll_heads + ((size_t)(tag & 1u) * a.heads + h) * D + cx.seg0;
+    flow_rows<T, hd, 2>(a, fr, cur, span_of(a, wh, kSpanOut, l, h, sizeof(T)), kSpanOut, xr,
+                        [&](int r, const float (&v)[2]) { ll_store2(P + r, v[0], v[1], tag); });
+  }
+}
+
+// ---------------------------------------------------------------- one step
+// One event through every layer; the score CTA writes the score to score_dst
+// (and score_copy when given). Returns the cluster-uniform verdict.
+template <typename T, int D>
+__device__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSmem& sm, FlowCtx& cx,
+                          const float* event, unsigned long long t, float* score_dst, float* score_copy) {
+  const Where wh{(int)cx.rank, (int)cx.cs, (int)cx.id, (int)cx.nc};
+  const int n = cx.n, seg0 = cx.seg0;
+  // The score CTA may still read x for the previous step.
+  if (cx.score_cluster && cx.steps > 0) cluster_sync();
+  if (threadIdx.x < kFlowFeatures) sm.ev[threadIdx.x] = __ldcv(event + threadIdx.x);
+  if (threadIdx.x < kFlowHd / 2) {
+    const float angle = (float)t * sm.rope[threadIdx.x];
+    sm.rope_cs[threadIdx.x] = make_float2(cosf(angle), sinf(angle));
+  }
+  __syncthreads();
+  // x[seg] = cast(W_in[seg] e)
+  {
+    FlowX<T, kFlowFeatures> xr;
+    xr.load(sm.ev);
+    flow_rows<T, kFlowFeatures, 1>(a, fr, cur, span_of(a, wh, kSpanIn, -1, 0, sizeof(T)), kSpanIn, xr,
+                                   [&](int r, const float (&v)[1]) { sm.seg[r] = Storage<T>::round(v[0]); });
+    __syncthreads();
+    if (!flow_publish(sm.x, sm.ssx, seg0, n, cx.rank, cx.cs, !fr.failed, kSiteIn, sm)) return false;
+  }
+  for (int l = 0; l < a.layers; ++l) {
+    const unsigned tag = (unsigned)(cx.epoch + cx.steps * (unsigned long long)a.layers + (unsigned long long)l + 1ull);
+    if (cx.heads_here) {
+      for (int h = (int)cx.id; h < a.heads; h += (int)cx.nc) {
+        if (h != (int)cx.id) cluster_sync();  // attention buffers are reused by the next head
+        flow_head<T, D>(a, fr, cur, sm, cx, l, h, t, tag, h == (int)cx.id);
+      }
+    }
+    // exchange 1: x'[seg] = cast(x[seg] + cast(sum_h P[h][seg]))
+    {
+      const unsigned long long* P = a.ll_heads + (size_t)(tag & 1u) * a.heads * D;
+      bool ok = flow_gather<D>(a, fr, P, a.heads, seg0, n, tag, sm);
+      if ((int)threadIdx.x < n)
+        sm.seg[threadIdx.x] = Storage<T>::round(sm.x[seg0 + threadIdx.x] + Storage<T>::round(sm.seg[threadIdx.x]));
+      __syncthreads();
+      if (!flow_publish(sm.x2, sm.ssx2, seg0, n, cx.rank, cx.cs, ok && !fr.failed, kSiteX2, sm)) return false;
+    }
+    // FFN: norm2, gate/up -> SwiGLU, down partial
+    {
+      const float scale = flow_norm_scale(sm.ssx2, cx.cs, n, D, a.epsilon);
+      flow_gain<T>(a, fr, cur, [&](const T* g) {
+        for (int i = threadIdx.x; i < D; i += kThreads)
+          sm.z[i] = Storage<T>::round(sm.x2[i] * scale * Storage<T>::load(g, i));
+      });
+      __syncthreads();
+      FlowX<T, D> xr;
+      xr.load(sm.z);
+      flow_rows<T, D, 2>(a, fr, cur, span_of(a, wh, kSpanGateUp, l, 0, sizeof(T)), kSpanGateUp, xr,
+                         [&](int r, const float (&v)[2]) {
+                           const float gt = Storage<T>::round(v[0]);
+                           const float up = Storage<T>::round(v[1]);
+                           sm.act[r >> 1] = Storage<T>::round((gt / (1.0f + expf(-gt))) * up);
+                         });
+      __syncthreads();
+      // partial[col] = sum_f act[f] W_down^T[f][col]: thread t owns 16-byte
+      // column vector t % NVd and rows f = g, g + G2, ... of the slice.
+      using R = FlowRow<T, D>;
+      constexpr int NVd = R::NV, G2 = kThreads / NVd, V = R::V;
+      const int cv = (int)threadIdx.x % NVd, g = (int)threadIdx.x / NVd;
+      float acc[V];
+#pragma unroll
+      for (int k = 0; k < V; ++k) acc[k] = 0.f;
+      const Span sd = span_of(a, wh, kSpanDown, l, 0, sizeof(T));
+      const FlowSplit sp = flow_split(sd, kSpanDown);
+      for (int c = 0; c < sp.chunks; ++c) {
+        const int r0 = c * sp.rows_per_chunk;
+        const int rows = min(sp.rows_per_chunk, sd.rows - r0);
+        const T* base = (const T*)flow_acquire(a, fr, cur);
+        int f = ((g - r0) % G2 + G2) % G2;
+        for (; f < rows; f += G2) {
+          const float av = sm.act[r0 + f];
+          float w[V];
+          Storage<T>::unpack(ld_shared_v4(base + (size_t)f * D + (size_t)cv * V), w);
+#pragma unroll
+          for (int k = 0; k < V; ++k) acc[k] = fmaf(w[k], av, acc[k]);
+        }
+        flow_release(fr, cur);
+      }
+      // sm.u.red was last read by exchange 1, before its cluster barrier.
+#pragma unroll
+      for (int k = 0; k < V; k += 4)
+        *reinterpret_cast<float4*>(&sm.u.red[g * D + cv * V + k]) = make_float4(acc[k], acc[k + 1], acc[k + 2], acc[k + 3]);
+      __syncthreads();
+      // column sums in group order, sent in float4s to the rank owning them
+      for (int c4 = threadIdx.x; c4 < D / 4; c4 += kThreads) {
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < G2; ++k) {
+          const float4 q = *reinterpret_cast<const float4*>(&sm.u.red[k * D + 4 * c4]);
+          s.x += q.x; s.y += q.y; s.z += q.z; s.w += q.w;
+        }
+        const int col = 4 * c4, owner = col / n;
+        dsmem_store4(&sm.dred[cx.rank * n + (col - owner * n)], (unsigned)owner, s);
+      }
+      cluster_sync();
+      // this rank's segment of the cluster partial, ranks added in order
+      unsigned long long* Dp = a.ll_clusters + ((size_t)(tag & 1u) * cx.nc + cx.id) * D + seg0;
+      if ((int)threadIdx.x < (n >> 1)) {
+        const int i = 2 * threadIdx.x;
+        float s0 = 0.f, s1 = 0.f;
+        for (unsigned r = 0; r < cx.cs; ++r) {
+          s0 += sm.dred[r * n + i];
+          s1 += sm.dred[r * n + i + 1];
+        }
+        ll_store2(Dp + i, s0, s1, tag);
+      }
+    }
+    // exchange 2: x[seg] = cast(x'[seg] + cast(sum_c D[c][seg]))
+    {
+      const unsigned long long* Dq = a.ll_clusters + (size_t)(tag & 1u) * cx.nc * D;
+      bool ok = flow_gather<D>(a, fr, Dq, (int)cx.nc, seg0, n, tag, sm);
+      if ((int)threadIdx.x < n) {
+        const float v = Storage<T>::round(sm.x2[seg0 + threadIdx.x] + Storage<T>::round(sm.seg[threadIdx.x]));
+        sm.seg[threadIdx.x] = v;
+        if (cx.score_cluster) a.hidden[(size_t)l * D + seg0 + threadIdx.x] = v;
+      }
+      __syncthreads();
+      if (!flow_publish(sm.x, sm.ssx, seg0, n, cx.rank, cx.cs, ok && !fr.failed, kSiteX, sm)) return false;
+    }
+  }
+  // final RMSNorm and score head (no cast), by the score CTA
+  if (cx.score_cluster && cx.rank == 0) {
+    const float scale = flow_norm_scale(sm.ssx, cx.cs, n, D, a.epsilon);
+    float acc = 0.f;
+    for (int i = threadIdx.x; i < D; i += kThreads)
+      acc = fmaf(sm.fscore[i], Storage<T>::round(sm.x[i] * scale * sm.fnorm[i]), acc);
+    const float total = block_reduce_sum(acc, sm.warp_scratch);
+    if (threadIdx.x == 0) {
+      *score_dst = total;
+      if (score_copy) *score_copy = total;
+    }
+  }
+  cx.steps += 1;
+  return true;
+}
+
+// ---------------------------------------------------------------- kernel
+// Trace mode: `count` events from f.inputs, positions derived from the stored
+// one plus the event index and stored once at the end. Persistent mode: the
+// mailbox worker of k2_persistent (reference src/cuda/Runtime.cu:58-122):
+// CTA 0 polls the mapped mailbox, stages the event and publishes each command
+// on a tagged control word every CTA polls; the score CTA publishes RUN
+// completions; RESET ends with a count of CTAs on the barrier counter.
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 1) k4_flow(StepArgs a, FlowLaunch f) {
+  extern __shared__ __align__(128) unsigned char flow_raw[];
+  FlowSmem& sm = *reinterpret_cast<FlowSmem*>(flow_raw);
+  FlowRing& fr = *reinterpret_cast<FlowRing*>(flow_raw + sizeof(FlowSmem));
+  if (!cluster_shape_ok(a)) {
+    if (f.mode == kFlowPersistent && blockIdx.x == 0) persistent_exit<T>(a, f.p);
+    return;
+  }
+  FlowCtx cx;
+  cx.rank = cluster_rank();
+  cx.cs = cluster_size();
+  cx.id = cluster_id();
+  cx.nc = cluster_count();
+  cx.n = D / (int)cx.cs;
+  cx.seg0 = (int)cx.rank * cx.n;
+  cx.heads_here = (int)cx.id < a.heads;
+  cx.score_cluster = cx.id == cx.nc - 1;
+  cx.epoch = ld_cg_u64(a.flow_epoch);
+  cx.steps = 0;
+  const unsigned long long t0 = ld_cg_u64(a.position);
+  for (int i = threadIdx.x; i < kFlowHd / 2; i += kThreads) sm.rope[i] = a.rope_freq[i];
+  if (cx.score_cluster && cx.rank == 0)
+    for (int i = threadIdx.x; i < D; i += kThreads) {
+      sm.fnorm[i] = Storage<T>::load((const T*)a.final_norm, i);
+      sm.fscore[i] = Storage<T>::load((const T*)a.score_w, i);
+    }
+  FlowCur cur{0};
+  const Where wh{(int)cx.rank, (int)cx.cs, (int)cx.id, (int)cx.nc};
+  const bool ring_ok = flow_ring_begin(a, fr, flow_raw + kFlowRingOffset, wh, sizeof(T),
+                                       f.mode == kFlowTrace ? f.count : 0ull);
+  if (!ring_ok && threadIdx.x == 0) set_error(a, kRingTable);
+  // every CTA of the cluster learns every rank's setup verdict
+  if (threadIdx.x < cx.cs) dsmem_store_u32(&sm.okv[kSiteSetup][cx.rank], threadIdx.x, ring_ok ? 1 : 0);
+  cluster_sync();
+  bool ok = true;
+  for (unsigned k = 0; k < cx.cs; ++k) ok = ok && (*reinterpret_cast<volatile int*>(&sm.okv[kSiteSetup][k]) != 0);
+  if (!ok) {
+    flow_drain(a, fr, cur);
+    if (f.mode == kFlowPersistent && blockIdx.x == 0) persistent_exit<T>(a, f.p);
+    return;
+  }
+
+  if (f.mode == kFlowTrace) {
+    for (unsigned long long e = 0; e < f.count && ok; ++e)
+      ok = flow_step<T, D>(a, fr, cur, sm, cx, f.inputs + e * kFlowFeatures, t0 + e, a.score,
+                           f.scores ? f.scores + e : nullptr);
+    if (ok && cx.score_cluster && cx.rank == 0 && threadIdx.x == 0) {
+      a.position[0] = t0 + f.count;
+      *a.flow_epoch = cx.epoch + f.count * (unsigned long long)a.layers;
+    }
+    flow_drain(a, fr, cur);
+    return;
+  }
+
+  // ---- persistent worker
+  const PersistArgs& p = f.p;
+  unsigned long long previous = p.initial_sequence, dispatched = 0, processed = 0, counts = 0;
+  bool exit_loop = false;
+  while (!exit_loop) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      const unsigned long long start = globaltimer();
+      unsigned long long seq;
+      int command = 0, arg = 0;
+      while ((seq = ld_acquire_sys(&p.mailbox->request)) == previous) {
+        if (globaltimer() - start >= p.idle_ns) { command = kFlowExit; break; }
+        if (p.backoff) __nanosleep(128);
+      }
+      if (command == 0) {
+        command = *reinterpret_cast<volatile int*>(&p.mailbox->command);
+        arg = *reinterpret_cast<volatile int*>(&p.mailbox->arg);
+        if (command == kRun)
+          for (int i = 0; i < kFlowFeatures; ++i) const_cast<float*>(a.input)[i] = __ldcv(f.mapped_input + i);
+        *a.flow_seq = seq;
+        previous = seq;
+      }
+      const unsigned long long word = ((dispatched + 1ull) << 32) | ((unsigned long long)(unsigned)(arg + 1) << 8) |
+                                      (unsigned long long)command;
+      __threadfence();
+      asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(a.flow_ctl), "l"(word) : "memory");
+    }
+    if (threadIdx.x == 0) {
+      const unsigned long long want = dispatched + 1ull;
+      const unsigned long long start = globaltimer();
+      unsigned long long w;
+      unsigned polls = 0;
+      while (((w = ld_acquire_gpu(a.flow_ctl)) >> 32) != (want & 0xffffffffull)) {
+        if ((++polls & 63u) == 0) {
+          if (ld_volatile_int(a.error) != 0) { w = kFlowExit; break; }
+          if (globaltimer() - start > p.dispatch_timeout_ns) {
+            set_error(a, kBarrierTimeout);
+            w = kFlowExit;
+            break;
+          }
+        }
+        flow_fill(fr);
+      }
+      sm.cmd = w;
+    }
+    __syncthreads();
+    const unsigned long long word = *reinterpret_cast<volatile unsigned long long*>(&sm.cmd);
+    const int command = (int)(word & 0xffull);
+    const int arg = (int)((word >> 8) & 0xffffffull) - 1;
+    dispatched += 1;
+    if (command == kRun) {
+      const unsigned long long t = ld_cg_u64(a.position);
+      if (!flow_step<T, D>(a, fr, cur, sm, cx, a.input, t, a.score, nullptr)) break;
+      if (cx.score_cluster && cx.rank == 0 && threadIdx.x == 0) {
+        a.position[0] = t + 1;
+        const unsigned long long seq = ld_cg_u64(a.flow_seq);
+        __threadfence_system();
+        st_release_sys(&p.mailbox->completion, seq);
+      }
+      processed += 1;
+      if (p.max_events && processed >= p.max_events) exit_loop = true;
+    } else if (command == kReset || command == kPing) {
+      // Every CTA takes the command before CTA 0 completes it, so the control
+      // word is not rewritten while a CTA has yet to read it.
+      if (command == kReset) reset_streams<T>(a, 0, 1);  // one stream: arg -1 and 0 both reset it
+      (void)arg;
+      __syncthreads();
+      counts += 1;
+      if (threadIdx.x == 0) {
+        __threadfence();
+        red_release_gpu_add(a.bar_counter, 1ull);
+      }
+      if (blockIdx.x == 0 && threadIdx.x == 0) {
+        const unsigned long long target = f.bar_base + counts * gridDim.x;
+        const unsigned long long start = globaltimer();
+        bool good = true;
+        while (ld_acquire_gpu(a.bar_counter) < target)
+          if (globaltimer() - start > a.bar_timeout_ns) { set_error(a, kBarrierTimeout); good = false; break; }
+        if (good) {
+          if (command == kPing) {
+            unsigned long long checksum = 0;
+            for (int i = 0; i < a.features; ++i) checksum += __float_as_uint(__ldcv(f.mapped_input + i));
+            *reinterpret_cast<volatile unsigned long long*>(&p.mailbox->checksum) = checksum;
+          }
+          const unsigned long long seq = ld_cg_u64(a.flow_seq);
+          __threadfence_system();
+          st_release_sys(&p.mailbox->completion, seq);
+        }
+      }
+    } else if (command == kStop) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) {
+        const unsigned long long seq = ld_cg_u64(a.flow_seq);
+        __threadfence_system();
+        st_release_sys(&p.mailbox->completion, seq);
+      }
+      exit_loop = true;
+    } else {
+      exit_loop = true;  // idle budget, error or an unknown command
+    }
+  }
+  // Leave together: every CTA counts itself out; CTA 0 then stores the tag
+  // base for the next launch and tells the host.
+  cluster_sync();
+  flow_drain(a, fr, cur);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    red_release_gpu_add(a.bar_counter, 1ull);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    const unsigned long long target = f.bar_base + (counts + 1ull) * gridDim.x;
+    const unsigned long long start = globaltimer();
+    while (ld_acquire_gpu(a.bar_counter) < target)
+      if (globaltimer() - start > a.bar_timeout_ns) { set_error(a, kBarrierTimeout); break; }
+    *a.flow_epoch = cx.epoch + processed * (unsigned long long)a.layers;
+  }
+  if (blockIdx.x == 0) persistent_exit<T>(a, p);
+}
+
+}  // namespace st

@@ -33,7 +33,8 @@
 #include <vector>
 
 #include "../../include/streaming_b200.h"
-#include "st_kernels.cuh"
+#include "st_flow.cuh"
+#include "st_flow_host.h"
 
 using namespace st;
 
@@ -153,6 +154,12 @@ struct st_runtime {
   // for 4 or more streams when the model allows it; ST_BATCHED=0/1 overrides.
   bool batched = false;
   bool tc = false;        // batched GEMM phases on the tensor cores (16-bit modes)
+  // One stream at the benchmark shapes: the device-loop backends (FUSED,
+  // PERSISTENT, device traces) run the flow kernel (st_flow.cuh) on its own
+  // cluster shape; ST_FLOW=0 selects the generic kernels.
+  bool flow = false;
+  const void* flow_fn = nullptr;
+  int fcluster = 0, fnclusters = 0, fgrid = 0;
   int bgrid = 0;
   int bsplit[4] = {1, 1, 1, 1};
   size_t tc_smem = 0;     // dynamic shared memory of the tensor-core rounds kernel
@@ -327,7 +334,32 @@ int launch_reset(st_runtime* rt, int s0, int s1) {
   return launch_ex(rt, ST_KERNEL(rt, reset), rt->grid, rt->cluster, false, p);
 }
 
+// The flow kernel's arguments: its own cluster shape in place of the generic one.
+StepArgs flow_args(const st_runtime* rt, const StepArgs& a0) {
+  StepArgs a = a0;
+  a.cluster_size = rt->fcluster;
+  a.clusters = rt->fnclusters;
+  return a;
+}
+
+int launch_flow(st_runtime* rt, const StepArgs& a0, const FlowLaunch& f) {
+  const cudaError_t e = flow_launch(rt->flow_fn, rt->fgrid, rt->fcluster, rt->stream, flow_args(rt, a0), f);
+  rt->launches += 1;
+  return rt->cuda(e, "flow cluster launch");
+}
+
+int launch_flow_trace(st_runtime* rt, const StepArgs& a, const float* inputs, unsigned long long count, float* scores) {
+  FlowLaunch f{};
+  f.mode = kFlowTrace;
+  f.inputs = inputs;
+  f.count = count;
+  f.scores = scores;
+  f.bar_base = rt->bar_base;
+  return launch_flow(rt, a, f);
+}
+
 int launch_fused(st_runtime* rt, const StepArgs& a0) {
+  if (rt->flow) return launch_flow_trace(rt, a0, a0.input, 1, nullptr);
   StepArgs a = a0;
   unsigned long long base = rt->bar_base;
   void* params[] = {&a, &base};
@@ -338,6 +370,7 @@ int launch_fused(st_runtime* rt, const StepArgs& a0) {
 
 int launch_trace(st_runtime* rt, const StepArgs& a0, const float* inputs, unsigned long long count, float* scores,
                  bool timeline = false) {
+  if (rt->flow && !timeline) return launch_flow_trace(rt, a0, inputs, count, scores);
   StepArgs a = a0;
   unsigned long long base = rt->bar_base;
   void* params[] = {&a, &inputs, &count, &scores, &base};
@@ -375,7 +408,8 @@ int check_device_error(st_runtime* rt) {
 int preload(st_runtime* rt) {
   const void* fns[] = {ST_KERNEL(rt, input), ST_KERNEL(rt, attention), ST_KERNEL(rt, ffn), ST_KERNEL(rt, final_),
                        ST_KERNEL(rt, reset), ST_LOOP_KERNEL(rt, fused), ST_LOOP_KERNEL(rt, trace), ST_LOOP_KERNEL(rt, persistent),
-                       ST_TIMELINE_KERNEL(rt), ST_KERNEL(rt, convert), rounds_fn(rt)};
+                       ST_TIMELINE_KERNEL(rt), ST_KERNEL(rt, convert), rounds_fn(rt),
+                       rt->flow ? rt->flow_fn : ST_KERNEL(rt, input)};
   for (const void* f : fns) {
     cudaFuncAttributes fa{};
     ST_CUDA(rt, cudaFuncGetAttributes(&fa, f));
@@ -402,6 +436,17 @@ int start_persistent(st_runtime* rt) {
   a.score = rt->out_d;
   const float* mapped = rt->in_d;
   unsigned long long base = rt->bar_base;
+  if (rt->flow) {
+    FlowLaunch f{};
+    f.mode = kFlowPersistent;
+    f.p = p;
+    f.mapped_input = mapped;
+    f.bar_base = base;
+    ST_CUDA(rt, cudaMemsetAsync(rt->args.flow_ctl, 0, sizeof(unsigned long long), rt->stream));
+    ST_TRY(launch_flow(rt, a, f));
+    rt->running = true;
+    return ST_OK;
+  }
   void* params[] = {&a, &p, &mapped, &base};
   ST_TRY(launch_ex(rt, persistent_fn(rt), rt->grid, rt->cluster, true, params));
   rt->running = true;
@@ -820,6 +865,53 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   const size_t bz16_at = take(rt->tc ? spad * (size_t)std::max(d, F) * 2 : 0);
   const size_t bar_at = take(sizeof(unsigned long long)), err_at = take(sizeof(int));
   const size_t rope_at = take((hd / 2) * sizeof(float)), ctl_at = take(sizeof(Control));
+  // flow kernel: choose it and its cluster shape (largest cluster whose
+  // co-resident count still gives every head its own cluster).
+  {
+    const char* env = std::getenv("ST_FLOW");
+    const int mode_index = m.mode == ST_MODE_FP16 ? 1 : m.mode == ST_MODE_BF16 ? 2 : 0;
+    rt->flow_fn = flow_kernel(mode_index, d);
+    const bool want = rt->flow_fn && S == 1 && hd == kFlowHd && m.features == kFlowFeatures && o.blocks == 0 &&
+                      !rt->batched && coop && !(env && env[0] == '0');
+    if (want) {
+      if (rt->cuda(cudaFuncSetAttribute(rt->flow_fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)flow_smem_bytes()), "cudaFuncSetAttribute flow") != ST_OK)
+        return bail(ST_ERR_CUDA);
+      int best_cs = 0, best_nc = 0;
+      for (int cs : {8, 4}) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(cs);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = flow_smem_bytes();
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = cs;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int nmax = 0;
+        if (rt->cuda(cudaOccupancyMaxActiveClusters(&nmax, rt->flow_fn, &cfg), "cudaOccupancyMaxActiveClusters flow") != ST_OK)
+          return bail(ST_ERR_CUDA);
+        const int nc = std::min(nmax, rt->sms / cs);
+        if (nc < 1) continue;
+        if (best_cs == 0 || (best_nc < m.heads && nc >= m.heads)) {
+          best_cs = cs;
+          best_nc = nc;
+        }
+        if (best_nc >= m.heads) break;
+      }
+      if (best_cs > 0) {
+        rt->flow = true;
+        rt->fcluster = best_cs;
+        rt->fnclusters = best_nc;
+        rt->fgrid = best_cs * best_nc;
+      }
+    }
+  }
+  const size_t llh_at = take(rt->flow ? 2 * (size_t)m.heads * d * 8 : 0);
+  const size_t llc_at = take(rt->flow ? 2 * (size_t)rt->fnclusters * d * 8 : 0);
+  const size_t fwords_at = take(3 * sizeof(unsigned long long));
   rt->scratch_bytes = co;
   if (rt->cuda(cudaMalloc(&rt->scratch, co), "cudaMalloc scratch") != ST_OK) return bail(ST_ERR_CUDA);
   if (rt->cuda(cudaMemsetAsync(rt->scratch, 0, co, rt->stream), "cudaMemset scratch") != ST_OK) return bail(ST_ERR_CUDA);
@@ -944,6 +1036,12 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
     rt->ring = ring_supported(a, rt->elem, rt->cluster, rt->nclusters) && !(env && env[0] == '0');
   }
   rt->control = (Control*)(rt->scratch + ctl_at);
+  a.ll_heads = (unsigned long long*)(rt->scratch + llh_at);
+  a.ll_clusters = (unsigned long long*)(rt->scratch + llc_at);
+  a.flow_epoch = (unsigned long long*)(rt->scratch + fwords_at);
+  a.flow_ctl = a.flow_epoch + 1;
+  a.flow_seq = a.flow_epoch + 2;
+  if (rt->flow && !flow_shape_ok(a, rt->elem, rt->fcluster, rt->fnclusters)) rt->flow = false;
   *out = rt;
   return ST_OK;
 }
@@ -1324,6 +1422,11 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     kernel = ST_KERNEL(rt, ffn);
     name = "k2_ffn (per-op block kernels)";
   }
+  const bool flow_loop = rt->flow && (rt->opt.backend == ST_BACKEND_FUSED || rt->opt.backend == ST_BACKEND_PERSISTENT);
+  if (flow_loop) {
+    kernel = rt->flow_fn;
+    name = "k4_flow";
+  }
   cudaFuncGetAttributes(&fa, kernel);
   static const char* backends[] = {"cuda", "graph", "cublas", "cublas-graph", "fused", "persistent"};
   static const char* modes[] = {"fp32", "fp16", "bf16"};
@@ -1333,13 +1436,14 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     << "\",\"blocks\":" << rt->grid << ",\"legal_cooperative_blocks\":" << rt->legal_blocks
     << ",\"threads\":" << kThreads << ",\"resource_kernel\":\"" << name << "\""
     << ",\"registers_per_thread\":" << fa.numRegs << ",\"local_bytes\":" << fa.localSizeBytes
-    << ",\"shared_bytes\":" << fa.sharedSizeBytes << ",\"dynamic_shared_bytes\":" << kSmem2
-    << ",\"cluster\":" << rt->cluster << ",\"clusters\":" << rt->nclusters
+    << ",\"shared_bytes\":" << fa.sharedSizeBytes << ",\"dynamic_shared_bytes\":" << (flow_loop ? flow_smem_bytes() : kSmem2)
+    << ",\"cluster\":" << (flow_loop ? rt->fcluster : rt->cluster) << ",\"clusters\":" << (flow_loop ? rt->fnclusters : rt->nclusters)
+    << ",\"flow\":" << (rt->flow ? "true" : "false") << ",\"flow_grid\":" << rt->fgrid
     << ",\"cooperative_clusters\":" << (rt->coop_clusters ? "true" : "false")
     << ",\"weight_ring\":" << (rt->ring ? "true" : "false") << ",\"l2_keep_layers\":" << rt->args.l2_keep_layers
     << ",\"attention_implementation\":\"one cluster per head, window split over the cluster, partials merged through DSMEM\""
     << ",\"matvec_implementation\":\"16-byte non-temporal loads; out- and down-projections K-split (per head, per ffn slice)\""
-    << ",\"barriers_per_step\":" << forward_barrier_count(rt)
+    << ",\"barriers_per_step\":" << (flow_loop ? 0 : forward_barrier_count(rt))
     << ",\"transport\":\"" << (rt->opt.backend == ST_BACKEND_PERSISTENT ? "mapped-system-load-store" : rt->opt.mapped ? "mapped-stream-sync" : "pinned-copy-stream-sync") << "\""
     << ",\"poll_policy\":\"" << (rt->opt.backoff ? "bounded-device-backoff-host-yield" : "tight") << "\""
     << ",\"workspace_storage\":\"FP32 with explicit rounding to the storage type\""

@@ -101,17 +101,23 @@ def test_odd_shapes_take_the_scalar_paths(mode):
 
 
 def test_fp32_is_bit_stable_across_runs_and_backends():
+    # Fixed reduction orders: a kernel family gives the same bits on every run.
+    # GRAPH runs the per-op kernels; FUSED and PERSISTENT run the single-stream
+    # flow kernel at this shape, whose sums are associated differently, so the
+    # two families agree within the fp32 policy rather than bit for bit.
     g = Golden("c1-small-fp32")
-    runs = []
-    for backend in (Backend.GRAPH, Backend.FUSED, Backend.PERSISTENT, Backend.GRAPH):
+    runs = {}
+    for backend in (Backend.GRAPH, Backend.FUSED, Backend.PERSISTENT, Backend.GRAPH, Backend.FUSED):
         rt = Runtime(g.model, RuntimeOptions(backend=backend, blocks=0))
         try:
-            runs.append(np.array([rt.step(e) for e in g.events[:40]]))
-            snap = rt.snapshot()
+            runs.setdefault(backend, []).append(np.array([rt.step(e) for e in g.events[:40]]))
         finally:
             rt.close()
-    for r in runs[1:]:
-        np.testing.assert_array_equal(r.view(np.uint32), runs[0].view(np.uint32))
+    graph, fused, persistent = runs[Backend.GRAPH], runs[Backend.FUSED], runs[Backend.PERSISTENT]
+    np.testing.assert_array_equal(graph[1].view(np.uint32), graph[0].view(np.uint32))
+    for r in fused[1:] + persistent:
+        np.testing.assert_array_equal(r.view(np.uint32), fused[0].view(np.uint32))
+    check_scores(fused[0], graph[0], g.model.config.layers, "fp32", "flow vs per-op")
 
 
 def test_device_trace_matches_step_by_step():
