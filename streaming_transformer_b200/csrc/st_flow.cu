@@ -29,6 +29,8 @@ const void* flow_kernel(int mode, int width) {
 
 size_t flow_smem_bytes() { return kFlowSmemBytes; }
 
+int flow_threads() { return kFlowThreads; }
+
 bool flow_shape_ok(const StepArgs& a, size_t elem, int cluster, int clusters) {
   if (a.streams != 1 || a.head_dim != kFlowHd || a.features != kFlowFeatures) return false;
   if (a.width != 256 && a.width != 512 && a.width != 1024) return false;
@@ -48,7 +50,7 @@ cudaError_t flow_launch(const void* fn, int grid, int cluster, cudaStream_t stre
   void* params[] = {&a, &f};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(kFlowThreads);
   cfg.dynamicSmemBytes = kFlowSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr;

@@ -76,7 +76,8 @@ constexpr int kFlowMaxChunks = 320;            // chunks per step one CTA may co
 constexpr int kFlowKvBytes = 16 * 1024;        // K and V rows one CTA prefetches per head
 constexpr int kFlowMaxD = 1024;
 constexpr int kFlowMaxAct = 512;               // SwiGLU outputs per CTA
-constexpr int kFlowIssuer = kThreads - 32;     // lane 0 of the last warp
+constexpr int kFlowThreads = kThreads + 32;    // 16 compute warps and the producer warp
+constexpr int kFlowProducer = kThreads;        // lane 0 of the producer warp
 
 enum FlowMode : int { kFlowTrace = 0, kFlowPersistent = 1 };
 enum FlowCommand : int { kFlowExit = 15 };
@@ -142,6 +143,22 @@ __host__ __device__ inline int flow_chunks_per_step(const StepArgs& a, const Whe
   return n;
 }
 
+// Rows, chunk count and rows per chunk of one span of this CTA. The same for
+// every layer and head, so computed once per launch (flow_plan) and read from
+// shared memory by the phases (the span arithmetic divides by runtime values).
+struct FlowSpan {
+  int rows, chunks, rpc;
+};
+struct FlowPlan {
+  FlowSpan in, qkv, out, gateup, down;
+  int qkv_lo;   // first q/k/v row pair of this rank within the head
+};
+__device__ inline FlowSpan flow_span(const StepArgs& a, const Where& w, int kind, size_t elem) {
+  const Span s = span_of(a, w, kind, 0, w.id < a.heads ? w.id : 0, elem);
+  const FlowSplit sp = flow_split(s, kind);
+  return {s.rows, sp.chunks, sp.rows_per_chunk};
+}
+
 // ---------------------------------------------------------------- shared memory
 struct FlowChunk {
   const char* src;
@@ -159,36 +176,82 @@ struct alignas(128) FlowRing {
   unsigned char* buf;
   unsigned capacity, head_off;
   int next, nchunks, failed, ok;
+  int stop;                              // the compute warps have left; the producer stops issuing
+  int tl_n;                              // timeline marks written (diagnostics)
   FlowChunk table[kFlowMaxChunks];
 };
 
 // Every DSMEM target sits at the same offset in every CTA of the cluster.
+// Exchange sites: data every rank of the cluster writes into its peers' shared
+// memory with st.async, each store completing its byte count on the
+// receiver's mbarrier for the site (no cluster barrier). Every site is double
+// buffered by the parity of its exchange count: a sender reaches exchange
+// k + 2 of a site only after every receiver has sent its part of exchange
+// k + 1, which each does after its last read of exchange k's buffer.
+enum FlowSite : int { kSiteX = 0, kSiteX2 = 1, kSiteQkv = 2, kSiteAtt = 3, kSiteDred = 4, kSites = 5 };
+
 struct alignas(128) FlowSmem {
-  float x[kFlowMaxD];                    // residual entering the layer (DSMEM target)
-  float x2[kFlowMaxD];                   // residual after attention (DSMEM target)
+  unsigned long long sbar[kSites][2];    // receive mbarriers per site and parity
+  float x[2][kFlowMaxD];                 // residual entering the layer (site X)
+  float x2[2][kFlowMaxD];                // residual after attention (site X2)
   float z[kFlowMaxD];                    // norm output, GEMV input
-  float dred[kFlowMaxD];                 // down partials from every rank, [CS][n] (DSMEM target)
+  float dred[2][kFlowMaxD];              // down partials from every rank, [CS][n] (site DRED)
   float seg[kFlowMaxD];                  // this rank's segment values before publishing
   float fnorm[kFlowMaxD];                // final norm gain (score CTA)
   float fscore[kFlowMaxD];               // score weights (score CTA)
-  float qkv[3 * kFlowHd];                // q, k, v of the current head (DSMEM target)
-  float apart[kFlowMaxCluster][kFlowHd + 2];  // CTA attention partials per rank (DSMEM target)
+  float qkv[2][3 * kFlowHd];             // q, k, v of the current head (site QKV)
+  float apart[2][kFlowMaxCluster][kFlowHd + 2];  // CTA attention partials per rank (site ATT)
   float wpart[kWarps][kFlowHd + 2];      // warp attention partials
   float o[kFlowHd];                      // merged attention output (cast)
   float act[kFlowMaxAct];                // this CTA's SwiGLU slice
-  float ssx[kFlowMaxCluster][8];         // sum of squares of x per rank and warp (DSMEM target)
-  float ssx2[kFlowMaxCluster][8];        // same for x' (DSMEM target)
-  int okv[4][kFlowMaxCluster];           // verdict per rank, one row per publishing site (DSMEM target)
+  float ssx[2][kFlowMaxCluster][8];      // sum of squares of x per rank and warp (site X)
+  float ssx2[2][kFlowMaxCluster][8];     // same for x' (site X2)
+  int okx[2][kFlowMaxCluster];           // verdict per rank (site X)
+  int okx2[2][kFlowMaxCluster];          // verdict per rank (site X2)
+  int oksetup[kFlowMaxCluster];          // launch setup verdict per rank
   float2 rope_cs[kFlowHd / 2];           // cos, sin of t * frequency
   float rope[kFlowHd / 2];               // frequencies 10000^(-2i/hd)
   float ev[kFlowFeatures];               // the event
   float warp_scratch[kWarps];
   unsigned long long cmd;                // persistent: the dispatched command
+  FlowPlan plan;                         // this CTA's span geometry
   union {
     alignas(16) unsigned char kv[kFlowKvBytes];   // K rows then V rows of this CTA's slots
     float red[kFlowKvBytes / 4];                   // gather / down group partials
   } u;
 };
+
+// ---------------------------------------------------------------- timeline
+// Phase marks of thread 0 of CTA a.timeline_cta, (clock64() << 8) | tag, when
+// a timeline buffer is given (diagnostics; one predictable branch otherwise).
+// With a.timeline_cta < 0 every CTA records pairs {tag, globaltimer ns} into
+// its own region of a.timeline_capacity / gridDim.x entries, for cross-CTA
+// comparisons.
+enum FlowMark : int {
+  kFmStep = 1, kFmIn, kFmNorm1, kFmQkv, kFmQkvSync, kFmAttn, kFmPartSync, kFmMerge, kFmOut, kFmGather1,
+  kFmPub2, kFmNorm2, kFmGateUp, kFmDown, kFmDredSync, kFmDpub, kFmGather2, kFmPub1, kFmScore, kFmAcqStart,
+  kFmAcqEnd, kFmBarIn, kFmBarOut
+};
+__device__ __forceinline__ void fmark(const StepArgs& a, FlowRing& fr, int tag) {
+  if (a.timeline != nullptr && threadIdx.x == 0) {
+    if ((int)blockIdx.x == a.timeline_cta) {
+      const int i = fr.tl_n;
+      if (i < a.timeline_capacity / kWarps) {
+        a.timeline[i] = (long long)((clock64() << 8) | (long long)tag);
+        fr.tl_n = i + 1;
+      }
+    } else if (a.timeline_cta < 0) {
+      const int per = a.timeline_capacity / (int)gridDim.x;
+      const int i = fr.tl_n;
+      if (2 * i + 1 < per) {
+        long long* r = a.timeline + (size_t)blockIdx.x * per;
+        r[2 * i] = tag;
+        r[2 * i + 1] = (long long)globaltimer();
+        fr.tl_n = i + 1;
+      }
+    }
+  }
+}
 
 constexpr size_t kFlowRingOffset = (sizeof(FlowSmem) + sizeof(FlowRing) + 127) / 128 * 128;
 constexpr size_t kFlowSmemBytes = kSmemLimit - kStaticSmemReserve;
@@ -224,52 +287,126 @@ __device__ __forceinline__ void dsmem_store4(float* local, unsigned rank, float4
                : "memory");
 }
 
-// ---------------------------------------------------------------- ring
-// The issuer: reclaim released chunks, then issue while a slot and enough
-// free bytes are available and the launch limit allows.
-static __device__ __noinline__ void flow_fill_slow(FlowRing& fr) {
-  while (fr.released < fr.issued &&
-         mbar_test_wait(&fr.empty[fr.released % kFlowSlots], (unsigned)((fr.released / kFlowSlots) & 1ull))) {
-    fr.tail = fr.end[fr.released % kFlowSlots];
-    fr.released += 1;
-  }
-  while (fr.issued < fr.limit && fr.issued < fr.released + kFlowSlots) {
-    const FlowChunk c = fr.table[fr.next];
-    const unsigned alloc = (c.bytes + 127u) & ~127u;
-    unsigned long long pos = fr.head;
-    unsigned off = fr.head_off;
-    if (off + alloc > fr.capacity) {  // never split a chunk across the end
-      pos += fr.capacity - off;
-      off = 0;
-    }
-    if (pos + alloc - fr.tail > fr.capacity) return;
-    const int slot = (int)(fr.issued % kFlowSlots);
-    fr.off[slot] = off;
-    fr.end[slot] = pos + alloc;
-    fr.head = pos + alloc;
-    fr.head_off = off + alloc == fr.capacity ? 0u : off + alloc;
-    mbar_expect_tx(&fr.full[slot], c.bytes);
-    bulk_copy(fr.buf + off, c.src, c.bytes, &fr.full[slot], c.keep ? fr.keep_policy : fr.stream_policy);
-    fr.next = fr.next + 1 == fr.nchunks ? 0 : fr.next + 1;
-    fr.issued += 1;
-  }
+// st.async: a store into CTA `rank`'s shared memory at the offset of `local`,
+// completing its bytes on that CTA's mbarrier at the offset of `bar`.
+__device__ __forceinline__ unsigned flow_remote(const void* local, unsigned rank) {
+  unsigned r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"((unsigned)__cvta_generic_to_shared(local)), "r"(rank));
+  return r;
 }
-__device__ __forceinline__ void flow_fill(FlowRing& fr) {
-  if (threadIdx.x == kFlowIssuer) flow_fill_slow(fr);
+__device__ __forceinline__ void st_async1(const float* dst, const unsigned long long* bar, unsigned rank, float v) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];"
+               ::"r"(flow_remote(dst, rank)), "f"(v), "r"(flow_remote(bar, rank)) : "memory");
+}
+__device__ __forceinline__ void st_async1i(const int* dst, const unsigned long long* bar, unsigned rank, int v) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
+               ::"r"(flow_remote(dst, rank)), "r"(v), "r"(flow_remote(bar, rank)) : "memory");
+}
+__device__ __forceinline__ void st_async2(const float* dst, const unsigned long long* bar, unsigned rank, float v0,
+                                          float v1) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
+               ::"r"(flow_remote(dst, rank)), "f"(v0), "f"(v1), "r"(flow_remote(bar, rank)) : "memory");
+}
+__device__ __forceinline__ void st_async4(const float* dst, const unsigned long long* bar, unsigned rank, float4 v) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+               ::"r"(flow_remote(dst, rank)), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(flow_remote(bar, rank))
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(unsigned long long* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"((unsigned)__cvta_generic_to_shared(bar)), "r"(parity) : "memory");
+  return ok != 0;
 }
 
-// Per-thread consumer position (uniform across the CTA).
+// ---------------------------------------------------------------- ring
+// Compute threads (warps 0-15) meet at named barrier 1; the producer warp
+// (warp 16) never joins it, so issuing never holds up a compute phase.
+__device__ __forceinline__ void flow_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
+__device__ __forceinline__ bool flow_bar_and(bool p) {
+  int r;
+  asm volatile(
+      "{\n\t.reg .pred a, r;\n\t"
+      "setp.ne.u32 a, %1, 0;\n\t"
+      "bar.red.and.pred r, 1, %2, a;\n\t"
+      "selp.u32 %0, 1, 0, r;\n\t}"
+      : "=r"(r) : "r"((unsigned)p), "n"(kThreads) : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void flow_bsync(FlowRing&) { flow_bar(); }
+
+// The producer: reclaim the bytes of chunks every compute warp has released,
+// then issue the next chunk of the table (cp.async.bulk global -> this CTA's
+// shared memory, completion on its full mbarrier, no multicast) as soon as a
+// slot and its bytes are free. Leaves when the launch's chunks are issued or
+// the compute warps set fr.stop, after waiting for the copies in flight;
+// every wait is bounded by wait_ns without progress.
+__device__ inline void flow_produce(const StepArgs& a, FlowRing& fr, unsigned long long wait_ns) {
+  unsigned long long since = globaltimer();
+  while (fr.issued < fr.limit) {
+    while (fr.released < fr.issued &&
+           mbar_test_wait(&fr.empty[fr.released % kFlowSlots], (unsigned)((fr.released / kFlowSlots) & 1ull))) {
+      fr.tail = fr.end[fr.released % kFlowSlots];
+      fr.released += 1;
+    }
+    bool issued = false;
+    if (fr.issued < fr.released + kFlowSlots) {
+      const FlowChunk c = fr.table[fr.next];
+      const unsigned alloc = (c.bytes + 127u) & ~127u;
+      unsigned long long pos = fr.head;
+      unsigned off = fr.head_off;
+      if (off + alloc > fr.capacity) {  // never split a chunk across the end
+        pos += fr.capacity - off;
+        off = 0;
+      }
+      if (pos + alloc - fr.tail <= fr.capacity) {
+        const int slot = (int)(fr.issued % kFlowSlots);
+        fr.off[slot] = off;
+        fr.end[slot] = pos + alloc;
+        fr.head = pos + alloc;
+        fr.head_off = off + alloc == fr.capacity ? 0u : off + alloc;
+        mbar_expect_tx(&fr.full[slot], c.bytes);
+        bulk_copy(fr.buf + off, c.src, c.bytes, &fr.full[slot], c.keep ? fr.keep_policy : fr.stream_policy);
+        fr.next = fr.next + 1 == fr.nchunks ? 0 : fr.next + 1;
+        fr.issued += 1;
+        issued = true;
+      }
+    }
+    if (issued) {
+      since = globaltimer();
+      continue;
+    }
+    if (*reinterpret_cast<volatile int*>(&fr.stop)) break;
+    // sleep until the oldest outstanding chunk is released
+    mbar_try_wait_for(&fr.empty[fr.released % kFlowSlots], (unsigned)((fr.released / kFlowSlots) & 1ull), 2000u);
+    if (globaltimer() - since > wait_ns) {
+      set_error(a, kBarrierTimeout);
+      break;
+    }
+  }
+  // copies still in flight land before the CTA may leave
+  for (unsigned long long c = fr.released; c < fr.issued; ++c) {
+    const int slot = (int)(c % kFlowSlots);
+    const unsigned parity = (unsigned)((c / kFlowSlots) & 1ull);
+    const unsigned long long start = globaltimer();
+    while (!mbar_try_wait(&fr.full[slot], parity))
+      if (globaltimer() - start > a.bar_timeout_ns) break;
+  }
+}
+
+// Per-thread consumer position (uniform across the compute warps).
 struct FlowCur {
   unsigned long long consumed;
 };
 
 static __device__ __noinline__ bool flow_wait_slow(FlowRing& fr, int slot, unsigned parity,
                                                    unsigned long long timeout_ns) {
-  const bool issuer = threadIdx.x == kFlowIssuer;
   const unsigned long long start = globaltimer();
   while (true) {
-    flow_fill(fr);
-    if (mbar_try_wait_for(&fr.full[slot], parity, issuer ? 200u : 20000u)) return true;
+    if (mbar_try_wait_for(&fr.full[slot], parity, 20000u)) return true;
     if (globaltimer() - start > timeout_ns) return false;
   }
 }
@@ -280,46 +417,34 @@ static __device__ __noinline__ bool flow_wait_slow(FlowRing& fr, int slot, unsig
 __device__ __forceinline__ const unsigned char* flow_acquire(const StepArgs& a, FlowRing& fr, const FlowCur& cur) {
   const int slot = (int)(cur.consumed % kFlowSlots);
   const unsigned parity = (unsigned)((cur.consumed / kFlowSlots) & 1ull);
+  fmark(a, fr, kFmAcqStart);
   if (!mbar_try_wait(&fr.full[slot], parity) && !*reinterpret_cast<volatile int*>(&fr.failed) &&
       !flow_wait_slow(fr, slot, parity, a.bar_timeout_ns)) {
     fr.failed = 1;
     set_error(a, kBarrierTimeout);
   }
+  fmark(a, fr, kFmAcqEnd);
   return fr.buf + (*reinterpret_cast<volatile int*>(&fr.failed) ? 0u : fr.off[slot]);
 }
 
-// Every thread of a warp, after the warp's last read of the chunk (or without
-// reading it): one arrival per warp on its empty mbarrier.
+// Every thread of a compute warp, after the warp's last read of the chunk (or
+// without reading it): one arrival per warp on its empty mbarrier.
 __device__ __forceinline__ void flow_release(FlowRing& fr, FlowCur& cur) {
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(&fr.empty[cur.consumed % kFlowSlots]);
   cur.consumed += 1;
-  flow_fill(fr);
 }
 
-// Wait for every issued copy (bounded) before the CTA leaves.
-__device__ inline void flow_drain(const StepArgs& a, FlowRing& fr, const FlowCur& cur) {
-  if (threadIdx.x == kFlowIssuer && fr.ok) {
-    for (unsigned long long c = cur.consumed; c < fr.issued; ++c) {
-      const int slot = (int)(c % kFlowSlots);
-      const unsigned parity = (unsigned)((c / kFlowSlots) & 1ull);
-      const unsigned long long start = globaltimer();
-      while (!mbar_try_wait(&fr.full[slot], parity))
-        if (globaltimer() - start > a.bar_timeout_ns) break;
-    }
-  }
-  __syncthreads();
-}
-
-// All threads: the chunk table (issuer), mbarriers, first issues. `limit`
-// bounds the chunks issued (0: unbounded). Returns false when the table does
-// not fit (the host checks this before choosing the kernel).
+// Every thread: the chunk table and mbarriers (built by the producer lane).
+// `steps` bounds the chunks issued (0: unbounded). Returns false when the
+// table does not fit (the host checks this before choosing the kernel).
 __device__ inline bool flow_ring_begin(const StepArgs& a, FlowRing& fr, unsigned char* buf, const Where& w,
                                        size_t elem, unsigned long long steps) {
-  if (threadIdx.x == kFlowIssuer) {
+  if (threadIdx.x == kFlowProducer) {
     fr.head = fr.tail = fr.issued = fr.released = 0;
     fr.head_off = 0;
     fr.failed = 0;
+    fr.stop = 0;
     fr.keep_policy = policy_evict_last();
     fr.stream_policy = policy_evict_first();
     fr.buf = buf;
@@ -364,9 +489,7 @@ __device__ inline bool flow_ring_begin(const StepArgs& a, FlowRing& fr, unsigned
     }
   }
   __syncthreads();
-  const bool ok = fr.ok != 0;
-  if (ok) flow_fill(fr);
-  return ok;
+  return fr.ok != 0;
 }
 
 // ---------------------------------------------------------------- warp GEMV
@@ -428,25 +551,21 @@ __device__ __forceinline__ void flow_dot(const T* row, int sl, const FlowX<T, K>
 // Rows of span s from the ring, U rows per group; epi(row, v[U]) runs on lane
 // 0 of each valid group (row relative to the span). Passes of RPP groups are
 // dealt to warps round robin across the span's chunks; a warp without a pass
-// in a chunk releases it without waiting (except the issuer's warp).
+// in a chunk releases it without waiting.
 template <typename T, int K, int U, class Epi>
-__device__ __forceinline__ void flow_rows(const StepArgs& a, FlowRing& fr, FlowCur& cur, const Span& s, int kind,
+__device__ __forceinline__ void flow_rows(const StepArgs& a, FlowRing& fr, FlowCur& cur, const FlowSpan sp,
                                           const FlowX<T, K>& x, Epi&& epi) {
   using R = FlowRow<T, K>;
-  const FlowSplit sp = flow_split(s, kind);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane / R::LPR, sl = lane - sub * R::LPR;
   constexpr int pr = U * R::RPP;
   int pass0 = 0;
   for (int c = 0; c < sp.chunks; ++c) {
-    const int r0 = c * sp.rows_per_chunk;
-    const int n = min(sp.rows_per_chunk, s.rows - r0);
+    const int r0 = c * sp.rpc;
+    const int n = min(sp.rpc, sp.rows - r0);
     const int passes = (n + pr - 1) / pr;
     const int first = (warp - pass0 % kWarps + kWarps) % kWarps;
-    // The issuer's warp waits for every chunk (issuing while it waits), so it
-    // never runs ahead to a barrier while other warps need a chunk it has
-    // yet to issue.
-    if (first < passes || warp == (kFlowIssuer >> 5)) {
+    if (first < passes) {
       const T* base = (const T*)flow_acquire(a, fr, cur);
       for (int p = first; p < passes; p += kWarps) {
         const int row = p * pr + sub * U;
@@ -499,8 +618,9 @@ __device__ __forceinline__ void flow_gain(const StepArgs& a, FlowRing& fr, FlowC
 template <int D>
 __device__ __forceinline__ bool flow_gather(const StepArgs& a, FlowRing& fr, const unsigned long long* rec, int nsrc,
                                             int seg0, int n, unsigned tag, FlowSmem& sm) {
-  const int np = n >> 1, G = kThreads / np;
-  const int e = (int)threadIdx.x % np, g = (int)threadIdx.x / np;
+  // n is a power of two (D / CS), so the thread split is by shifts.
+  const int np = n >> 1, lg = 31 - __clz(np), G = kThreads >> lg;
+  const int e = (int)threadIdx.x & (np - 1), g = (int)threadIdx.x >> lg;
   float s0 = 0.f, s1 = 0.f;
   bool ok = true;
   unsigned long long start = 0;
@@ -521,7 +641,6 @@ __device__ __forceinline__ bool flow_gather(const StepArgs& a, FlowRing& fr, con
 #pragma unroll
       for (int k = 0; k < 8; ++k) ready = ready && ll_tag(r[k][0]) == tag && ll_tag(r[k][1]) == tag;
       if (ready) break;
-      flow_fill(fr);
       if ((++polls & 31u) == 0) {
         if (ld_volatile_int(a.error) != 0) { ok = false; break; }
         const unsigned long long now = globaltimer();
@@ -537,42 +656,82 @@ __device__ __forceinline__ bool flow_gather(const StepArgs& a, FlowRing& fr, con
   }
   sm.u.red[g * n + 2 * e] = s0;
   sm.u.red[g * n + 2 * e + 1] = s1;
-  ok = __syncthreads_and(ok) != 0;
+  ok = flow_bar_and(ok);
   if ((int)threadIdx.x < n) {
     float t = 0.f;
     for (int k = 0; k < G; ++k) t += sm.u.red[k * n + threadIdx.x];
     sm.seg[threadIdx.x] = t;
   }
-  __syncthreads();
+  flow_bsync(fr);
   return ok;
 }
 
-// Publish this rank's segment: dst[seg0 + i] = sm.seg[i] (i < n) into every
-// rank of the cluster, with the segment's sum of squares (per warp) and this
-// CTA's verdict; ends with a cluster barrier. Returns the cluster's verdict.
-// A rank reads its row of verdicts right after the barrier; each publishing
-// site has its own row, and between two publishes at one site every rank
-// passes another cluster barrier, so a row is never rewritten while read.
-enum FlowSite : int { kSiteSetup = 0, kSiteIn = 1, kSiteX2 = 2, kSiteX = 3 };
-__device__ __forceinline__ bool flow_publish(float* dst, float (*ss)[8], int seg0, int n, unsigned rank,
-                                             unsigned cs, bool ok, int site, FlowSmem& sm) {
-  const int np = n >> 1;
-  const int t = (int)threadIdx.x;
+// ---------------------------------------------------------------- step context
+struct FlowCtx {
+  unsigned rank, cs, id, nc;
+  int n, seg0;
+  int slot, valid;           // t % W and the retained slot count of the current step
+  bool heads_here, score_cluster;
+  unsigned long long epoch;  // tag base of this launch
+  unsigned long long steps;  // steps this launch has run
+  unsigned k[kSites];        // exchanges so far per site (selects buffer and mbarrier phase)
+  unsigned bx, bx2;          // buffers holding the current x and x'
+};
+
+// Receive exchange k of a site: thread 0 arms the site's mbarrier with the
+// bytes every rank sends (one arrival), every thread waits for the phase to
+// complete (bounded; the issuer keeps issuing). False when the wait ran out.
+__device__ __forceinline__ bool flow_receive(const StepArgs& a, FlowRing& fr, FlowSmem& sm, int site, unsigned k,
+                                             unsigned bytes) {
+  unsigned long long* bar = &sm.sbar[site][k & 1u];
+  const unsigned parity = (k >> 1) & 1u;
+  if (threadIdx.x == 0) mbar_expect_tx(bar, bytes);
+  fmark(a, fr, kFmBarIn);
+  bool ok = true;
+  if (!mbar_try_wait_cluster(bar, parity)) {
+    const unsigned long long start = globaltimer();
+    unsigned polls = 0;
+    while (!mbar_try_wait_cluster(bar, parity)) {
+      if ((++polls & 63u) == 0 && globaltimer() - start > a.bar_timeout_ns) {
+        set_error(a, kBarrierTimeout);
+        ok = false;
+        break;
+      }
+    }
+  }
+  fmark(a, fr, kFmBarOut);
+  return ok;
+}
+
+// Publish this rank's segment (sm.seg[i], i < n) as x (site X) or x' (site
+// X2) of every rank, with the segment's per-warp sums of squares and this
+// CTA's verdict, then receive every rank's. Returns the cluster's verdict
+// (every CTA of the cluster sees the same flags).
+__device__ __forceinline__ bool flow_publish(const StepArgs& a, FlowRing& fr, FlowSmem& sm, FlowCtx& cx, int site,
+                                             bool ok) {
+  const unsigned k = cx.k[site]++;
+  const unsigned b = k & 1u;
+  float* dst = site == kSiteX ? sm.x[b] : sm.x2[b];
+  float(*ss)[8] = site == kSiteX ? sm.ssx[b] : sm.ssx2[b];
+  int* okv = site == kSiteX ? sm.okx[b] : sm.okx2[b];
+  const unsigned long long* bar = &sm.sbar[site][b];
+  const int n = cx.n, np = n >> 1, nw = (np + 31) >> 5, t = (int)threadIdx.x;
   float q = 0.f;
   if (t < np) {
     const float v0 = sm.seg[2 * t], v1 = sm.seg[2 * t + 1];
-    for (unsigned k = 0; k < cs; ++k) dsmem_store2(dst + seg0 + 2 * t, k, v0, v1);
+    for (unsigned r = 0; r < cx.cs; ++r) st_async2(dst + cx.seg0 + 2 * t, bar, r, v0, v1);
     q = v0 * v0 + v1 * v1;
   }
-  if (t < ((np + 31) & ~31)) {
+  if (t < nw * 32) {
     q = warp_sum(q);
     if ((t & 31) == 0)
-      for (unsigned k = 0; k < cs; ++k) dsmem_store(&ss[rank][t >> 5], k, q);
+      for (unsigned r = 0; r < cx.cs; ++r) st_async1(&ss[cx.rank][t >> 5], bar, r, q);
   }
-  if (t < (int)cs) dsmem_store_u32(&sm.okv[site][rank], (unsigned)t, ok ? 1 : 0);
-  cluster_sync();
-  bool all = true;
-  for (unsigned k = 0; k < cs; ++k) all = all && (*reinterpret_cast<volatile int*>(&sm.okv[site][k]) != 0);
+  if (t < (int)cx.cs) st_async1i(&okv[cx.rank], bar, (unsigned)t, ok ? 1 : 0);
+  bool all = flow_receive(a, fr, sm, site, k, cx.cs * (unsigned)(4 * n + 4 * nw + 4));
+  for (unsigned r = 0; r < cx.cs; ++r) all = all && (*reinterpret_cast<volatile int*>(&okv[r]) != 0);
+  if (site == kSiteX) cx.bx = b;
+  else cx.bx2 = b;
   return all;
 }
 
@@ -585,29 +744,18 @@ __device__ __forceinline__ float flow_norm_scale(const float (*ss)[8], unsigned 
   return 1.0f / sqrtf(t / (float)d + eps);
 }
 
-// ---------------------------------------------------------------- step context
-struct FlowCtx {
-  unsigned rank, cs, id, nc;
-  int n, seg0;
-  bool heads_here, score_cluster;
-  unsigned long long epoch;  // tag base of this launch
-  unsigned long long steps;  // steps this launch has run
-};
-
 // ---------------------------------------------------------------- attention
 // One head h of layer l: q/k/v rows, attention over the retained slots and
 // the out-projection rows of this rank's segment, published as P[h].
-// Returns false when a ring wait failed (nothing to undo; the error word ends
-// the launch at the next exchange).
+// Returns false when a wait ran out (the error word is set; the next
+// exchange's verdict ends the launch).
 template <typename T, int D>
-__device__ __forceinline__ void flow_head(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSmem& sm,
-                                          const FlowCtx& cx, int l, int h, unsigned long long t, unsigned tag,
+__device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSmem& sm,
+                                          FlowCtx& cx, int l, int h, unsigned long long t, unsigned tag,
                                           bool first_head) {
   constexpr int hd = kFlowHd;
   const int W = a.window;
-  const int slot = (int)(t % (unsigned long long)W);
-  const int valid = t + 1 < (unsigned long long)W ? (int)(t + 1) : W;
-  const Where wh{(int)cx.rank, (int)cx.cs, (int)cx.id, (int)cx.nc};
+  const int slot = cx.slot, valid = cx.valid;
   const size_t head_base = (((size_t)l * a.heads + h) * (size_t)W) * hd;
   T* keys = (T*)a.keys + head_base;
   T* values = (T*)a.values + head_base;
@@ -630,19 +778,23 @@ __device__ __forceinline__ void flow_head(const StepArgs& a, FlowRing& fr, FlowC
     cp_async_commit();
   }
   if (first_head) {
-    const float scale = flow_norm_scale(sm.ssx, cx.cs, cx.n, D, a.epsilon);
+    const float scale = flow_norm_scale(sm.ssx[cx.bx], cx.cs, cx.n, D, a.epsilon);
+    const float* x = sm.x[cx.bx];
     flow_gain<T>(a, fr, cur, [&](const T* g) {
-      for (int i = threadIdx.x; i < D; i += kThreads) sm.z[i] = Storage<T>::round(sm.x[i] * scale * Storage<T>::load(g, i));
+      for (int i = threadIdx.x; i < D; i += kThreads) sm.z[i] = Storage<T>::round(x[i] * scale * Storage<T>::load(g, i));
     });
-    __syncthreads();
+    flow_bsync(fr);
+    fmark(a, fr, kFmNorm1);
   }
-  // q, k, v row pairs of this rank
+  // q, k, v row pairs of this rank, sent into every rank's q/k/v buffer
+  const unsigned kq = cx.k[kSiteQkv]++, bq = kq & 1u;
+  float* qkv = sm.qkv[bq];
   {
-    int lo, hi;
-    split(3 * hd / 2, (int)cx.rank, (int)cx.cs, lo, hi);
+    const unsigned long long* qbar = &sm.sbar[kSiteQkv][bq];
+    const int lo = sm.plan.qkv_lo;
     FlowX<T, D> xr;
     xr.load(sm.z);
-    flow_rows<T, D, 2>(a, fr, cur, span_of(a, wh, kSpanQkv, l, h, sizeof(T)), kSpanQkv, xr,
+    flow_rows<T, D, 2>(a, fr, cur, sm.plan.qkv, xr,
                        [&](int r, const float (&v)[2]) {
                          const int row = 2 * lo + r;
                          const int which = row / hd, dim = row - which * hd;
@@ -655,7 +807,7 @@ __device__ __forceinline__ void flow_head(const StepArgs& a, FlowRing& fr, FlowC
                            v0 = Storage<T>::round(r0v);
                            v1 = Storage<T>::round(r1v);
                          }
-                         for (unsigned k = 0; k < cx.cs; ++k) dsmem_store2(&sm.qkv[row], k, v0, v1);
+                         for (unsigned k = 0; k < cx.cs; ++k) st_async2(&qkv[row], qbar, k, v0, v1);
                          if (which > 0) {
                            T* ring = which == 1 ? keys : values;
                            const size_t at = (size_t)slot * hd + dim;
@@ -664,23 +816,27 @@ __device__ __forceinline__ void flow_head(const StepArgs& a, FlowRing& fr, FlowC
                          }
                        });
   }
+  fmark(a, fr, kFmQkv);
+  // this CTA's K/V copies, then every rank's q/k/v rows
   if (kv_smem) cp_async_wait_all();
-  cluster_sync();
+  flow_bar();
+  bool ok = flow_receive(a, fr, sm, kSiteQkv, kq, 3u * hd * 4u);
+  fmark(a, fr, kFmQkvSync);
   // attention over this CTA's slots: an online softmax per warp
   {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const T* Ks = reinterpret_cast<const T*>(sm.u.kv);
     const T* Vs = Ks + (size_t)nj * hd;
-    const float2 q = *reinterpret_cast<const float2*>(&sm.qkv[2 * lane]);
+    const float2 q = *reinterpret_cast<const float2*>(&qkv[2 * lane]);
     const float root = sqrtf((float)hd);
     float m = -INFINITY, lsum = 0.f, acc0 = 0.f, acc1 = 0.f;
     for (int j = j0 + warp; j < j1; j += kWarps) {
       float k0, k1, v0, v1;
       if (j == slot) {
-        k0 = sm.qkv[hd + 2 * lane];
-        k1 = sm.qkv[hd + 2 * lane + 1];
-        v0 = sm.qkv[2 * hd + 2 * lane];
-        v1 = sm.qkv[2 * hd + 2 * lane + 1];
+        k0 = qkv[hd + 2 * lane];
+        k1 = qkv[hd + 2 * lane + 1];
+        v0 = qkv[2 * hd + 2 * lane];
+        v1 = qkv[2 * hd + 2 * lane + 1];
       } else if (kv_smem) {
         k0 = Storage<T>::load(Ks + (size_t)(j - j0) * hd, 2 * lane);
         k1 = Storage<T>::load(Ks + (size_t)(j - j0) * hd, 2 * lane + 1);
@@ -708,7 +864,10 @@ __device__ __forceinline__ void flow_head(const StepArgs& a, FlowRing& fr, FlowC
       sm.wpart[warp][1] = lsum;
     }
   }
-  __syncthreads();
+  flow_bsync(fr);
+  fmark(a, fr, kFmAttn);
+  const unsigned ka = cx.k[kSiteAtt]++, ba = ka & 1u;
+  float(*apart)[kFlowHd + 2] = sm.apart[ba];
   if (threadIdx.x < 64) {
     // warps 0 and 1: this CTA's partial (M, L, A[dim]) from the 16 warp partials
     const int lane = threadIdx.x & 31, dim = threadIdx.x;
@@ -720,92 +879,103 @@ __device__ __forceinline__ void flow_head(const StepArgs& a, FlowRing& fr, FlowC
     float A = 0.f;
 #pragma unroll
     for (int k = 0; k < kWarps; ++k) A = fmaf(sm.wpart[k][2 + dim], __shfl_sync(0xffffffffu, sk, k), A);
-    for (unsigned r = 0; r < cx.cs; ++r) dsmem_store(&sm.apart[cx.rank][2 + dim], r, A);
-    if (threadIdx.x < cx.cs) dsmem_store2(&sm.apart[cx.rank][0], threadIdx.x, M, L);
+    const unsigned long long* abar = &sm.sbar[kSiteAtt][ba];
+    for (unsigned r = 0; r < cx.cs; ++r) st_async1(&apart[cx.rank][2 + dim], abar, r, A);
+    if (threadIdx.x < cx.cs) st_async2(&apart[cx.rank][0], abar, threadIdx.x, M, L);
   }
-  cluster_sync();
+  ok = flow_receive(a, fr, sm, kSiteAtt, ka, cx.cs * (unsigned)(4 * hd + 8)) && ok;
+  fmark(a, fr, kFmPartSync);
   if (threadIdx.x < 64) {
     // merge the cluster's partials in rank order -> o (cast)
     const int lane = threadIdx.x & 31, dim = threadIdx.x;
-    const float mr = lane < (int)cx.cs ? sm.apart[lane][0] : -INFINITY;
-    const float lr = lane < (int)cx.cs ? sm.apart[lane][1] : 0.f;
+    const float mr = lane < (int)cx.cs ? apart[lane][0] : -INFINITY;
+    const float lr = lane < (int)cx.cs ? apart[lane][1] : 0.f;
     const float M = warp_max(lr > 0.f ? mr : -INFINITY);
     const float sr = lr > 0.f ? expf(mr - M) : 0.f;
     const float L = warp_sum(lr * sr);
     float A = 0.f;
-    for (unsigned r = 0; r < cx.cs; ++r) A = fmaf(sm.apart[r][2 + dim], __shfl_sync(0xffffffffu, sr, r), A);
+    for (unsigned r = 0; r < cx.cs; ++r) A = fmaf(apart[r][2 + dim], __shfl_sync(0xffffffffu, sr, r), A);
     sm.o[dim] = Storage<T>::round(A / L);
   }
-  __syncthreads();
+  flow_bsync(fr);
+  fmark(a, fr, kFmMerge);
   // out-projection rows of this rank's segment, published as P[h]
   {
     FlowX<T, hd> xr;
     xr.load(sm.o);
     unsigned long long* P = a.ll_heads + ((size_t)(tag & 1u) * a.heads + h) * D + cx.seg0;
-    flow_rows<T, hd, 2>(a, fr, cur, span_of(a, wh, kSpanOut, l, h, sizeof(T)), kSpanOut, xr,
+    flow_rows<T, hd, 2>(a, fr, cur, sm.plan.out, xr,
                         [&](int r, const float (&v)[2]) { ll_store2(P + r, v[0], v[1], tag); });
   }
+  fmark(a, fr, kFmOut);
+  return ok;
 }
 
 // ---------------------------------------------------------------- one step
 // One event through every layer; the score CTA writes the score to score_dst
 // (and score_copy when given). Returns the cluster-uniform verdict.
 template <typename T, int D>
-__device__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSmem& sm, FlowCtx& cx,
+__device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSmem& sm, FlowCtx& cx,
                           const float* event, unsigned long long t, float* score_dst, float* score_copy) {
-  const Where wh{(int)cx.rank, (int)cx.cs, (int)cx.id, (int)cx.nc};
   const int n = cx.n, seg0 = cx.seg0;
-  // The score CTA may still read x for the previous step.
-  if (cx.score_cluster && cx.steps > 0) cluster_sync();
+  fmark(a, fr, kFmStep);
+  cx.slot = (int)(t % (unsigned long long)a.window);
+  cx.valid = t + 1 < (unsigned long long)a.window ? (int)(t + 1) : a.window;
   if (threadIdx.x < kFlowFeatures) sm.ev[threadIdx.x] = __ldcv(event + threadIdx.x);
   if (threadIdx.x < kFlowHd / 2) {
     const float angle = (float)t * sm.rope[threadIdx.x];
     sm.rope_cs[threadIdx.x] = make_float2(cosf(angle), sinf(angle));
   }
-  __syncthreads();
+  flow_bsync(fr);
   // x[seg] = cast(W_in[seg] e)
   {
     FlowX<T, kFlowFeatures> xr;
     xr.load(sm.ev);
-    flow_rows<T, kFlowFeatures, 1>(a, fr, cur, span_of(a, wh, kSpanIn, -1, 0, sizeof(T)), kSpanIn, xr,
+    flow_rows<T, kFlowFeatures, 1>(a, fr, cur, sm.plan.in, xr,
                                    [&](int r, const float (&v)[1]) { sm.seg[r] = Storage<T>::round(v[0]); });
-    __syncthreads();
-    if (!flow_publish(sm.x, sm.ssx, seg0, n, cx.rank, cx.cs, !fr.failed, kSiteIn, sm)) return false;
+    flow_bsync(fr);
+    if (!flow_publish(a, fr, sm, cx, kSiteX, !fr.failed)) return false;
+    fmark(a, fr, kFmIn);
   }
   for (int l = 0; l < a.layers; ++l) {
     const unsigned tag = (unsigned)(cx.epoch + cx.steps * (unsigned long long)a.layers + (unsigned long long)l + 1ull);
-    if (cx.heads_here) {
-      for (int h = (int)cx.id; h < a.heads; h += (int)cx.nc) {
-        if (h != (int)cx.id) cluster_sync();  // attention buffers are reused by the next head
-        flow_head<T, D>(a, fr, cur, sm, cx, l, h, t, tag, h == (int)cx.id);
-      }
-    }
+    bool hok = true;
+    if (cx.heads_here)
+      for (int h = (int)cx.id; h < a.heads; h += (int)cx.nc)
+        hok = flow_head<T, D>(a, fr, cur, sm, cx, l, h, t, tag, h == (int)cx.id) && hok;
     // exchange 1: x'[seg] = cast(x[seg] + cast(sum_h P[h][seg]))
     {
       const unsigned long long* P = a.ll_heads + (size_t)(tag & 1u) * a.heads * D;
-      bool ok = flow_gather<D>(a, fr, P, a.heads, seg0, n, tag, sm);
+      const bool ok = flow_gather<D>(a, fr, P, a.heads, seg0, n, tag, sm) && hok;
+      fmark(a, fr, kFmGather1);
+      const float* x = sm.x[cx.bx];
       if ((int)threadIdx.x < n)
-        sm.seg[threadIdx.x] = Storage<T>::round(sm.x[seg0 + threadIdx.x] + Storage<T>::round(sm.seg[threadIdx.x]));
-      __syncthreads();
-      if (!flow_publish(sm.x2, sm.ssx2, seg0, n, cx.rank, cx.cs, ok && !fr.failed, kSiteX2, sm)) return false;
+        sm.seg[threadIdx.x] = Storage<T>::round(x[seg0 + threadIdx.x] + Storage<T>::round(sm.seg[threadIdx.x]));
+      flow_bsync(fr);
+      if (!flow_publish(a, fr, sm, cx, kSiteX2, ok && !fr.failed)) return false;
+      fmark(a, fr, kFmPub2);
     }
     // FFN: norm2, gate/up -> SwiGLU, down partial
+    bool dok = true;
     {
-      const float scale = flow_norm_scale(sm.ssx2, cx.cs, n, D, a.epsilon);
+      const float scale = flow_norm_scale(sm.ssx2[cx.bx2], cx.cs, n, D, a.epsilon);
+      const float* x2 = sm.x2[cx.bx2];
       flow_gain<T>(a, fr, cur, [&](const T* g) {
         for (int i = threadIdx.x; i < D; i += kThreads)
-          sm.z[i] = Storage<T>::round(sm.x2[i] * scale * Storage<T>::load(g, i));
+          sm.z[i] = Storage<T>::round(x2[i] * scale * Storage<T>::load(g, i));
       });
-      __syncthreads();
+      flow_bsync(fr);
+      fmark(a, fr, kFmNorm2);
       FlowX<T, D> xr;
       xr.load(sm.z);
-      flow_rows<T, D, 2>(a, fr, cur, span_of(a, wh, kSpanGateUp, l, 0, sizeof(T)), kSpanGateUp, xr,
+      flow_rows<T, D, 2>(a, fr, cur, sm.plan.gateup, xr,
                          [&](int r, const float (&v)[2]) {
                            const float gt = Storage<T>::round(v[0]);
                            const float up = Storage<T>::round(v[1]);
                            sm.act[r >> 1] = Storage<T>::round((gt / (1.0f + expf(-gt))) * up);
                          });
-      __syncthreads();
+      flow_bsync(fr);
+      fmark(a, fr, kFmGateUp);
       // partial[col] = sum_f act[f] W_down^T[f][col]: thread t owns 16-byte
       // column vector t % NVd and rows f = g, g + G2, ... of the slice.
       using R = FlowRow<T, D>;
@@ -814,11 +984,10 @@ __device__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSme
       float acc[V];
 #pragma unroll
       for (int k = 0; k < V; ++k) acc[k] = 0.f;
-      const Span sd = span_of(a, wh, kSpanDown, l, 0, sizeof(T));
-      const FlowSplit sp = flow_split(sd, kSpanDown);
+      const FlowSpan sp = sm.plan.down;
       for (int c = 0; c < sp.chunks; ++c) {
-        const int r0 = c * sp.rows_per_chunk;
-        const int rows = min(sp.rows_per_chunk, sd.rows - r0);
+        const int r0 = c * sp.rpc;
+        const int rows = min(sp.rpc, sp.rows - r0);
         const T* base = (const T*)flow_acquire(a, fr, cur);
         int f = ((g - r0) % G2 + G2) % G2;
         for (; f < rows; f += G2) {
@@ -830,12 +999,16 @@ __device__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSme
         }
         flow_release(fr, cur);
       }
-      // sm.u.red was last read by exchange 1, before its cluster barrier.
+      fmark(a, fr, kFmDown);
+      // sm.u.red was last read by exchange 1, before its publish.
 #pragma unroll
       for (int k = 0; k < V; k += 4)
         *reinterpret_cast<float4*>(&sm.u.red[g * D + cv * V + k]) = make_float4(acc[k], acc[k + 1], acc[k + 2], acc[k + 3]);
-      __syncthreads();
+      flow_bsync(fr);
       // column sums in group order, sent in float4s to the rank owning them
+      const unsigned kd = cx.k[kSiteDred]++, bd = kd & 1u;
+      float* dred = sm.dred[bd];
+      const unsigned long long* dbar = &sm.sbar[kSiteDred][bd];
       for (int c4 = threadIdx.x; c4 < D / 4; c4 += kThreads) {
         float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int k = 0; k < G2; ++k) {
@@ -843,46 +1016,57 @@ __device__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSme
           s.x += q.x; s.y += q.y; s.z += q.z; s.w += q.w;
         }
         const int col = 4 * c4, owner = col / n;
-        dsmem_store4(&sm.dred[cx.rank * n + (col - owner * n)], (unsigned)owner, s);
+        st_async4(&dred[cx.rank * n + (col - owner * n)], dbar, (unsigned)owner, s);
       }
-      cluster_sync();
+      dok = flow_receive(a, fr, sm, kSiteDred, kd, cx.cs * (unsigned)n * 4u);
+      fmark(a, fr, kFmDredSync);
       // this rank's segment of the cluster partial, ranks added in order
       unsigned long long* Dp = a.ll_clusters + ((size_t)(tag & 1u) * cx.nc + cx.id) * D + seg0;
       if ((int)threadIdx.x < (n >> 1)) {
         const int i = 2 * threadIdx.x;
         float s0 = 0.f, s1 = 0.f;
         for (unsigned r = 0; r < cx.cs; ++r) {
-          s0 += sm.dred[r * n + i];
-          s1 += sm.dred[r * n + i + 1];
+          s0 += dred[r * n + i];
+          s1 += dred[r * n + i + 1];
         }
         ll_store2(Dp + i, s0, s1, tag);
       }
+      fmark(a, fr, kFmDpub);
     }
     // exchange 2: x[seg] = cast(x'[seg] + cast(sum_c D[c][seg]))
     {
       const unsigned long long* Dq = a.ll_clusters + (size_t)(tag & 1u) * cx.nc * D;
-      bool ok = flow_gather<D>(a, fr, Dq, (int)cx.nc, seg0, n, tag, sm);
+      const bool ok = flow_gather<D>(a, fr, Dq, (int)cx.nc, seg0, n, tag, sm) && dok;
+      fmark(a, fr, kFmGather2);
+      const float* x2 = sm.x2[cx.bx2];
       if ((int)threadIdx.x < n) {
-        const float v = Storage<T>::round(sm.x2[seg0 + threadIdx.x] + Storage<T>::round(sm.seg[threadIdx.x]));
+        const float v = Storage<T>::round(x2[seg0 + threadIdx.x] + Storage<T>::round(sm.seg[threadIdx.x]));
         sm.seg[threadIdx.x] = v;
         if (cx.score_cluster) a.hidden[(size_t)l * D + seg0 + threadIdx.x] = v;
       }
-      __syncthreads();
-      if (!flow_publish(sm.x, sm.ssx, seg0, n, cx.rank, cx.cs, ok && !fr.failed, kSiteX, sm)) return false;
+      flow_bsync(fr);
+      if (!flow_publish(a, fr, sm, cx, kSiteX, ok && !fr.failed)) return false;
+      fmark(a, fr, kFmPub1);
     }
   }
   // final RMSNorm and score head (no cast), by the score CTA
   if (cx.score_cluster && cx.rank == 0) {
-    const float scale = flow_norm_scale(sm.ssx, cx.cs, n, D, a.epsilon);
+    const float scale = flow_norm_scale(sm.ssx[cx.bx], cx.cs, n, D, a.epsilon);
+    const float* x = sm.x[cx.bx];
     float acc = 0.f;
     for (int i = threadIdx.x; i < D; i += kThreads)
-      acc = fmaf(sm.fscore[i], Storage<T>::round(sm.x[i] * scale * sm.fnorm[i]), acc);
-    const float total = block_reduce_sum(acc, sm.warp_scratch);
+      acc = fmaf(sm.fscore[i], Storage<T>::round(x[i] * scale * sm.fnorm[i]), acc);
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) sm.warp_scratch[threadIdx.x >> 5] = acc;
+    flow_bar();
+    float total = 0.f;
+    for (int w = 0; w < kWarps; ++w) total += sm.warp_scratch[w];
     if (threadIdx.x == 0) {
       *score_dst = total;
       if (score_copy) *score_copy = total;
     }
   }
+  fmark(a, fr, kFmScore);
   cx.steps += 1;
   return true;
 }
@@ -895,7 +1079,7 @@ __device__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSme
 // on a tagged control word every CTA polls; the score CTA publishes RUN
 // completions; RESET ends with a count of CTAs on the barrier counter.
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 1) k4_flow(StepArgs a, FlowLaunch f) {
+__global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunch f) {
   extern __shared__ __align__(128) unsigned char flow_raw[];
   FlowSmem& sm = *reinterpret_cast<FlowSmem*>(flow_raw);
   FlowRing& fr = *reinterpret_cast<FlowRing*>(flow_raw + sizeof(FlowSmem));
@@ -914,6 +1098,9 @@ __global__ void __launch_bounds__(kThreads, 1) k4_flow(StepArgs a, FlowLaunch f)
   cx.score_cluster = cx.id == cx.nc - 1;
   cx.epoch = ld_cg_u64(a.flow_epoch);
   cx.steps = 0;
+  for (int i = 0; i < kSites; ++i) cx.k[i] = 0;
+  cx.bx = cx.bx2 = 0;
+  fr.tl_n = 0;
   const unsigned long long t0 = ld_cg_u64(a.position);
   for (int i = threadIdx.x; i < kFlowHd / 2; i += kThreads) sm.rope[i] = a.rope_freq[i];
   if (cx.score_cluster && cx.rank == 0)
@@ -923,98 +1110,127 @@ __global__ void __launch_bounds__(kThreads, 1) k4_flow(StepArgs a, FlowLaunch f)
     }
   FlowCur cur{0};
   const Where wh{(int)cx.rank, (int)cx.cs, (int)cx.id, (int)cx.nc};
+  if (threadIdx.x == 0) {
+    FlowPlan pl;
+    pl.in = flow_span(a, wh, kSpanIn, sizeof(T));
+    pl.qkv = flow_span(a, wh, kSpanQkv, sizeof(T));
+    pl.out = flow_span(a, wh, kSpanOut, sizeof(T));
+    pl.gateup = flow_span(a, wh, kSpanGateUp, sizeof(T));
+    pl.down = flow_span(a, wh, kSpanDown, sizeof(T));
+    int lo, hi;
+    split_range(3 * kFlowHd / 2, wh.rank, wh.size, lo, hi);
+    pl.qkv_lo = lo;
+    sm.plan = pl;
+    // one arrival (the receiver's expect_tx) per phase; the peers' st.async
+    // stores complete the transaction bytes
+    for (int i = 0; i < kSites; ++i) {
+      mbar_init(&sm.sbar[i][0], 1);
+      mbar_init(&sm.sbar[i][1], 1);
+    }
+    fence_mbar_init();
+  }
   const bool ring_ok = flow_ring_begin(a, fr, flow_raw + kFlowRingOffset, wh, sizeof(T),
                                        f.mode == kFlowTrace ? f.count : 0ull);
   if (!ring_ok && threadIdx.x == 0) set_error(a, kRingTable);
   // every CTA of the cluster learns every rank's setup verdict
-  if (threadIdx.x < cx.cs) dsmem_store_u32(&sm.okv[kSiteSetup][cx.rank], threadIdx.x, ring_ok ? 1 : 0);
+  // (the barrier also orders the mbarrier initialisation before any peer's st.async)
+  if (threadIdx.x < cx.cs) dsmem_store_u32(&sm.oksetup[cx.rank], threadIdx.x, ring_ok ? 1 : 0);
   cluster_sync();
   bool ok = true;
-  for (unsigned k = 0; k < cx.cs; ++k) ok = ok && (*reinterpret_cast<volatile int*>(&sm.okv[kSiteSetup][k]) != 0);
-  if (!ok) {
-    flow_drain(a, fr, cur);
-    if (f.mode == kFlowPersistent && blockIdx.x == 0) persistent_exit<T>(a, f.p);
+  for (unsigned k = 0; k < cx.cs; ++k) ok = ok && (*reinterpret_cast<volatile int*>(&sm.oksetup[k]) != 0);
+  if (!ok) {  // nothing issued or sent yet
+    if (f.mode == kFlowPersistent && blockIdx.x == 0 && threadIdx.x < kThreads) persistent_exit<T>(a, f.p);
     return;
   }
 
-  if (f.mode == kFlowTrace) {
-    for (unsigned long long e = 0; e < f.count && ok; ++e)
-      ok = flow_step<T, D>(a, fr, cur, sm, cx, f.inputs + e * kFlowFeatures, t0 + e, a.score,
-                           f.scores ? f.scores + e : nullptr);
-    if (ok && cx.score_cluster && cx.rank == 0 && threadIdx.x == 0) {
-      a.position[0] = t0 + f.count;
-      *a.flow_epoch = cx.epoch + f.count * (unsigned long long)a.layers;
-    }
-    flow_drain(a, fr, cur);
-    return;
-  }
-
-  // ---- persistent worker
+  // One command loop for both modes, so the step is inlined at a single call
+  // site (a call that takes the kernel parameters by reference would copy them
+  // to local memory). Trace mode: RUN for each of f.count events. Persistent
+  // mode: CTA 0 polls the mailbox and publishes each command on the tagged
+  // control word.
+  const bool trace = f.mode == kFlowTrace;
   const PersistArgs& p = f.p;
   unsigned long long previous = p.initial_sequence, dispatched = 0, processed = 0, counts = 0;
-  bool exit_loop = false;
+  if (threadIdx.x >= kThreads) {
+    // the producer warp: lane 0 streams the weights until the compute warps leave
+    if (threadIdx.x == kFlowProducer)
+      flow_produce(a, fr, trace ? a.bar_timeout_ns : p.idle_ns + p.dispatch_timeout_ns + a.bar_timeout_ns);
+    __syncwarp();
+  }
+  bool exit_loop = threadIdx.x >= kThreads;
   while (!exit_loop) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-      const unsigned long long start = globaltimer();
-      unsigned long long seq;
-      int command = 0, arg = 0;
-      while ((seq = ld_acquire_sys(&p.mailbox->request)) == previous) {
-        if (globaltimer() - start >= p.idle_ns) { command = kFlowExit; break; }
-        if (p.backoff) __nanosleep(128);
+    int command, arg = -1;
+    if (trace) {
+      command = processed < f.count ? kRun : kFlowExit;
+    } else {
+      if (blockIdx.x == 0 && threadIdx.x == 0) {
+        const unsigned long long start = globaltimer();
+        unsigned long long seq;
+        int cmd = 0, carg = 0;
+        while ((seq = ld_acquire_sys(&p.mailbox->request)) == previous) {
+          if (globaltimer() - start >= p.idle_ns) { cmd = kFlowExit; break; }
+          if (p.backoff) __nanosleep(128);
+        }
+        if (cmd == 0) {
+          cmd = *reinterpret_cast<volatile int*>(&p.mailbox->command);
+          carg = *reinterpret_cast<volatile int*>(&p.mailbox->arg);
+          if (cmd == kRun)
+            for (int i = 0; i < kFlowFeatures; ++i) const_cast<float*>(a.input)[i] = __ldcv(f.mapped_input + i);
+          *a.flow_seq = seq;
+          previous = seq;
+        }
+        const unsigned long long word = ((dispatched + 1ull) << 32) |
+                                        ((unsigned long long)(unsigned)(carg + 1) << 8) | (unsigned long long)cmd;
+        __threadfence();
+        asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(a.flow_ctl), "l"(word) : "memory");
       }
-      if (command == 0) {
-        command = *reinterpret_cast<volatile int*>(&p.mailbox->command);
-        arg = *reinterpret_cast<volatile int*>(&p.mailbox->arg);
-        if (command == kRun)
-          for (int i = 0; i < kFlowFeatures; ++i) const_cast<float*>(a.input)[i] = __ldcv(f.mapped_input + i);
-        *a.flow_seq = seq;
-        previous = seq;
-      }
-      const unsigned long long word = ((dispatched + 1ull) << 32) | ((unsigned long long)(unsigned)(arg + 1) << 8) |
-                                      (unsigned long long)command;
-      __threadfence();
-      asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(a.flow_ctl), "l"(word) : "memory");
-    }
-    if (threadIdx.x == 0) {
-      const unsigned long long want = dispatched + 1ull;
-      const unsigned long long start = globaltimer();
-      unsigned long long w;
-      unsigned polls = 0;
-      while (((w = ld_acquire_gpu(a.flow_ctl)) >> 32) != (want & 0xffffffffull)) {
-        if ((++polls & 63u) == 0) {
-          if (ld_volatile_int(a.error) != 0) { w = kFlowExit; break; }
-          if (globaltimer() - start > p.dispatch_timeout_ns) {
-            set_error(a, kBarrierTimeout);
-            w = kFlowExit;
-            break;
+      if (threadIdx.x == 0) {
+        const unsigned long long want = dispatched + 1ull;
+        const unsigned long long start = globaltimer();
+        unsigned long long w;
+        unsigned polls = 0;
+        while (((w = ld_acquire_gpu(a.flow_ctl)) >> 32) != (want & 0xffffffffull)) {
+          if ((++polls & 63u) == 0) {
+            if (ld_volatile_int(a.error) != 0) { w = kFlowExit; break; }
+            if (globaltimer() - start > p.dispatch_timeout_ns) {
+              set_error(a, kBarrierTimeout);
+              w = kFlowExit;
+              break;
+            }
           }
         }
-        flow_fill(fr);
+        sm.cmd = w;
       }
-      sm.cmd = w;
+      flow_bar();
+      const unsigned long long word = *reinterpret_cast<volatile unsigned long long*>(&sm.cmd);
+      command = (int)(word & 0xffull);
+      arg = (int)((word >> 8) & 0xffffffull) - 1;
+      dispatched += 1;
     }
-    __syncthreads();
-    const unsigned long long word = *reinterpret_cast<volatile unsigned long long*>(&sm.cmd);
-    const int command = (int)(word & 0xffull);
-    const int arg = (int)((word >> 8) & 0xffffffull) - 1;
-    dispatched += 1;
     if (command == kRun) {
-      const unsigned long long t = ld_cg_u64(a.position);
-      if (!flow_step<T, D>(a, fr, cur, sm, cx, a.input, t, a.score, nullptr)) break;
-      if (cx.score_cluster && cx.rank == 0 && threadIdx.x == 0) {
-        a.position[0] = t + 1;
-        const unsigned long long seq = ld_cg_u64(a.flow_seq);
-        __threadfence_system();
-        st_release_sys(&p.mailbox->completion, seq);
+      const unsigned long long t = trace ? t0 + processed : ld_cg_u64(a.position);
+      const float* event = trace ? f.inputs + processed * kFlowFeatures : a.input;
+      float* copy = trace && f.scores ? f.scores + processed : nullptr;
+      if (!flow_step<T, D>(a, fr, cur, sm, cx, event, t, a.score, copy)) {
+        ok = false;
+        break;
       }
       processed += 1;
-      if (p.max_events && processed >= p.max_events) exit_loop = true;
+      if (!trace) {
+        if (cx.score_cluster && cx.rank == 0 && threadIdx.x == 0) {
+          a.position[0] = t + 1;
+          const unsigned long long seq = ld_cg_u64(a.flow_seq);
+          __threadfence_system();
+          st_release_sys(&p.mailbox->completion, seq);
+        }
+        if (p.max_events && processed >= p.max_events) exit_loop = true;
+      }
     } else if (command == kReset || command == kPing) {
       // Every CTA takes the command before CTA 0 completes it, so the control
       // word is not rewritten while a CTA has yet to read it.
       if (command == kReset) reset_streams<T>(a, 0, 1);  // one stream: arg -1 and 0 both reset it
       (void)arg;
-      __syncthreads();
+      flow_bar();
       counts += 1;
       if (threadIdx.x == 0) {
         __threadfence();
@@ -1045,13 +1261,23 @@ __global__ void __launch_bounds__(kThreads, 1) k4_flow(StepArgs a, FlowLaunch f)
       }
       exit_loop = true;
     } else {
-      exit_loop = true;  // idle budget, error or an unknown command
+      exit_loop = true;  // end of the trace, idle budget, error or an unknown command
     }
   }
-  // Leave together: every CTA counts itself out; CTA 0 then stores the tag
-  // base for the next launch and tells the host.
+  if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(&fr.stop) = 1;
+  // No CTA leaves while a peer may still store into its shared memory, or
+  // before its producer has seen its copies land.
   cluster_sync();
-  flow_drain(a, fr, cur);
+  if (threadIdx.x >= kThreads) return;
+  if (trace) {
+    if (ok && cx.score_cluster && cx.rank == 0 && threadIdx.x == 0) {
+      a.position[0] = t0 + f.count;
+      *a.flow_epoch = cx.epoch + f.count * (unsigned long long)a.layers;
+    }
+    return;
+  }
+  // Persistent: every CTA counts itself out; CTA 0 then stores the tag base
+  // for the next launch and tells the host.
   if (threadIdx.x == 0) {
     __threadfence();
     red_release_gpu_add(a.bar_counter, 1ull);

@@ -12,8 +12,9 @@ struct FlowLaunch;
 
 // k4_flow<T, width> for mode 0 fp32, 1 fp16, 2 bf16; null for other widths.
 const void* flow_kernel(int mode, int width);
-// Dynamic shared memory of k4_flow.
+// Dynamic shared memory and threads per CTA of k4_flow.
 size_t flow_smem_bytes();
+int flow_threads();
 // True when the flow kernel serves this model on a grid of `clusters`
 // clusters of `cluster` CTAs (shapes, ffn slice, chunk tables).
 bool flow_shape_ok(const StepArgs& a, size_t elem, int cluster, int clusters);

@@ -370,7 +370,7 @@ int launch_fused(st_runtime* rt, const StepArgs& a0) {
 
 int launch_trace(st_runtime* rt, const StepArgs& a0, const float* inputs, unsigned long long count, float* scores,
                  bool timeline = false) {
-  if (rt->flow && !timeline) return launch_flow_trace(rt, a0, inputs, count, scores);
+  if (rt->flow) return launch_flow_trace(rt, a0, inputs, count, scores);
   StepArgs a = a0;
   unsigned long long base = rt->bar_base;
   void* params[] = {&a, &inputs, &count, &scores, &base};
@@ -881,7 +881,7 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
       for (int cs : {8, 4}) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(cs);
-        cfg.blockDim = dim3(kThreads);
+        cfg.blockDim = dim3(flow_threads());
         cfg.dynamicSmemBytes = flow_smem_bytes();
         cudaLaunchAttribute attr;
         attr.id = cudaLaunchAttributeClusterDimension;
@@ -1361,8 +1361,9 @@ int st_device_timeline(st_runtime* rt, const float* inputs, size_t count, long l
 int st_device_timeline_cta(st_runtime* rt, const float* inputs, size_t count, int cta, long long* marks,
                            size_t capacity, size_t* used) {
   if (!rt || !inputs || !marks || count == 0 || capacity == 0) return ST_ERR_INVALID;
-  const int grid = rt->batched ? rt->bgrid : rt->grid;
-  if (cta < 0 || cta >= grid) return rt->fail(ST_ERR_INVALID, "timeline CTA %d outside the grid of %d", cta, grid);
+  const int grid = rt->batched ? rt->bgrid : rt->flow ? rt->fgrid : rt->grid;
+  // cta -1: every CTA of the flow kernel records {tag, globaltimer} pairs
+  if (cta < (rt->flow ? -1 : 0) || cta >= grid) return rt->fail(ST_ERR_INVALID, "timeline CTA %d outside the grid of %d", cta, grid);
   if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
   if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
   if (rt->opt.backend == ST_BACKEND_PERSISTENT) ST_TRY(st_stop(rt));
@@ -1434,7 +1435,7 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
   std::ostringstream o;
   o << "{\"environment\":" << probe_json(rt->device, &pst) << ",\"backend\":\"" << backends[rt->opt.backend]
     << "\",\"blocks\":" << rt->grid << ",\"legal_cooperative_blocks\":" << rt->legal_blocks
-    << ",\"threads\":" << kThreads << ",\"resource_kernel\":\"" << name << "\""
+    << ",\"threads\":" << (flow_loop ? flow_threads() : kThreads) << ",\"resource_kernel\":\"" << name << "\""
     << ",\"registers_per_thread\":" << fa.numRegs << ",\"local_bytes\":" << fa.localSizeBytes
     << ",\"shared_bytes\":" << fa.sharedSizeBytes << ",\"dynamic_shared_bytes\":" << (flow_loop ? flow_smem_bytes() : kSmem2)
     << ",\"cluster\":" << (flow_loop ? rt->fcluster : rt->cluster) << ",\"clusters\":" << (flow_loop ? rt->fnclusters : rt->nclusters)
