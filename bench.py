@@ -103,10 +103,31 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "profiling-recipe fallback 6.65 TB/s (of fallback)"
 
 
-def measured_traffic(name):
+def kernel_name(info):
+    """The device-loop kernel the runtime runs for the timed trace."""
+    if info.get("batched"):
+        return "k3_rounds"
+    return "k4_flow" if info.get("flow") else "k2_trace"
+
+
+def kernel_label(info, mode, streams):
+    name = kernel_name(info)
+    if name == "k3_rounds":
+        return f"k3_rounds ({mode}, batched round of {streams} streams)"
+    if name == "k4_flow":
+        return (f"k4_flow ({mode}, {info.get('clusters')} clusters of {info.get('cluster')} CTAs, "
+                "tagged-record exchanges, producer-warp weight ring)")
+    return f"k2_trace ({mode}, {'weight ring' if info.get('weight_ring') else 'direct loads'})"
+
+
+def measured_traffic(config_name, kernel):
+    """DRAM bytes per step of `kernel` on `config_name` from a committed ncu
+    capture (profiles/traffic.json), or None when none was taken for it."""
     path = ROOT / "profiles" / "traffic.json"
     try:
-        entry = json.loads(path.read_text())[name]
+        entry = json.loads(path.read_text())[config_name]
+        if entry.get("kernel", "k2_trace") != kernel:
+            return None, None
         return float(entry["dram_bytes_per_step"]), entry.get("source", "")
     except (OSError, ValueError, KeyError):
         return None, None
@@ -296,7 +317,7 @@ def run_b200(args):
     peak, peak_src = measured_peak()
     alg = metrics.trace_bytes(config, mode, K, streams=S)
     achieved = alg / K / (us * 1e-6) / 1e9
-    traffic, traffic_src = measured_traffic(args.config) if not info.get("batched") else (None, None)
+    traffic, traffic_src = measured_traffic(args.config, kernel_name(info))
     ws = metrics.weight_bytes(config, mode) + S * 2 * config.layers * config.width * config.window * metrics.ELEM_BYTES[mode]
     line = {
         "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -312,9 +333,7 @@ def run_b200(args):
                          "pinned copies of the S inputs and scores, host clock")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic,
-                     "kernel": (f"k3_rounds ({mode}, batched round of {S} streams)" if info.get("batched")
-                                else f"k2_trace ({mode}, weight ring)" if info.get("weight_ring")
-                                else f"k2_trace ({mode}, direct loads)"),
+                     "kernel": kernel_label(info, mode, S),
                      "algorithmic_bytes_per_step": alg / K, "peak_source": peak_src,
                      "traffic_source": traffic_src},
         "gpu_launches": launches,

@@ -232,24 +232,38 @@ enum FlowMark : int {
   kFmPub2, kFmNorm2, kFmGateUp, kFmDown, kFmDredSync, kFmDpub, kFmGather2, kFmPub1, kFmScore, kFmAcqStart,
   kFmAcqEnd, kFmBarIn, kFmBarOut
 };
-__device__ __forceinline__ void fmark(const StepArgs& a, FlowRing& fr, int tag) {
-  if (a.timeline != nullptr && threadIdx.x == 0) {
-    if ((int)blockIdx.x == a.timeline_cta) {
-      const int i = fr.tl_n;
-      if (i < a.timeline_capacity / kWarps) {
-        a.timeline[i] = (long long)((clock64() << 8) | (long long)tag);
-        fr.tl_n = i + 1;
-      }
-    } else if (a.timeline_cta < 0) {
-      const int per = a.timeline_capacity / (int)gridDim.x;
-      const int i = fr.tl_n;
-      if (2 * i + 1 < per) {
-        long long* r = a.timeline + (size_t)blockIdx.x * per;
-        r[2 * i] = tag;
-        r[2 * i + 1] = (long long)globaltimer();
-        fr.tl_n = i + 1;
-      }
+// The step's code is long and runs once per layer, so everything that is off
+// the hot path (diagnostics, error reporting, slow waits) lives in functions
+// of its own, called with scalars (a call that took the kernel parameters by
+// reference would copy them to local memory); the hot path stays small enough
+// to keep its instructions cached.
+static __device__ __noinline__ void fmark_slow(long long* tl, int capacity, int cta, int* n, int tag) {
+  if ((int)blockIdx.x == cta) {
+    const int i = *n;
+    if (i < capacity / kWarps) {
+      tl[i] = (long long)((clock64() << 8) | (long long)tag);
+      *n = i + 1;
     }
+  } else if (cta < 0) {
+    const int per = capacity / (int)gridDim.x;
+    const int i = *n;
+    if (2 * i + 1 < per) {
+      long long* r = tl + (size_t)blockIdx.x * per;
+      r[2 * i] = tag;
+      r[2 * i + 1] = (long long)globaltimer();
+      *n = i + 1;
+    }
+  }
+}
+__device__ __forceinline__ void fmark(const StepArgs& a, FlowRing& fr, int tag) {
+  if (a.timeline != nullptr && threadIdx.x == 0) fmark_slow(a.timeline, a.timeline_capacity, a.timeline_cta, &fr.tl_n, tag);
+}
+
+// First error wins; mirrored to the host (set_error with scalars).
+static __device__ __noinline__ void flow_error(int* error, int* host_error, int code) {
+  if (atomicCAS(error, 0, code) == 0 && host_error) {
+    *reinterpret_cast<volatile int*>(host_error) = code;
+    __threadfence_system();
   }
 }
 
@@ -324,14 +338,17 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(unsigned long long* bar, u
 
 // ---------------------------------------------------------------- ring
 // Compute threads (warps 0-15) meet at named barrier 1; the producer warp
-// (warp 16) never joins it, so issuing never holds up a compute phase.
-__device__ __forceinline__ void flow_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
+// (warp 16) never joins it, so issuing never holds up a compute phase. The
+// non-aligned barrier forms: a warp may reach them diverged (one lane still
+// polling while the others wait), which the .aligned forms (bar.sync,
+// bar.red) do not allow.
+__device__ __forceinline__ void flow_bar() { asm volatile("barrier.sync 1, %0;" ::"n"(kThreads) : "memory"); }
 __device__ __forceinline__ bool flow_bar_and(bool p) {
   int r;
   asm volatile(
       "{\n\t.reg .pred a, r;\n\t"
       "setp.ne.u32 a, %1, 0;\n\t"
-      "bar.red.and.pred r, 1, %2, a;\n\t"
+      "barrier.red.and.pred r, 1, %2, a;\n\t"
       "selp.u32 %0, 1, 0, r;\n\t}"
       : "=r"(r) : "r"((unsigned)p), "n"(kThreads) : "memory");
   return r != 0;
@@ -383,7 +400,7 @@ __device__ inline void flow_produce(const StepArgs& a, FlowRing& fr, unsigned lo
     // sleep until the oldest outstanding chunk is released
     mbar_try_wait_for(&fr.empty[fr.released % kFlowSlots], (unsigned)((fr.released / kFlowSlots) & 1ull), 2000u);
     if (globaltimer() - since > wait_ns) {
-      set_error(a, kBarrierTimeout);
+      flow_error(a.error, a.host_error, kBarrierTimeout);
       break;
     }
   }
@@ -421,7 +438,7 @@ __device__ __forceinline__ const unsigned char* flow_acquire(const StepArgs& a, 
   if (!mbar_try_wait(&fr.full[slot], parity) && !*reinterpret_cast<volatile int*>(&fr.failed) &&
       !flow_wait_slow(fr, slot, parity, a.bar_timeout_ns)) {
     fr.failed = 1;
-    set_error(a, kBarrierTimeout);
+    flow_error(a.error, a.host_error, kBarrierTimeout);
   }
   fmark(a, fr, kFmAcqEnd);
   return fr.buf + (*reinterpret_cast<volatile int*>(&fr.failed) ? 0u : fr.off[slot]);
@@ -615,9 +632,12 @@ __device__ __forceinline__ void flow_gain(const StepArgs& a, FlowRing& fr, FlowC
 // index order. Thread t polls element pair t % (n/2) for sources congruent to
 // t / (n/2) modulo G = 1024 / n, eight sources per round trip. Returns false
 // (error word set) when a wait ran out or another CTA failed.
-template <int D>
-__device__ __forceinline__ bool flow_gather(const StepArgs& a, FlowRing& fr, const unsigned long long* rec, int nsrc,
-                                            int seg0, int n, unsigned tag, FlowSmem& sm) {
+// Inlined at its two call sites: an out-of-line copy (divergent polling, then
+// the named-barrier reductions inside the call) gave nondeterministic results
+// on B200, while the inlined form is bit-stable run to run.
+__device__ __forceinline__ bool flow_gather_impl(const unsigned long long* rec, int stride, int nsrc, int seg0,
+                                                     int n, unsigned tag, float* red, float* seg, int* error,
+                                                     int* host_error, unsigned long long timeout_ns) {
   // n is a power of two (D / CS), so the thread split is by shifts.
   const int np = n >> 1, lg = 31 - __clz(np), G = kThreads >> lg;
   const int e = (int)threadIdx.x & (np - 1), g = (int)threadIdx.x >> lg;
@@ -633,7 +653,7 @@ __device__ __forceinline__ bool flow_gather(const StepArgs& a, FlowRing& fr, con
       for (int k = 0; k < 8; ++k) {
         const int src = src0 + k * G;
         if (src < nsrc) {
-          ll_load2(rec + (size_t)src * D + seg0 + 2 * e, r[k][0], r[k][1]);
+          ll_load2(rec + (size_t)src * stride + seg0 + 2 * e, r[k][0], r[k][1]);
         } else {
           r[k][0] = r[k][1] = ll_pack(0.f, tag);
         }
@@ -642,10 +662,10 @@ __device__ __forceinline__ bool flow_gather(const StepArgs& a, FlowRing& fr, con
       for (int k = 0; k < 8; ++k) ready = ready && ll_tag(r[k][0]) == tag && ll_tag(r[k][1]) == tag;
       if (ready) break;
       if ((++polls & 31u) == 0) {
-        if (ld_volatile_int(a.error) != 0) { ok = false; break; }
+        if (ld_volatile_int(error) != 0) { ok = false; break; }
         const unsigned long long now = globaltimer();
         if (start == 0) start = now;
-        else if (now - start > a.bar_timeout_ns) { set_error(a, kBarrierTimeout); ok = false; break; }
+        else if (now - start > timeout_ns) { flow_error(error, host_error, kBarrierTimeout); ok = false; break; }
       }
     }
 #pragma unroll
@@ -654,16 +674,21 @@ __device__ __forceinline__ bool flow_gather(const StepArgs& a, FlowRing& fr, con
       s1 += ll_value(r[k][1]);
     }
   }
-  sm.u.red[g * n + 2 * e] = s0;
-  sm.u.red[g * n + 2 * e + 1] = s1;
+  red[g * n + 2 * e] = s0;
+  red[g * n + 2 * e + 1] = s1;
   ok = flow_bar_and(ok);
   if ((int)threadIdx.x < n) {
     float t = 0.f;
-    for (int k = 0; k < G; ++k) t += sm.u.red[k * n + threadIdx.x];
-    sm.seg[threadIdx.x] = t;
+    for (int k = 0; k < G; ++k) t += red[k * n + threadIdx.x];
+    seg[threadIdx.x] = t;
   }
-  flow_bsync(fr);
+  flow_bar();
   return ok;
+}
+template <int D>
+__device__ __forceinline__ bool flow_gather(const StepArgs& a, FlowRing&, const unsigned long long* rec, int nsrc,
+                                            int seg0, int n, unsigned tag, FlowSmem& sm) {
+  return flow_gather_impl(rec, D, nsrc, seg0, n, tag, sm.u.red, sm.seg, a.error, a.host_error, a.bar_timeout_ns);
 }
 
 // ---------------------------------------------------------------- step context
@@ -678,58 +703,76 @@ struct FlowCtx {
   unsigned bx, bx2;          // buffers holding the current x and x'
 };
 
-// Receive exchange k of a site: thread 0 arms the site's mbarrier with the
-// bytes every rank sends (one arrival), every thread waits for the phase to
-// complete (bounded; the issuer keeps issuing). False when the wait ran out.
-__device__ __forceinline__ bool flow_receive(const StepArgs& a, FlowRing& fr, FlowSmem& sm, int site, unsigned k,
-                                             unsigned bytes) {
-  unsigned long long* bar = &sm.sbar[site][k & 1u];
-  const unsigned parity = (k >> 1) & 1u;
-  if (threadIdx.x == 0) mbar_expect_tx(bar, bytes);
-  fmark(a, fr, kFmBarIn);
-  bool ok = true;
-  if (!mbar_try_wait_cluster(bar, parity)) {
-    const unsigned long long start = globaltimer();
-    unsigned polls = 0;
-    while (!mbar_try_wait_cluster(bar, parity)) {
-      if ((++polls & 63u) == 0 && globaltimer() - start > a.bar_timeout_ns) {
-        set_error(a, kBarrierTimeout);
-        ok = false;
-        break;
-      }
+// Bounded wait for an exchange phase that had not completed at the first try.
+static __device__ __noinline__ bool flow_receive_slow(unsigned long long* bar, unsigned parity, int* error,
+                                                      int* host_error, unsigned long long timeout_ns) {
+  const unsigned long long start = globaltimer();
+  unsigned polls = 0;
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if ((++polls & 63u) == 0 && globaltimer() - start > timeout_ns) {
+      flow_error(error, host_error, kBarrierTimeout);
+      return false;
     }
   }
+  return true;
+}
+
+// Receive exchange k of a site: thread 0 arms the site's mbarrier with the
+// bytes every rank sends (one arrival), every thread waits for the phase to
+// complete (bounded). False when the wait ran out.
+__device__ __forceinline__ bool flow_receive_at(unsigned long long* bar, unsigned k, unsigned bytes, int* error,
+                                                int* host_error, unsigned long long timeout_ns) {
+  const unsigned parity = (k >> 1) & 1u;
+  if (threadIdx.x == 0) mbar_expect_tx(bar, bytes);
+  return mbar_try_wait_cluster(bar, parity) || flow_receive_slow(bar, parity, error, host_error, timeout_ns);
+}
+__device__ __forceinline__ bool flow_receive(const StepArgs& a, FlowRing& fr, FlowSmem& sm, int site, unsigned k,
+                                             unsigned bytes) {
+  fmark(a, fr, kFmBarIn);
+  const bool ok = flow_receive_at(&sm.sbar[site][k & 1u], k, bytes, a.error, a.host_error, a.bar_timeout_ns);
   fmark(a, fr, kFmBarOut);
   return ok;
 }
 
-// Publish this rank's segment (sm.seg[i], i < n) as x (site X) or x' (site
-// X2) of every rank, with the segment's per-warp sums of squares and this
-// CTA's verdict, then receive every rank's. Returns the cluster's verdict
+// Publish this rank's segment (seg[i], i < n) into dst of every rank, with the
+// segment's per-warp sums of squares (ss, [rank][warp]) and this CTA's verdict
+// (okv[rank]), then receive every rank's part; returns the cluster's verdict
 // (every CTA of the cluster sees the same flags).
-__device__ __forceinline__ bool flow_publish(const StepArgs& a, FlowRing& fr, FlowSmem& sm, FlowCtx& cx, int site,
-                                             bool ok) {
-  const unsigned k = cx.k[site]++;
-  const unsigned b = k & 1u;
-  float* dst = site == kSiteX ? sm.x[b] : sm.x2[b];
-  float(*ss)[8] = site == kSiteX ? sm.ssx[b] : sm.ssx2[b];
-  int* okv = site == kSiteX ? sm.okx[b] : sm.okx2[b];
-  const unsigned long long* bar = &sm.sbar[site][b];
-  const int n = cx.n, np = n >> 1, nw = (np + 31) >> 5, t = (int)threadIdx.x;
+static __device__ __noinline__ bool flow_publish_impl(const float* seg, float* dst, float* ss, int* okv,
+                                                      unsigned long long* bar, unsigned k, unsigned rank, unsigned cs,
+                                                      int seg0, int n, bool ok, int* error, int* host_error,
+                                                      unsigned long long timeout_ns) {
+  const int np = n >> 1, nw = (np + 31) >> 5, t = (int)threadIdx.x;
   float q = 0.f;
   if (t < np) {
-    const float v0 = sm.seg[2 * t], v1 = sm.seg[2 * t + 1];
-    for (unsigned r = 0; r < cx.cs; ++r) st_async2(dst + cx.seg0 + 2 * t, bar, r, v0, v1);
+    const float v0 = seg[2 * t], v1 = seg[2 * t + 1];
+    for (unsigned r = 0; r < cs; ++r) st_async2(dst + seg0 + 2 * t, bar, r, v0, v1);
     q = v0 * v0 + v1 * v1;
   }
   if (t < nw * 32) {
     q = warp_sum(q);
     if ((t & 31) == 0)
-      for (unsigned r = 0; r < cx.cs; ++r) st_async1(&ss[cx.rank][t >> 5], bar, r, q);
+      for (unsigned r = 0; r < cs; ++r) st_async1(&ss[rank * 8 + (t >> 5)], bar, r, q);
   }
-  if (t < (int)cx.cs) st_async1i(&okv[cx.rank], bar, (unsigned)t, ok ? 1 : 0);
-  bool all = flow_receive(a, fr, sm, site, k, cx.cs * (unsigned)(4 * n + 4 * nw + 4));
-  for (unsigned r = 0; r < cx.cs; ++r) all = all && (*reinterpret_cast<volatile int*>(&okv[r]) != 0);
+  if (t < (int)cs) st_async1i(&okv[rank], bar, (unsigned)t, ok ? 1 : 0);
+  bool all = flow_receive_at(bar, k, cs * (unsigned)(4 * n + 4 * nw + 4), error, host_error, timeout_ns);
+  for (unsigned r = 0; r < cs; ++r) all = all && (*reinterpret_cast<volatile int*>(&okv[r]) != 0);
+  return all;
+}
+
+// Publish at site X (x) or X2 (x'): the site's next buffer, then the
+// context's current-buffer index.
+__device__ __forceinline__ bool flow_publish(const StepArgs& a, FlowRing& fr, FlowSmem& sm, FlowCtx& cx, int site,
+                                             bool ok) {
+  const unsigned k = cx.k[site]++;
+  const unsigned b = k & 1u;
+  fmark(a, fr, kFmBarIn);
+  const bool all = site == kSiteX
+      ? flow_publish_impl(sm.seg, sm.x[b], &sm.ssx[b][0][0], sm.okx[b], &sm.sbar[kSiteX][b], k, cx.rank, cx.cs,
+                          cx.seg0, cx.n, ok, a.error, a.host_error, a.bar_timeout_ns)
+      : flow_publish_impl(sm.seg, sm.x2[b], &sm.ssx2[b][0][0], sm.okx2[b], &sm.sbar[kSiteX2][b], k, cx.rank, cx.cs,
+                          cx.seg0, cx.n, ok, a.error, a.host_error, a.bar_timeout_ns);
+  fmark(a, fr, kFmBarOut);
   if (site == kSiteX) cx.bx = b;
   else cx.bx2 = b;
   return all;
@@ -1131,7 +1174,7 @@ __global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunc
   }
   const bool ring_ok = flow_ring_begin(a, fr, flow_raw + kFlowRingOffset, wh, sizeof(T),
                                        f.mode == kFlowTrace ? f.count : 0ull);
-  if (!ring_ok && threadIdx.x == 0) set_error(a, kRingTable);
+  if (!ring_ok && threadIdx.x == 0) flow_error(a.error, a.host_error, kRingTable);
   // every CTA of the cluster learns every rank's setup verdict
   // (the barrier also orders the mbarrier initialisation before any peer's st.async)
   if (threadIdx.x < cx.cs) dsmem_store_u32(&sm.oksetup[cx.rank], threadIdx.x, ring_ok ? 1 : 0);
@@ -1193,7 +1236,7 @@ __global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunc
           if ((++polls & 63u) == 0) {
             if (ld_volatile_int(a.error) != 0) { w = kFlowExit; break; }
             if (globaltimer() - start > p.dispatch_timeout_ns) {
-              set_error(a, kBarrierTimeout);
+              flow_error(a.error, a.host_error, kBarrierTimeout);
               w = kFlowExit;
               break;
             }
@@ -1241,7 +1284,7 @@ __global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunc
         const unsigned long long start = globaltimer();
         bool good = true;
         while (ld_acquire_gpu(a.bar_counter) < target)
-          if (globaltimer() - start > a.bar_timeout_ns) { set_error(a, kBarrierTimeout); good = false; break; }
+          if (globaltimer() - start > a.bar_timeout_ns) { flow_error(a.error, a.host_error, kBarrierTimeout); good = false; break; }
         if (good) {
           if (command == kPing) {
             unsigned long long checksum = 0;
@@ -1266,7 +1309,9 @@ __global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunc
   }
   if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(&fr.stop) = 1;
   // No CTA leaves while a peer may still store into its shared memory, or
-  // before its producer has seen its copies land.
+  // before its producer has seen its copies land (the cluster barrier is the
+  // aligned form: every warp reconverges first).
+  __syncwarp();
   cluster_sync();
   if (threadIdx.x >= kThreads) return;
   if (trace) {
@@ -1286,7 +1331,7 @@ __global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunc
     const unsigned long long target = f.bar_base + (counts + 1ull) * gridDim.x;
     const unsigned long long start = globaltimer();
     while (ld_acquire_gpu(a.bar_counter) < target)
-      if (globaltimer() - start > a.bar_timeout_ns) { set_error(a, kBarrierTimeout); break; }
+      if (globaltimer() - start > a.bar_timeout_ns) { flow_error(a.error, a.host_error, kBarrierTimeout); break; }
     *a.flow_epoch = cx.epoch + processed * (unsigned long long)a.layers;
   }
   if (blockIdx.x == 0) persistent_exit<T>(a, p);

@@ -120,6 +120,25 @@ def test_fp32_is_bit_stable_across_runs_and_backends():
     check_scores(fused[0], graph[0], g.model.config.layers, "fp32", "flow vs per-op")
 
 
+@pytest.mark.parametrize("backend", [Backend.PERSISTENT, Backend.FUSED], ids=lambda b: b.name.lower())
+def test_main_shape_runs_are_bit_identical(backend):
+    # The device-loop step exchanges partial sums between clusters while other
+    # clusters still run; any race shows as runs that differ in the last bits
+    # and drift apart through the K/V ring. 260 events cover two ring revolutions.
+    config, _ = synthetic.CONFIGS["c2-main-fp32"]
+    model = synthetic.make_model(config, "fp32", seed=42)
+    events = synthetic.make_events(260, 32, seed=7)
+    runs = []
+    for _ in range(2):
+        with Runtime(model, RuntimeOptions(backend=backend, blocks=0)) as rt:
+            scores = np.array([rt.step(e) for e in events], dtype=np.float32)
+            snap = rt.snapshot()
+        runs.append((scores, snap.keys, snap.hidden))
+    np.testing.assert_array_equal(runs[1][0].view(np.uint32), runs[0][0].view(np.uint32))
+    np.testing.assert_array_equal(runs[1][1].view(np.uint32), runs[0][1].view(np.uint32))
+    np.testing.assert_array_equal(runs[1][2].view(np.uint32), runs[0][2].view(np.uint32))
+
+
 def test_device_trace_matches_step_by_step():
     g = Golden("ref-main-mixed")
     for backend in (Backend.GRAPH, Backend.FUSED, Backend.PERSISTENT):
