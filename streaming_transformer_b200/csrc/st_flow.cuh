@@ -1206,26 +1206,37 @@ __global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunc
     if (trace) {
       command = processed < f.count ? kRun : kFlowExit;
     } else {
-      if (blockIdx.x == 0 && threadIdx.x == 0) {
-        const unsigned long long start = globaltimer();
-        unsigned long long seq;
+      if (blockIdx.x == 0 && threadIdx.x < 32) {
+        // warp 0 of CTA 0: lane 0 polls the mailbox, the warp stages the event
+        // (one mapped read per lane, in parallel), lane 0 publishes the command
+        const int lane = threadIdx.x;
+        unsigned long long seq = 0;
         int cmd = 0, carg = 0;
-        while ((seq = ld_acquire_sys(&p.mailbox->request)) == previous) {
-          if (globaltimer() - start >= p.idle_ns) { cmd = kFlowExit; break; }
-          if (p.backoff) __nanosleep(128);
+        if (lane == 0) {
+          const unsigned long long start = globaltimer();
+          while ((seq = ld_acquire_sys(&p.mailbox->request)) == previous) {
+            if (globaltimer() - start >= p.idle_ns) { cmd = kFlowExit; break; }
+            if (p.backoff) __nanosleep(128);
+          }
+          if (cmd == 0) {
+            cmd = *reinterpret_cast<volatile int*>(&p.mailbox->command);
+            carg = *reinterpret_cast<volatile int*>(&p.mailbox->arg);
+          }
         }
-        if (cmd == 0) {
-          cmd = *reinterpret_cast<volatile int*>(&p.mailbox->command);
-          carg = *reinterpret_cast<volatile int*>(&p.mailbox->arg);
-          if (cmd == kRun)
-            for (int i = 0; i < kFlowFeatures; ++i) const_cast<float*>(a.input)[i] = __ldcv(f.mapped_input + i);
-          *a.flow_seq = seq;
-          previous = seq;
+        cmd = __shfl_sync(0xffffffffu, cmd, 0);
+        if (cmd == kRun)
+          for (int i = lane; i < kFlowFeatures; i += 32) const_cast<float*>(a.input)[i] = __ldcv(f.mapped_input + i);
+        __syncwarp();
+        if (lane == 0) {
+          if (cmd != kFlowExit) {
+            *a.flow_seq = seq;
+            previous = seq;
+          }
+          const unsigned long long word = ((dispatched + 1ull) << 32) |
+                                          ((unsigned long long)(unsigned)(carg + 1) << 8) | (unsigned long long)cmd;
+          __threadfence();
+          asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(a.flow_ctl), "l"(word) : "memory");
         }
-        const unsigned long long word = ((dispatched + 1ull) << 32) |
-                                        ((unsigned long long)(unsigned)(carg + 1) << 8) | (unsigned long long)cmd;
-        __threadfence();
-        asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(a.flow_ctl), "l"(word) : "memory");
       }
       if (threadIdx.x == 0) {
         const unsigned long long want = dispatched + 1ull;
