@@ -16,17 +16,16 @@
 //     z = norm1(x)                    every CTA, the gain from the ring
 //     q, k, v rows of head h          row pairs split over the cluster, RoPE and
 //                                     casts in the warp epilogue, broadcast into
-//                                     every rank through DSMEM; k, v to slot t % W
-//     cluster barrier
+//                                     every rank (st.async); k, v to slot t % W
+//     receive (the site's mbarrier)
 //     attention over [0, valid)       slots split over the cluster, an online
 //                                     softmax per warp, warps merged per CTA, the
-//                                     CTA partial broadcast through DSMEM
-//     cluster barrier; merge -> o_h (cast)
+//                                     CTA partial sent into every rank (st.async)
+//     receive; merge -> o_h (cast)
 //     out-projection rows of segment r (K-split by head): P[h][seg r] published
-//   exchange 1 (every CTA)            rank r gathers P[*][seg r] of every head,
-//                                     x'[seg r] = cast(x + cast(sum_h P[h])),
-//                                     broadcast to the cluster with its sum of
-//                                     squares; cluster barrier
+//   exchange 1 (every CTA)            every CTA gathers P[*] of every head for the
+//                                     whole width, x' = cast(x + cast(sum_h P[h])) and
+//                                     its sum of squares, no cluster handoff
 //   FFN (every CTA)                   z = norm2(x'); gate/up row pairs of this CTA's
 //                                     ffn slice -> SwiGLU; down-projection K-split
 //                                     over the slice -> partial d-vector;
@@ -34,7 +33,8 @@
 //                                     rank r publishes D[c][seg r]
 //   exchange 2 (every CTA)            rank r gathers D[*][seg r] of every cluster,
 //                                     x[seg r] = cast(x' + cast(sum_c D[c])),
-//                                     broadcast; cluster barrier
+//                                     published into every rank (st.async) with its
+//                                     sum of squares and the rank's verdict
 //
 // Publishing is by tagged records: an 8-byte store of {fp32 value, 32-bit tag}
 // (single-copy atomic), the tag unique to (step, layer). A consumer polls the
@@ -188,12 +188,12 @@ struct alignas(128) FlowRing {
 // buffered by the parity of its exchange count: a sender reaches exchange
 // k + 2 of a site only after every receiver has sent its part of exchange
 // k + 1, which each does after its last read of exchange k's buffer.
-enum FlowSite : int { kSiteX = 0, kSiteX2 = 1, kSiteQkv = 2, kSiteAtt = 3, kSiteDred = 4, kSites = 5 };
+enum FlowSite : int { kSiteX = 0, kSiteQkv = 1, kSiteAtt = 2, kSiteDred = 3, kSites = 4 };
 
 struct alignas(128) FlowSmem {
   unsigned long long sbar[kSites][2];    // receive mbarriers per site and parity
   float x[2][kFlowMaxD];                 // residual entering the layer (site X)
-  float x2[2][kFlowMaxD];                // residual after attention (site X2)
+  float x2[kFlowMaxD];                   // residual after attention (every CTA computes all of it)
   float z[kFlowMaxD];                    // norm output, GEMV input
   float dred[2][kFlowMaxD];              // down partials from every rank, [CS][n] (site DRED)
   float seg[kFlowMaxD];                  // this rank's segment values before publishing
@@ -205,9 +205,7 @@ struct alignas(128) FlowSmem {
   float o[kFlowHd];                      // merged attention output (cast)
   float act[kFlowMaxAct];                // this CTA's SwiGLU slice
   float ssx[2][kFlowMaxCluster][8];      // sum of squares of x per rank and warp (site X)
-  float ssx2[2][kFlowMaxCluster][8];     // same for x' (site X2)
   int okx[2][kFlowMaxCluster];           // verdict per rank (site X)
-  int okx2[2][kFlowMaxCluster];          // verdict per rank (site X2)
   int oksetup[kFlowMaxCluster];          // launch setup verdict per rank
   float2 rope_cs[kFlowHd / 2];           // cos, sin of t * frequency
   float rope[kFlowHd / 2];               // frequencies 10000^(-2i/hd)
@@ -691,6 +689,63 @@ __device__ __forceinline__ bool flow_gather(const StepArgs& a, FlowRing&, const 
   return flow_gather_impl(rec, D, nsrc, seg0, n, tag, sm.u.red, sm.seg, a.error, a.host_error, a.bar_timeout_ns);
 }
 
+// Every element of x' = cast(x + cast(sum_h P[h])) for the whole width, into
+// x2 (local), with sum(x'^2) returned through *ss; heads summed in a fixed
+// order. Thread t polls element pair t % (D/2) for heads congruent to t / (D/2).
+template <typename T, int D>
+__device__ __forceinline__ bool flow_gather_full(const unsigned long long* rec, int nsrc, unsigned tag,
+                                                 const float* x, float* x2, float* red, float* scratch, float* ss,
+                                                 int* error, int* host_error, unsigned long long timeout_ns) {
+  constexpr int np = D / 2, G = kThreads / np;
+  const int e = (int)threadIdx.x % np, g = (int)threadIdx.x / np;
+  float s0 = 0.f, s1 = 0.f;
+  bool ok = true;
+  unsigned long long start = 0;
+  unsigned polls = 0;
+  for (int src0 = g; src0 < nsrc && ok; src0 += 8 * G) {
+    unsigned long long r[8][2];
+    while (true) {
+      bool ready = true;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int src = src0 + k * G;
+        if (src < nsrc) ll_load2(rec + (size_t)src * D + 2 * e, r[k][0], r[k][1]);
+        else r[k][0] = r[k][1] = ll_pack(0.f, tag);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ready = ready && ll_tag(r[k][0]) == tag && ll_tag(r[k][1]) == tag;
+      if (ready) break;
+      __nanosleep(64);
+      if ((++polls & 31u) == 0) {
+        if (ld_volatile_int(error) != 0) { ok = false; break; }
+        const unsigned long long now = globaltimer();
+        if (start == 0) start = now;
+        else if (now - start > timeout_ns) { flow_error(error, host_error, kBarrierTimeout); ok = false; break; }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) { s0 += ll_value(r[k][0]); s1 += ll_value(r[k][1]); }
+  }
+  red[g * D + 2 * e] = s0;
+  red[g * D + 2 * e + 1] = s1;
+  ok = flow_bar_and(ok);
+  float q = 0.f;
+  for (int i = threadIdx.x; i < D; i += kThreads) {
+    float t = 0.f;
+    for (int k = 0; k < G; ++k) t += red[k * D + i];
+    const float v = Storage<T>::round(x[i] + Storage<T>::round(t));
+    x2[i] = v;
+    q = fmaf(v, v, q);
+  }
+  q = warp_sum(q);
+  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = q;
+  flow_bar();
+  float total = 0.f;
+  for (int w = 0; w < kWarps; ++w) total += scratch[w];
+  *ss = total;
+  return ok;
+}
+
 // ---------------------------------------------------------------- step context
 struct FlowCtx {
   unsigned rank, cs, id, nc;
@@ -700,7 +755,7 @@ struct FlowCtx {
   unsigned long long epoch;  // tag base of this launch
   unsigned long long steps;  // steps this launch has run
   unsigned k[kSites];        // exchanges so far per site (selects buffer and mbarrier phase)
-  unsigned bx, bx2;          // buffers holding the current x and x'
+  unsigned bx;               // buffer holding the current x
 };
 
 // Bounded wait for an exchange phase that had not completed at the first try.
@@ -760,21 +815,15 @@ static __device__ __noinline__ bool flow_publish_impl(const float* seg, float* d
   return all;
 }
 
-// Publish at site X (x) or X2 (x'): the site's next buffer, then the
-// context's current-buffer index.
-__device__ __forceinline__ bool flow_publish(const StepArgs& a, FlowRing& fr, FlowSmem& sm, FlowCtx& cx, int site,
-                                             bool ok) {
-  const unsigned k = cx.k[site]++;
+// Publish x (site X) into the site's next buffer, then make it current.
+__device__ __forceinline__ bool flow_publish(const StepArgs& a, FlowRing& fr, FlowSmem& sm, FlowCtx& cx, bool ok) {
+  const unsigned k = cx.k[kSiteX]++;
   const unsigned b = k & 1u;
   fmark(a, fr, kFmBarIn);
-  const bool all = site == kSiteX
-      ? flow_publish_impl(sm.seg, sm.x[b], &sm.ssx[b][0][0], sm.okx[b], &sm.sbar[kSiteX][b], k, cx.rank, cx.cs,
-                          cx.seg0, cx.n, ok, a.error, a.host_error, a.bar_timeout_ns)
-      : flow_publish_impl(sm.seg, sm.x2[b], &sm.ssx2[b][0][0], sm.okx2[b], &sm.sbar[kSiteX2][b], k, cx.rank, cx.cs,
-                          cx.seg0, cx.n, ok, a.error, a.host_error, a.bar_timeout_ns);
+  const bool all = flow_publish_impl(sm.seg, sm.x[b], &sm.ssx[b][0][0], sm.okx[b], &sm.sbar[kSiteX][b], k, cx.rank,
+                                     cx.cs, cx.seg0, cx.n, ok, a.error, a.host_error, a.bar_timeout_ns);
   fmark(a, fr, kFmBarOut);
-  if (site == kSiteX) cx.bx = b;
-  else cx.bx2 = b;
+  cx.bx = b;
   return all;
 }
 
@@ -977,7 +1026,7 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
     flow_rows<T, kFlowFeatures, 1>(a, fr, cur, sm.plan.in, xr,
                                    [&](int r, const float (&v)[1]) { sm.seg[r] = Storage<T>::round(v[0]); });
     flow_bsync(fr);
-    if (!flow_publish(a, fr, sm, cx, kSiteX, !fr.failed)) return false;
+    if (!flow_publish(a, fr, sm, cx, !fr.failed)) return false;
     fmark(a, fr, kFmIn);
   }
   for (int l = 0; l < a.layers; ++l) {
@@ -986,23 +1035,20 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
     if (cx.heads_here)
       for (int h = (int)cx.id; h < a.heads; h += (int)cx.nc)
         hok = flow_head<T, D>(a, fr, cur, sm, cx, l, h, t, tag, h == (int)cx.id) && hok;
-    // exchange 1: x'[seg] = cast(x[seg] + cast(sum_h P[h][seg]))
+    // exchange 1 (whole width, no cluster handoff): x' = cast(x + cast(sum_h P[h]))
+    float ssq = 0.f;
+    bool ok1;
     {
       const unsigned long long* P = a.ll_heads + (size_t)(tag & 1u) * a.heads * D;
-      const bool ok = flow_gather<D>(a, fr, P, a.heads, seg0, n, tag, sm) && hok;
+      ok1 = flow_gather_full<T, D>(P, a.heads, tag, sm.x[cx.bx], sm.x2, sm.u.red, sm.warp_scratch, &ssq, a.error,
+                                   a.host_error, a.bar_timeout_ns) && hok && !fr.failed;
       fmark(a, fr, kFmGather1);
-      const float* x = sm.x[cx.bx];
-      if ((int)threadIdx.x < n)
-        sm.seg[threadIdx.x] = Storage<T>::round(x[seg0 + threadIdx.x] + Storage<T>::round(sm.seg[threadIdx.x]));
-      flow_bsync(fr);
-      if (!flow_publish(a, fr, sm, cx, kSiteX2, ok && !fr.failed)) return false;
-      fmark(a, fr, kFmPub2);
     }
     // FFN: norm2, gate/up -> SwiGLU, down partial
     bool dok = true;
     {
-      const float scale = flow_norm_scale(sm.ssx2[cx.bx2], cx.cs, n, D, a.epsilon);
-      const float* x2 = sm.x2[cx.bx2];
+      const float scale = 1.0f / sqrtf(ssq / (float)D + a.epsilon);
+      const float* x2 = sm.x2;
       flow_gain<T>(a, fr, cur, [&](const T* g) {
         for (int i = threadIdx.x; i < D; i += kThreads)
           sm.z[i] = Storage<T>::round(x2[i] * scale * Storage<T>::load(g, i));
@@ -1079,16 +1125,16 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
     // exchange 2: x[seg] = cast(x'[seg] + cast(sum_c D[c][seg]))
     {
       const unsigned long long* Dq = a.ll_clusters + (size_t)(tag & 1u) * cx.nc * D;
-      const bool ok = flow_gather<D>(a, fr, Dq, (int)cx.nc, seg0, n, tag, sm) && dok;
+      const bool ok = flow_gather<D>(a, fr, Dq, (int)cx.nc, seg0, n, tag, sm) && dok && ok1;
       fmark(a, fr, kFmGather2);
-      const float* x2 = sm.x2[cx.bx2];
+      const float* x2 = sm.x2;
       if ((int)threadIdx.x < n) {
         const float v = Storage<T>::round(x2[seg0 + threadIdx.x] + Storage<T>::round(sm.seg[threadIdx.x]));
         sm.seg[threadIdx.x] = v;
         if (cx.score_cluster) a.hidden[(size_t)l * D + seg0 + threadIdx.x] = v;
       }
       flow_bsync(fr);
-      if (!flow_publish(a, fr, sm, cx, kSiteX, ok && !fr.failed)) return false;
+      if (!flow_publish(a, fr, sm, cx, ok && !fr.failed)) return false;
       fmark(a, fr, kFmPub1);
     }
   }
@@ -1142,7 +1188,7 @@ __global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunc
   cx.epoch = ld_cg_u64(a.flow_epoch);
   cx.steps = 0;
   for (int i = 0; i < kSites; ++i) cx.k[i] = 0;
-  cx.bx = cx.bx2 = 0;
+  cx.bx = 0;
   fr.tl_n = 0;
   const unsigned long long t0 = ld_cg_u64(a.position);
   for (int i = threadIdx.x; i < kFlowHd / 2; i += kThreads) sm.rope[i] = a.rope_freq[i];
