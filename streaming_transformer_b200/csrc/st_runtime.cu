@@ -878,7 +878,11 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
                                         (int)flow_smem_bytes()), "cudaFuncSetAttribute flow") != ST_OK)
         return bail(ST_ERR_CUDA);
       int best_cs = 0, best_nc = 0;
-      for (int cs : {8, 4}) {
+      // ST_FLOW_CLUSTER=2/4/8 forces the cluster size (tuning).
+      const char* cenv = std::getenv("ST_FLOW_CLUSTER");
+      const int forced = cenv ? std::atoi(cenv) : 0;
+      for (int cs : {8, 4, 2}) {
+        if (forced ? cs != forced : cs == 2) continue;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(cs);
         cfg.blockDim = dim3(flow_threads());
