@@ -220,6 +220,12 @@ class Runtime:
             raise
         self._in = np.zeros((self.streams, c.features), dtype=np.float32)
         self._out = np.zeros(self.streams, dtype=np.float32)
+        # the per-step call reuses its pointers and bound entry point
+        self._in0 = self._in[0]
+        self._in_p = _fptr(self._in)
+        self._out_p = _fptr(self._out)
+        self._st_step = lib.st_step
+        self._features = c.features
 
     # -- lifecycle
     def close(self) -> None:
@@ -243,8 +249,10 @@ class Runtime:
     # -- hot path
     def step(self, event) -> float:
         """reference Runtime::step: one event (features floats) -> one score."""
-        self._in[0, :] = np.asarray(event, dtype=np.float32).reshape(-1)[: self.config.features]
-        _check(library().st_step(self._h, _fptr(self._in), _fptr(self._out)), self._h)
+        self._in0[:] = np.asarray(event, dtype=np.float32).reshape(-1)[: self._features]
+        code = self._st_step(self._h, self._in_p, self._out_p)
+        if code != ST_OK:
+            _check(code, self._h)
         return float(self._out[0])
 
     def step_batch(self, events) -> np.ndarray:
