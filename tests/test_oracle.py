@@ -180,3 +180,13 @@ def test_streaming_differs_from_recomputed_window():
     fresh = Oracle(m)
     naive = [fresh.step(e) for e in events[-5:]][-1]
     assert abs(naive - last) > 1e-4
+
+
+def test_stress_sampling_and_reset_schedule():
+    import stress
+    pts = stress.sample_points(1_000_000, 16, 3)
+    assert len(pts) == 16 and pts[0] == 0 and pts[-1] == 1_000_000 - 4
+    assert all(b > a for a, b in zip(pts, pts[1:]))
+    assert stress.sample_points(3, 4, 3) == []
+    assert [i for i in range(30_100) if stress.resets_before(i, 10007)] == [10007, 20014, 30021]
+    assert not any(stress.resets_before(i, 0) for i in range(100))
