@@ -22,9 +22,21 @@ Arms (both print the same metric/unit/config):
     The reference's CPU step. Its Eigen implementation (src/cpu/Cpu.cpp)
     cannot be built here (no Eigen), so the C restatement in oracle/ is timed
     with every host thread, on a bounded sample; rank 0 only.
+Steady state: the device arm first steps max(--warmup, window) untimed events
+from reset, so every timed step attends over a full window, then times K
+events that continue from that state (st_device_trace_continue).
+
 Multi-GPU (torchrun): the single-stream configs do not shard, so every rank
 runs an independent replica stream (weak scaling, no collective on the step
-path); value = total steps of all ranks / max device time.
+path); value = total steps of all ranks / max device time. With --streams S > 1
+the S streams are the job's total and are partitioned evenly over the ranks
+(S / N each; strong scaling, as the benchmark's C4 line defines it).
+
+Unless --no-c4 is given (or the workload is C4 itself), the line also carries a
+"c4" record: Large bf16 with 256 streams in total partitioned over the N GPUs,
+stepped by the batched round from a full window, aggregate stream-steps/s
+against the per-GPU-count roofline (every GPU reads the whole weights once per
+round plus its own streams' K/V).
 """
 from __future__ import annotations
 
@@ -61,7 +73,10 @@ def parse_args():
     p.add_argument("--config", default="c2-main-fp32", choices=sorted(synthetic.CONFIGS))
     p.add_argument("--window", type=int, default=0, help="override the window (C3 sweep)")
     p.add_argument("--streams", type=int, default=1,
-                   help="independent streams per GPU (C4/C5-A: the total is streams x GPUs, partitioned by rank)")
+                   help="independent streams in total, partitioned evenly over the GPUs (C4: 256); "
+                        "1 = one replica stream per GPU")
+    p.add_argument("--no-c4", action="store_true", help="skip the C4 256-stream partition record")
+    p.add_argument("--c4-rounds", type=int, default=100, help="timed rounds of the C4 record (at most --steps)")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
@@ -74,18 +89,31 @@ def workload(args):
     return config, mode
 
 
+def streams_per_rank(total, world):
+    """Streams each rank steps: 1 (a replica) when total is 1, else total / world."""
+    if total <= 1:
+        return 1
+    if total % world:
+        raise SystemExit(f"--streams {total} does not split evenly over {world} GPUs")
+    return total // world
+
+
 def config_json(args, config, mode, working_set, world=1):
-    s = max(1, args.streams)
-    per_gpu = "single stream per GPU" if s == 1 else f"{s} streams per GPU"
+    total = max(1, args.streams)
+    s = streams_per_rank(total, world)
+    per_gpu = ("single stream per GPU" if total == 1 else
+               f"{total} streams in total, {s} per GPU")
     return {
         "workload": f"{args.config}: {mode} {per_gpu}, d{config.width} L{config.layers} "
                     f"H{config.heads} hd{config.head_dim} F{config.ffn} W{config.window}, "
                     f"{config.features} features",
         "model": "local-causal pre-RMSNorm transformer (streaming step)",
+        "streams_total": total if total > 1 else world,
         "streams_per_gpu": s,
         "global_batch": s * world,
         "seq_len": config.window,
-        "parallelism": "streams partitioned across GPUs (independent, no collective)" if s > 1
+        "steady_state": "timed steps follow max(warmup, window) untimed steps: every timed step attends a full window",
+        "parallelism": "streams partitioned across GPUs (independent, no collective)" if total > 1
                        else "replicas (independent streams, no collective)",
         "data": "seeded N(0,0.02) weights, unit norm gains, N(0,1) events",
         "l2": ("working set %.1f MB > 126 MB L2, no flush" % (working_set / 1e6)) if working_set > L2_BYTES
@@ -225,7 +253,8 @@ def run_reference(args):
     o.run(probe)
     per = max((time.perf_counter() - t0) / 2, 1e-6)
     o.reset()
-    warm = int(min(args.warmup, 30.0 / per))
+    # as on the device arm, at least a full window of untimed events first
+    warm = int(min(max(args.warmup, config.window), 30.0 / per))
     timed = int(max(1, min(args.steps, 150.0 / per)))
     events = synthetic.make_events(warm + timed, config.features, seed=123)
     o.run(events[:warm])
@@ -264,6 +293,38 @@ def combine_ranks(values, dist=None, group=None):
     return [float(x) for x in t]
 
 
+def c4_roofline(world, peak_gbs):
+    """Per-GPU-count roofline of the C4 partition: every GPU reads the whole
+    weights once per round plus its own streams' K/V over a full window and
+    writes one K/V row per stream and layer; aggregate stream-steps/s."""
+    config, mode = synthetic.CONFIGS["c4-large-bf16"]
+    per_rank = 256 // world
+    per_gpu_bytes = metrics.step_bytes(config, mode, config.window, streams=per_rank)
+    round_s = per_gpu_bytes / (peak_gbs * 1e9)
+    return 256 / round_s, int(per_gpu_bytes)
+
+
+def run_rounds(model, config, S, rank, warm, timed, local, seed_base):
+    """Batched rounds of S streams: `warm` untimed rounds from reset (filling the
+    windows), then `timed` rounds continuing from that state. Returns
+    (us per round, kernels launched in the timed region, runtime info)."""
+    import torch
+    events = np.stack([synthetic.make_events(warm + timed, config.features, seed=seed_base + rank * S + s)
+                       for s in range(S)], axis=1)
+    dev = torch.from_numpy(np.ascontiguousarray(events)).cuda()
+    rt = Runtime(model, RuntimeOptions(backend=Backend.FUSED, blocks=0, device=local), streams=S)
+    try:
+        rt.device_trace_resident(dev.data_ptr(), warm)
+        torch.cuda.synchronize()
+        stride = S * config.features
+        us, launches = rt.device_trace_continue(dev[warm:].data_ptr(), timed)
+        info = rt.info()
+    finally:
+        rt.close()
+    del dev
+    return us, launches, info, stride
+
+
 def run_b200(args):
     import torch
     world, rank, local = dist_env()
@@ -275,7 +336,7 @@ def run_b200(args):
         # Host-side coordination (barriers, max over ranks) runs over gloo: an
         # NCCL barrier synchronizes the whole device, which would wait for the
         # resident persistent worker of the e2e phase until its idle budget
-        # ends it. The step path itself has no collective (replicas).
+        # ends it. The step path itself has no collective.
         host = dist.new_group(backend="gloo", timeout=timedelta(seconds=120))
 
     def barrier(device_wide=True):
@@ -292,10 +353,13 @@ def run_b200(args):
     config, mode = workload(args)
     model = synthetic.make_model(config, mode, seed=42)
     K, W = max(1, args.steps), max(3, args.warmup)
-    S = max(1, args.streams)
+    total = max(1, args.streams)
+    S = streams_per_rank(total, world)
+    # Untimed device steps before the timed region: at least a full window.
+    Wd = max(W, config.window)
     # stream g = rank * S + s has its own seeded trace
-    events = np.stack([synthetic.make_events(K + W, config.features, seed=123 + rank * S + s) for s in range(S)],
-                      axis=1)  # [K + W, S, features]
+    events = np.stack([synthetic.make_events(K + Wd, config.features, seed=123 + rank * S + s) for s in range(S)],
+                      axis=1)  # [K + Wd, S, features]
     e2e_lat = []
     with ClockSampler(local) as clocks:
         # One stream: the persistent mailbox (lowest latency). Several streams:
@@ -304,46 +368,63 @@ def run_b200(args):
         rt = Runtime(model, RuntimeOptions(backend=backend, blocks=0, device=local), streams=S)
         step = (lambda e: rt.step(e[0])) if S == 1 else rt.step_batch
         try:
-            # ---- e2e through the public API: host events in, host scores out
-            for e in events[:W]:
+            # ---- e2e through the public API: host events in, host scores out.
+            # The warm-up fills the window, so the timed calls are steady state.
+            for e in events[:Wd]:
                 step(e)
-            rt.reset()
             barrier(device_wide=False)
             t_start = time.perf_counter()
-            for e in events[W:W + K]:
+            for e in events[Wd:Wd + K]:
                 t0 = time.perf_counter_ns()
                 step(e)
                 e2e_lat.append((time.perf_counter_ns() - t0) / 1000.0)
             e2e_wall = time.perf_counter() - t_start
             barrier(device_wide=False)
-            # ---- device-resident: trace preloaded in HBM, one resident kernel
+            # ---- device-resident: trace preloaded in HBM, one resident kernel;
+            # Wd untimed steps from reset, then K timed steps from that state
             dev_events = torch.from_numpy(np.ascontiguousarray(events)).cuda()
             torch.cuda.synchronize()
-            rt.device_trace_resident(dev_events.data_ptr(), W)       # warm-up (untimed)
+            rt.device_trace_resident(dev_events.data_ptr(), Wd)       # warm-up (untimed)
             barrier()
-            us, launches = rt.device_trace_resident(dev_events[W:].data_ptr(), K)  # us per round of S streams
+            us, launches = rt.device_trace_continue(dev_events[Wd:].data_ptr(), K)  # us per round of S streams
             barrier()
             info = rt.info()
         finally:
             rt.close()
+        del dev_events
+        c4 = None
+        if not args.no_c4 and args.config != "c4-large-bf16":
+            c4_config, c4_mode = synthetic.CONFIGS["c4-large-bf16"]
+            c4_model = synthetic.make_model(c4_config, c4_mode, seed=42)
+            c4_S = 256 // world
+            c4_K = max(1, min(K, args.c4_rounds))
+            barrier()
+            c4_us, c4_launches, c4_info, _ = run_rounds(c4_model, c4_config, c4_S, rank, c4_config.window, c4_K,
+                                                        local, 7000)
+            barrier()
+            c4 = (c4_us, c4_K, c4_S, c4_launches, c4_info, c4_config, c4_mode)
     elapsed_s = us * K / 1e6
-    max_elapsed, max_e2e = combine_ranks([elapsed_s, e2e_wall], dist, host)
+    times = [elapsed_s, e2e_wall] + ([c4[0] * c4[1] / 1e6] if c4 else [])
+    maxed = combine_ranks(times, dist, host)
+    max_elapsed, max_e2e = maxed[0], maxed[1]
     if dist:
         dist.destroy_process_group()
     if rank != 0:
         return 0
     value = world * S * K / max_elapsed
     peak, peak_src = measured_peak()
-    alg = metrics.trace_bytes(config, mode, K, streams=S)
+    alg = metrics.trace_bytes(config, mode, K, start=Wd, streams=S)
     achieved = alg / K / (us * 1e-6) / 1e9
     traffic, traffic_src = measured_traffic(args.config, kernel_name(info))
     ws = metrics.weight_bytes(config, mode) + S * 2 * config.layers * config.width * config.window * metrics.ELEM_BYTES[mode]
     line = {
         "metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": K, "warmup": W,
-        "ms_per_step": max_elapsed * 1000.0 / K, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": max_elapsed * 1000.0 / K, "higher_is_better": True,
+        "scaling": "strong" if total > 1 else "weak",
         "vs_baseline": None, "dtype": mode, "data": "synthetic",
         "config": config_json(args, config, mode, ws, world),
-        "p50_us_per_step_device": us,
+        "mean_us_per_step_device": us,
+        "device_warmup_steps": Wd,
         "e2e": {"value": world * S * K / max_e2e, "unit": "steps/s", "h2d_bytes_per_step": 4 * config.features * S,
                 "d2h_bytes_per_step": 4 * S, "p50_us": metrics.nearest_rank(e2e_lat, 0.5),
                 "p99_us": metrics.nearest_rank(e2e_lat, 0.99),
@@ -362,6 +443,20 @@ def run_b200(args):
                     "barriers_per_step": info.get("barriers_per_step"), "batched": info.get("batched"),
                     "batched_grid": info.get("batched_grid"), "batched_splits": info.get("batched_splits")},
     }
+    if c4:
+        c4_us, c4_K, c4_S, c4_launches, c4_info, c4_config, c4_mode = c4
+        c4_value = world * c4_S * c4_K / maxed[2]
+        roof, per_gpu_bytes = c4_roofline(world, peak)
+        line["c4"] = {
+            "workload": (f"c4-large-bf16: 256 streams in total, {c4_S} per GPU on {world} GPU(s), d1024 L12 H16 "
+                         f"F4096 W256 bf16, batched round, {c4_config.window} untimed rounds then {c4_K} timed"),
+            "value": c4_value, "unit": "stream-steps/s", "scaling": "strong", "streams_total": 256,
+            "streams_per_gpu": c4_S, "rounds": c4_K, "ms_per_round": maxed[2] * 1000.0 / c4_K,
+            "roofline_stream_steps_per_s": roof, "roofline_frac": c4_value / roof,
+            "per_gpu_bytes_per_round": per_gpu_bytes, "peak_source": peak_src,
+            "kernel": kernel_label(c4_info, c4_mode, c4_S), "gpu_launches": c4_launches,
+            "tensor_cores": c4_info.get("batched_tensor_cores"),
+        }
     if world == 1 and not args.no_cpu_baseline:
         sps, n, dt = time_cpu_oracle(model, events[:, 0], 1, args.cpu_seconds, K)
         line["cpu_baseline"] = {

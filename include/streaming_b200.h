@@ -175,6 +175,14 @@ int st_device_timeline_cta(st_runtime* rt, const float* inputs, size_t count, in
 int st_device_trace_resident(st_runtime* rt, const float* device_inputs, size_t count,
                              double* us_per_step, uint64_t* kernel_launches);
 
+/* Same as st_device_trace_resident, but from the current state: no reset
+ * before the timed region, so positions continue where the previous step,
+ * trace or st_load_state left them (steady-state timing with a full window).
+ * *kernel_launches counts every kernel of the timed region. New; the
+ * reference's deviceTrace always starts from reset. */
+int st_device_trace_continue(st_runtime* rt, const float* device_inputs, size_t count,
+                             double* us_per_step, uint64_t* kernel_launches);
+
 /* Allocation-free attention. No counterpart in the reference.
  *
  * Split-window attention over one layer's K/V ring, as the step computes it,

@@ -454,7 +454,7 @@ __device__ __forceinline__ void flow_release(FlowRing& fr, FlowCur& cur) {
 // `steps` bounds the chunks issued (0: unbounded). Returns false when the
 // table does not fit (the host checks this before choosing the kernel).
 __device__ inline bool flow_ring_begin(const StepArgs& a, FlowRing& fr, unsigned char* buf, const Where& w,
-                                       size_t elem, unsigned long long steps) {
+                                       size_t elem, unsigned long long steps, unsigned capacity) {
   if (threadIdx.x == kFlowProducer) {
     fr.head = fr.tail = fr.issued = fr.released = 0;
     fr.head_off = 0;
@@ -463,7 +463,7 @@ __device__ inline bool flow_ring_begin(const StepArgs& a, FlowRing& fr, unsigned
     fr.keep_policy = policy_evict_last();
     fr.stream_policy = policy_evict_first();
     fr.buf = buf;
-    fr.capacity = kFlowRingCapacity;
+    fr.capacity = capacity;
     fr.next = 0;
     int n = 0;
     bool ok = true;
@@ -781,7 +781,8 @@ __device__ __forceinline__ bool flow_receive_at(unsigned long long* bar, unsigne
   if (threadIdx.x == 0) mbar_expect_tx(bar, bytes);
   return mbar_try_wait_cluster(bar, parity) || flow_receive_slow(bar, parity, error, host_error, timeout_ns);
 }
-__device__ __forceinline__ bool flow_receive(const StepArgs& a, FlowRing& fr, FlowSmem& sm, int site, unsigned k,
+template <class Sm>
+__device__ __forceinline__ bool flow_receive(const StepArgs& a, FlowRing& fr, Sm& sm, int site, unsigned k,
                                              unsigned bytes) {
   fmark(a, fr, kFmBarIn);
   const bool ok = flow_receive_at(&sm.sbar[site][k & 1u], k, bytes, a.error, a.host_error, a.bar_timeout_ns);
@@ -816,7 +817,8 @@ static __device__ __noinline__ bool flow_publish_impl(const float* seg, float* d
 }
 
 // Publish x (site X) into the site's next buffer, then make it current.
-__device__ __forceinline__ bool flow_publish(const StepArgs& a, FlowRing& fr, FlowSmem& sm, FlowCtx& cx, bool ok) {
+template <class Sm>
+__device__ __forceinline__ bool flow_publish(const StepArgs& a, FlowRing& fr, Sm& sm, FlowCtx& cx, bool ok) {
   const unsigned k = cx.k[kSiteX]++;
   const unsigned b = k & 1u;
   fmark(a, fr, kFmBarIn);
@@ -1167,11 +1169,15 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
 // CTA 0 polls the mapped mailbox, stages the event and publishes each command
 // on a tagged control word every CTA polls; the score CTA publishes RUN
 // completions; RESET ends with a count of CTAs on the barrier counter.
-template <typename T, int D>
-__global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunch f) {
-  extern __shared__ __align__(128) unsigned char flow_raw[];
-  FlowSmem& sm = *reinterpret_cast<FlowSmem*>(flow_raw);
-  FlowRing& fr = *reinterpret_cast<FlowRing*>(flow_raw + sizeof(FlowSmem));
+// The body of the single-stream step kernels (k4_flow here, k5_chain in
+// st_chain.cuh): Sm is the kernel's shared-memory struct (the ring bookkeeping
+// follows it, the ring buffer starts at ring_offset), step(a, fr, cur, sm, cx,
+// event, t, score_dst, score_copy) runs one event.
+template <typename T, int D, class Sm, class Step>
+__device__ __forceinline__ void flow_run(const StepArgs& a, const FlowLaunch& f, unsigned char* flow_raw,
+                                         size_t ring_offset, unsigned ring_capacity, Step&& step) {
+  Sm& sm = *reinterpret_cast<Sm*>(flow_raw);
+  FlowRing& fr = *reinterpret_cast<FlowRing*>(flow_raw + sizeof(Sm));
   if (!cluster_shape_ok(a)) {
     if (f.mode == kFlowPersistent && blockIdx.x == 0) persistent_exit<T>(a, f.p);
     return;
@@ -1218,8 +1224,8 @@ __global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunc
     }
     fence_mbar_init();
   }
-  const bool ring_ok = flow_ring_begin(a, fr, flow_raw + kFlowRingOffset, wh, sizeof(T),
-                                       f.mode == kFlowTrace ? f.count : 0ull);
+  const bool ring_ok = flow_ring_begin(a, fr, flow_raw + ring_offset, wh, sizeof(T),
+                                       f.mode == kFlowTrace ? f.count : 0ull, ring_capacity);
   if (!ring_ok && threadIdx.x == 0) flow_error(a.error, a.host_error, kRingTable);
   // every CTA of the cluster learns every rank's setup verdict
   // (the barrier also orders the mbarrier initialisation before any peer's st.async)
@@ -1311,7 +1317,7 @@ __global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunc
       const unsigned long long t = trace ? t0 + processed : ld_cg_u64(a.position);
       const float* event = trace ? f.inputs + processed * kFlowFeatures : a.input;
       float* copy = trace && f.scores ? f.scores + processed : nullptr;
-      if (!flow_step<T, D>(a, fr, cur, sm, cx, event, t, a.score, copy)) {
+      if (!step(a, fr, cur, sm, cx, event, t, a.score, copy)) {
         ok = false;
         break;
       }
@@ -1392,6 +1398,16 @@ __global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunc
     *a.flow_epoch = cx.epoch + processed * (unsigned long long)a.layers;
   }
   if (blockIdx.x == 0) persistent_exit<T>(a, p);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunch f) {
+  extern __shared__ __align__(128) unsigned char flow_raw[];
+  flow_run<T, D, FlowSmem>(a, f, flow_raw, kFlowRingOffset, kFlowRingCapacity,
+                           [](const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSmem& sm, FlowCtx& cx,
+                              const float* event, unsigned long long t, float* dst, float* copy) {
+                             return flow_step<T, D>(a, fr, cur, sm, cx, event, t, dst, copy);
+                           });
 }
 
 }  // namespace st

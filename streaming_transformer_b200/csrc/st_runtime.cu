@@ -1301,13 +1301,13 @@ int st_trace_step(st_runtime* rt, const float* input, float* score, st_trace_fn 
 }
 
 static int device_trace_impl(st_runtime* rt, const float* dev_inputs, size_t count, float* dev_scores,
-                             double* us_per_step) {
+                             double* us_per_step, bool reset = true) {
   const int S = rt->desc.streams;
   const size_t stride = (size_t)S * rt->desc.features;
   StepArgs a = rt->args;
   a.input = rt->dev_input;
   a.score = rt->dev_score;
-  ST_TRY(launch_reset(rt, 0, S));
+  if (reset) ST_TRY(launch_reset(rt, 0, S));
   ST_CUDA(rt, cudaEventRecord(rt->ev_start, rt->stream));
   if (rt->batched) {
     ST_TRY(launch_rounds(rt, a, dev_inputs, count, dev_scores));
@@ -1412,6 +1412,18 @@ int st_device_trace_resident(st_runtime* rt, const float* device_inputs, size_t 
   ST_TRY(device_trace_impl(rt, device_inputs, count, nullptr, us_per_step));
   // The reset that precedes the timed region is not counted.
   if (kernel_launches) *kernel_launches = rt->launches - before - 1;
+  return ST_OK;
+}
+
+int st_device_trace_continue(st_runtime* rt, const float* device_inputs, size_t count, double* us_per_step,
+                             uint64_t* kernel_launches) {
+  if (!rt || !device_inputs || count == 0) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
+  if (rt->opt.backend == ST_BACKEND_PERSISTENT) ST_TRY(st_stop(rt));
+  const uint64_t before = rt->launches;
+  ST_TRY(device_trace_impl(rt, device_inputs, count, nullptr, us_per_step, false));
+  if (kernel_launches) *kernel_launches = rt->launches - before;
   return ST_OK;
 }
 

@@ -121,6 +121,8 @@ def library() -> ctypes.CDLL:
             "st_device_timeline_cta": (I, [P, F, S, I, ctypes.POINTER(ctypes.c_longlong), S, ctypes.POINTER(S)]),
             "st_device_trace_resident": (I, [P, ctypes.c_void_p, S, ctypes.POINTER(ctypes.c_double),
                                              ctypes.POINTER(U64)]),
+            "st_device_trace_continue": (I, [P, ctypes.c_void_p, S, ctypes.POINTER(ctypes.c_double),
+                                             ctypes.POINTER(U64)]),
             "st_info": (I, [P, ctypes.c_char_p, S, ctypes.POINTER(S)]),
             "st_probe": (I, [I, ctypes.c_char_p, S, ctypes.POINTER(S)]),
             "st_kernel_launches": (U64, [P]),
@@ -342,6 +344,15 @@ class Runtime:
         us = ctypes.c_double(0)
         launches = ctypes.c_uint64(0)
         _check(library().st_device_trace_resident(self._h, ctypes.c_void_p(device_ptr), int(count),
+                                                  ctypes.byref(us), ctypes.byref(launches)), self._h)
+        return us.value, int(launches.value)
+
+    def device_trace_continue(self, device_ptr: int, count: int) -> tuple[float, int]:
+        """As device_trace_resident, but from the current state (no reset): positions
+        continue, so a warm-up of at least a window gives steady-state steps."""
+        us = ctypes.c_double(0)
+        launches = ctypes.c_uint64(0)
+        _check(library().st_device_trace_continue(self._h, ctypes.c_void_p(device_ptr), int(count),
                                                   ctypes.byref(us), ctypes.byref(launches)), self._h)
         return us.value, int(launches.value)
 

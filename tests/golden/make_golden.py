@@ -1,7 +1,7 @@
 """Generate the committed golden fixtures under tests/golden/ (run in the build container).
 
-Needs the read-only reference checkout (default /root/reference, or $ST_REFERENCE);
-never runs on the GPU box. Three families:
+Needs a read-only checkout of the reference, named by $ST_REFERENCE; never
+runs on the GPU box. Three families:
 
 ref-small-{fp32,mixed}
     The reference's own committed checkpoint, trace and reset schedule
@@ -36,7 +36,9 @@ import torch
 
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT))
-REFERENCE = Path(os.environ.get("ST_REFERENCE", "/root/reference"))
+if not os.environ.get("ST_REFERENCE"):
+    raise SystemExit("set ST_REFERENCE to a checkout of the reference repository")
+REFERENCE = Path(os.environ["ST_REFERENCE"])
 sys.path.insert(0, str(REFERENCE))
 
 from reference.model import Config, Streaming  # noqa: E402  (reference import, read only)
@@ -138,7 +140,9 @@ def ref_main(mode: str) -> None:
 
 
 def synthetic_golden(name: str, config_key: str, mode: str, count: int, seed: int = 42,
-                     trace_seed: int = 123, state_layers: list[int] | None = None) -> None:
+                     trace_seed: int = 123, state_layers: list[int] | None = None,
+                     resets: list[int] | None = None, hidden_events: list[int] | None = None) -> None:
+    """hidden_events None: every event's hidden vectors; resets None: one reset at W + 5."""
     config, _ = synthetic.CONFIGS[config_key]
     model = synthetic.make_model(config, mode, seed)
     events = synthetic.make_events(count, config.features, trace_seed)
@@ -146,16 +150,18 @@ def synthetic_golden(name: str, config_key: str, mode: str, count: int, seed: in
         weights = {n: torch.from_numpy(model.get(n)).bfloat16() for n in model.names()}
     else:
         weights = {n: torch.from_numpy(model.get(n)) for n in model.names()}
-    resets = [config.window + 5] if count > config.window + 5 else []
+    if resets is None:
+        resets = [config.window + 5] if count > config.window + 5 else []
     state_events = [count - 1]
     scores, hidden, keys, values = run_reference(config.to_json(), weights, events, resets, mode,
-                                                 state_events)
+                                                 state_events, hidden_events)
     state_layers = state_layers or list(range(config.layers))
     keys, values = keys[:, state_layers], values[:, state_layers]
     write(OUT / name, dict(source="reference/model.py Streaming on synthetic weights",
                            config=config.to_json(), mode=mode, seed=seed, trace_seed=trace_seed,
                            events=count, resets=resets, state_events=state_events,
-                           state_layers=state_layers, hidden_events="all"),
+                           state_layers=state_layers,
+                           hidden_events="all" if hidden_events is None else hidden_events),
           scores=scores, hidden=hidden, keys=keys, values=values, state_events=np.array(state_events))
 
 
@@ -171,7 +177,13 @@ def main() -> None:
         synthetic_golden("c1-small-fp32", "c1-small-fp32", "fp32", 80)
         synthetic_golden("c1-small-bf16", "c1-small-fp32", "bf16", 80)
     if "c2" in families:
-        synthetic_golden("c2-main-fp32", "c2-main-fp32", "fp32", 24, state_layers=[0, 7])
+        # the reference's fixture pattern (scripts/validate.py:40-52): 3W + 9
+        # events with a reset before event 2W + 3, so the ring wraps twice
+        w = synthetic.CONFIGS["c2-main-fp32"][0].window
+        count = 3 * w + 9
+        hidden_events = sorted({0, 1, w - 1, w, w + 1, 2 * w + 2, 2 * w + 3, 2 * w + 4, count - 1})
+        synthetic_golden("c2-main-fp32", "c2-main-fp32", "fp32", count, state_layers=[0, 7],
+                         resets=[2 * w + 3], hidden_events=hidden_events)
 
 
 if __name__ == "__main__":

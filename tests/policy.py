@@ -13,6 +13,30 @@ docs/NumericalPolicy.md:5-20):
   RMS(err) / max(1, RMS(ref)) <= 0.002.
 NaN/Inf always fails.
 
+fp32 is held to a second, tighter bound on top of the reference policy: the
+benchmark definition asks for fp32 outputs and cache states "within 1e-5
+relative" of the reference CPU path. That is read as the relative error of
+each compared tensor, ||a - r||_2 / ||r||_2 <= 1e-5 per layer of every state
+tensor (keys, values, hidden) and over the compared score sequence; the
+reference policy's elementwise bound (above) still applies to every
+coordinate. ``check_state`` and ``check_scores`` apply both to every fp32
+comparison. A per-coordinate 1e-5 is not a bound two correct fp32
+implementations meet: at the Large shape (d1024, 12 layers, from one random
+state, 3 steps) the reference's own reference/model.py and this repo's CPU
+restatement of its Cpu.cpp differ by up to 9.98e-6 of a key row's RMS, while
+their relative L2 difference stays at 1.4e-7 (keys) to 2.5e-6 (layer-11
+hidden) -- sums of 1024-4096 products taken in different orders
+(tests/golden/measure_depth_noise.py prints these figures).
+
+Depth: the reference tuned its relative-L2 gate on models of at most 4
+layers. Rounding-midpoint flips accumulate with depth, so past layer 3 the
+gate grows linearly with the layer index, gate * (l + 1) / 4, as the
+coordinate bound already does with (l + 1). Measured at the Large bf16 shape
+(12 layers, the same run as above): reference/model.py with a bf16 cast and
+this repo's oracle differ by 0.0005, 0.0032, 0.0055, 0.0073 ... 0.0162
+relative L2 at layers 0, 1, 2, 3 ... 11 -- two CPU references already past
+the flat 0.016 gate at layer 11, and about a third of the scaled 0.048.
+
 bf16 variant (declared, not a silent retune): the reference tuned its two
 absolute terms -- the 0.002 coordinate atol and the 0.002 relative-L2 gate -- to
 fp16's unit roundoff. bf16 keeps 7 mantissa bits instead of 10, so its unit
@@ -34,6 +58,7 @@ import numpy as np
 
 
 L2_GATE = {"mixed": 0.002, "bf16": 0.016}
+FP32_RELATIVE = 1e-5
 ATOL = {"mixed": 0.002, "bf16": 0.016}
 
 
@@ -41,8 +66,11 @@ def is_mixed(mode) -> bool:
     return mode not in (False, "fp32")
 
 
-def l2_gate(mode) -> float:
-    return L2_GATE["bf16"] if mode == "bf16" else L2_GATE["mixed"]
+def l2_gate(mode, layer: int = 0) -> float:
+    """Relative-L2 gate of a mixed-precision state tensor in zero-based layer
+    ``layer``: the reference's gate through layer 3, then scaled by (l + 1) / 4."""
+    base = L2_GATE["bf16"] if mode == "bf16" else L2_GATE["mixed"]
+    return base * max(1.0, (layer + 1) / 4.0)
 
 
 def mixed_atol(mode) -> float:
@@ -52,7 +80,7 @@ def mixed_atol(mode) -> float:
 def state_errors(actual, reference, layer, mixed=True):
     """reference/numerical.py:13-26. The last axis is the state vector.
     ``mixed`` is True/False or a mode name ("fp32", "mixed", "bf16")."""
-    gate = l2_gate(mixed)
+    gate = l2_gate(mixed, layer)
     matol = mixed_atol(mixed)
     mixed = is_mixed(mixed)
     actual = np.asarray(actual, dtype=np.float64)
@@ -92,17 +120,40 @@ def score_errors(actual, reference, layers, mixed=True):
                 normalized_rmse=normalized, passed=failed == 0 and (not mixed or normalized <= gate))
 
 
+def fp32_relative_errors(actual, reference):
+    """The fp32 "1e-5 relative" bound on one tensor: ||a - r|| / ||r|| <= 1e-5
+    (a zero reference needs an exactly zero result)."""
+    actual = np.asarray(actual, dtype=np.float64)
+    reference = np.asarray(reference, dtype=np.float64)
+    if actual.shape != reference.shape:
+        raise ValueError("State tensor shapes differ")
+    if not (np.all(np.isfinite(actual)) and np.all(np.isfinite(reference))):
+        return dict(relative_l2=float("inf"), passed=False)
+    norm = float(np.linalg.norm(reference.ravel()))
+    err = float(np.linalg.norm((actual - reference).ravel()))
+    rel = err / norm if norm > 0 else (0.0 if err == 0 else float("inf"))
+    return dict(relative_l2=rel, passed=rel <= FP32_RELATIVE)
+
+
 def check_state(actual, reference, mixed, what=""):
-    """Apply state_errors per layer; ``actual``/``reference`` have the layer on axis 0."""
+    """Apply state_errors per layer; ``actual``/``reference`` have the layer on axis 0.
+    fp32 must also pass the 1e-5 relative bound per state vector."""
     actual = np.asarray(actual)
     reference = np.asarray(reference)
     assert actual.shape == reference.shape, (what, actual.shape, reference.shape)
     for layer in range(reference.shape[0]):
         result = state_errors(actual[layer], reference[layer], layer, mixed)
         assert result["passed"], (what, layer, result)
+        if not is_mixed(mixed):
+            rel = fp32_relative_errors(actual[layer], reference[layer])
+            assert rel["passed"], (what, layer, "fp32 1e-5 relative", rel)
 
 
 def check_scores(actual, reference, layers, mixed, what=""):
     result = score_errors(actual, reference, layers, mixed)
     assert result["passed"], (what, result)
+    if not is_mixed(mixed):
+        rel = fp32_relative_errors(actual, reference)
+        assert rel["passed"], (what, "fp32 1e-5 relative", rel)
+        result = dict(result, relative_l2=rel["relative_l2"])
     return result
