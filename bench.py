@@ -135,15 +135,17 @@ def kernel_name(info):
     """The device-loop kernel the runtime runs for the timed trace."""
     if info.get("batched"):
         return "k3_rounds"
-    return "k4_flow" if info.get("flow") else "k2_trace"
+    if info.get("flow"):
+        return info.get("resource_kernel", "k4_flow")
+    return "k2_trace"
 
 
 def kernel_label(info, mode, streams):
     name = kernel_name(info)
     if name == "k3_rounds":
         return f"k3_rounds ({mode}, batched round of {streams} streams)"
-    if name == "k4_flow":
-        return (f"k4_flow ({mode}, {info.get('clusters')} clusters of {info.get('cluster')} CTAs, "
+    if name in ("k4_flow", "k5_chain"):
+        return (f"{name} ({mode}, {info.get('clusters')} clusters of {info.get('cluster')} CTAs, "
                 "tagged-record exchanges, producer-warp weight ring)")
     return f"k2_trace ({mode}, {'weight ring' if info.get('weight_ring') else 'direct loads'})"
 

@@ -207,8 +207,11 @@ int st_device_trace_continue(st_runtime* rt, const float* device_inputs, size_t 
  * before any stream capture. Every call shares the one array and overwrites
  * the previous call's partials, so calls that may overlap on the GPU (other
  * streams, other host threads) race and must be serialized by the caller.
- * Sizes needing more than the array holds are rejected with ST_ERR_INVALID;
- * the message is in st_attention_static_error(). */
+ * Dimensions beyond heads * head_dim <= 1024 or a window above 4096 are
+ * rejected with ST_ERR_INVALID (every admitted shape fits the array; the
+ * library checks that at compile time); the message is in
+ * st_attention_static_error(). A CUDA error already pending on the calling
+ * thread is reported as ST_ERR_CUDA and left pending. */
 #define ST_ATTENTION_STATIC_MAX_FLOATS 262144
 int st_attention_static(int device, int mode, int heads, int head_dim, int window, uint64_t position,
                         const float* q, const void* keys, const void* values, float* out, void* stream);

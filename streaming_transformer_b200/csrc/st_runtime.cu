@@ -159,6 +159,10 @@ struct st_runtime {
   // cluster shape; ST_FLOW=0 selects the generic kernels.
   bool flow = false;
   const void* flow_fn = nullptr;
+  // The single-stream kernel: k5_chain (compact code, st_chain.cuh) unless
+  // ST_CHAIN=0 selects k4_flow (st_flow.cuh); flow_diag_fn records timelines.
+  bool chain = false;
+  const void* flow_diag_fn = nullptr;
   int fcluster = 0, fnclusters = 0, fgrid = 0;
   int bgrid = 0;
   int bsplit[4] = {1, 1, 1, 1};
@@ -343,7 +347,8 @@ StepArgs flow_args(const st_runtime* rt, const StepArgs& a0) {
 }
 
 int launch_flow(st_runtime* rt, const StepArgs& a0, const FlowLaunch& f) {
-  const cudaError_t e = flow_launch(rt->flow_fn, rt->fgrid, rt->fcluster, rt->stream, flow_args(rt, a0), f);
+  const void* fn = a0.timeline ? rt->flow_diag_fn : rt->flow_fn;
+  const cudaError_t e = flow_launch(fn, rt->fgrid, rt->fcluster, rt->stream, flow_args(rt, a0), f);
   rt->launches += 1;
   return rt->cuda(e, "flow cluster launch");
 }
@@ -409,7 +414,7 @@ int preload(st_runtime* rt) {
   const void* fns[] = {ST_KERNEL(rt, input), ST_KERNEL(rt, attention), ST_KERNEL(rt, ffn), ST_KERNEL(rt, final_),
                        ST_KERNEL(rt, reset), ST_LOOP_KERNEL(rt, fused), ST_LOOP_KERNEL(rt, trace), ST_LOOP_KERNEL(rt, persistent),
                        ST_TIMELINE_KERNEL(rt), ST_KERNEL(rt, convert), rounds_fn(rt),
-                       rt->flow ? rt->flow_fn : ST_KERNEL(rt, input)};
+                       rt->flow ? rt->flow_fn : ST_KERNEL(rt, input), rt->flow ? rt->flow_diag_fn : ST_KERNEL(rt, input)};
   for (const void* f : fns) {
     cudaFuncAttributes fa{};
     ST_CUDA(rt, cudaFuncGetAttributes(&fa, f));
@@ -870,11 +875,16 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   {
     const char* env = std::getenv("ST_FLOW");
     const int mode_index = m.mode == ST_MODE_FP16 ? 1 : m.mode == ST_MODE_BF16 ? 2 : 0;
-    rt->flow_fn = flow_kernel(mode_index, d);
+    const char* kenv = std::getenv("ST_CHAIN");
+    rt->chain = !(kenv && kenv[0] == '0');
+    rt->flow_fn = rt->chain ? chain_kernel(mode_index, d, false) : flow_kernel(mode_index, d);
+    rt->flow_diag_fn = rt->chain ? chain_kernel(mode_index, d, true) : rt->flow_fn;
     const bool want = rt->flow_fn && S == 1 && hd == kFlowHd && m.features == kFlowFeatures && o.blocks == 0 &&
                       !rt->batched && coop && !(env && env[0] == '0');
     if (want) {
       if (rt->cuda(cudaFuncSetAttribute(rt->flow_fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)flow_smem_bytes()), "cudaFuncSetAttribute flow") != ST_OK ||
+          rt->cuda(cudaFuncSetAttribute(rt->flow_diag_fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)flow_smem_bytes()), "cudaFuncSetAttribute flow") != ST_OK)
         return bail(ST_ERR_CUDA);
       int best_cs = 0, best_nc = 0;
@@ -1442,7 +1452,7 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
   const bool flow_loop = rt->flow && (rt->opt.backend == ST_BACKEND_FUSED || rt->opt.backend == ST_BACKEND_PERSISTENT);
   if (flow_loop) {
     kernel = rt->flow_fn;
-    name = "k4_flow";
+    name = rt->chain ? "k5_chain" : "k4_flow";
   }
   cudaFuncGetAttributes(&fa, kernel);
   static const char* backends[] = {"cuda", "graph", "cublas", "cublas-graph", "fused", "persistent"};

@@ -25,6 +25,14 @@ namespace {
 // that loads this library holds this array until the process exits.
 static __device__ __align__(256) float g_attention_scratch[ST_ATTENTION_STATIC_MAX_FLOATS];
 
+// Dimension limits of the entry point, and proof that every shape they admit
+// fits the array: heads * head_dim <= 1024 with head_dim >= 2 gives at most
+// 512 heads of (2 + 2) floats per chunk, and a window of 4096 slots 128 chunks.
+constexpr int kStaticMaxWidth = 1024, kStaticMaxWindow = 4096;
+static_assert((long long)(kStaticMaxWidth / 2) * ((kStaticMaxWindow + kAttChunk - 1) / kAttChunk) * (2 + 2) <=
+                  ST_ATTENTION_STATIC_MAX_FLOATS,
+              "the largest admitted attention shape must fit the static scratch array");
+
 constexpr int kMaxDevices = 64;
 std::mutex g_mutex;
 float* g_scratch_address[kMaxDevices] = {};
@@ -87,11 +95,18 @@ __global__ void __launch_bounds__(kThreads) k_merge_static(StepArgs a, int valid
 
 template <typename T>
 int launch(const StepArgs& a, int valid, float* out, cudaStream_t stream) {
+  // An error left by an earlier launch on this thread belongs to its caller:
+  // report it without clearing it rather than take it for this call's own.
+  cudaError_t e = cudaPeekAtLastError();
+  if (e != cudaSuccess)
+    return fail(ST_ERR_CUDA, std::string("an earlier CUDA error is pending: ") + cudaGetErrorString(e));
   const int items = a.heads * a.nchunks_max;
   k_attention_static<T><<<(items + kWarps - 1) / kWarps, kThreads, 0, stream>>>(a, valid);
+  if ((e = cudaGetLastError()) != cudaSuccess)
+    return fail(ST_ERR_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
   k_merge_static<T><<<(a.width + kThreads - 1) / kThreads, kThreads, 0, stream>>>(a, valid, out);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(ST_ERR_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
+  if ((e = cudaGetLastError()) != cudaSuccess)
+    return fail(ST_ERR_CUDA, std::string("attention merge launch: ") + cudaGetErrorString(e));
   return ST_OK;
 }
 
@@ -104,10 +119,13 @@ int st_attention_static(int device, int mode, int heads, int head_dim, int windo
   if (!q || !keys || !values || !out) return fail(ST_ERR_INVALID, "null pointer");
   if (device < 0 || device >= kMaxDevices) return fail(ST_ERR_INVALID, "device ordinal out of range");
   if (mode < ST_MODE_FP32 || mode > ST_MODE_BF16) return fail(ST_ERR_INVALID, "unknown storage mode");
-  if (heads < 1 || head_dim < 2 || head_dim % 2 || (long long)heads * head_dim > 1024 || window < 1 || window > 4096)
+  if (heads < 1 || head_dim < 2 || head_dim % 2 || (long long)heads * head_dim > kStaticMaxWidth || window < 1 ||
+      window > kStaticMaxWindow)
     return fail(ST_ERR_INVALID, "Invalid or unsupported attention dimensions");
   const int nchunks = (window + kAttChunk - 1) / kAttChunk;
   const long long need = (long long)heads * nchunks * (head_dim + 2);
+  // A guard only: the static_assert above shows the dimension limits keep
+  // every admitted shape within the array.
   if (need > ST_ATTENTION_STATIC_MAX_FLOATS)
     return fail(ST_ERR_INVALID, "attention partials need " + std::to_string(need) +
                                     " floats, above the static scratch of " +
@@ -132,7 +150,9 @@ int st_attention_static(int device, int mode, int heads, int head_dim, int windo
     a.keys = const_cast<void*>(keys);
     a.values = const_cast<void*>(values);
     a.part = scratch;
-    const int valid = position + 1 < (uint64_t)window ? (int)(position + 1) : window;
+    // retained slots: position + 1 until the ring is full (no overflow at the
+    // largest position)
+    const int valid = position >= (uint64_t)window - 1 ? window : (int)(position + 1);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (mode == ST_MODE_FP16) st = launch<__half>(a, valid, out, s);
     else if (mode == ST_MODE_BF16) st = launch<__nv_bfloat16>(a, valid, out, s);
