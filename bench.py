@@ -144,7 +144,7 @@ def kernel_label(info, mode, streams):
     name = kernel_name(info)
     if name == "k3_rounds":
         return f"k3_rounds ({mode}, batched round of {streams} streams)"
-    if name in ("k4_flow", "k5_chain"):
+    if name == "k4_flow":
         return (f"{name} ({mode}, {info.get('clusters')} clusters of {info.get('cluster')} CTAs, "
                 "tagged-record exchanges, producer-warp weight ring)")
     return f"k2_trace ({mode}, {'weight ring' if info.get('weight_ring') else 'direct loads'})"

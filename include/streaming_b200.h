@@ -166,7 +166,10 @@ int st_device_timeline(st_runtime* rt, const float* inputs, size_t count, long l
 /* Same, recorded by CTA `cta` of the grid (0 <= cta < blocks in st_info, or
  * < batched_grid when st_info reports "batched": then thread 0 of that CTA
  * records the end of every phase of the batched round, tags 40-48, and every
- * grid-barrier exit, tag 49, in warp 0's row). */
+ * grid-barrier exit, tag 49, in warp 0's row). For the single-stream step
+ * kernel ("flow" in st_info) pass cta = -1 and capacity >= flow_grid * 32:
+ * marks[c * 32 + tag] receives CTA c's clock64() cycles spent in the phase
+ * ending at each tag, summed over the steps, and marks[c * 32] the steps. */
 int st_device_timeline_cta(st_runtime* rt, const float* inputs, size_t count, int cta, long long* marks,
                            size_t capacity, size_t* used);
 

@@ -85,6 +85,9 @@ struct StepArgs {
   int timeline_capacity;
   int timeline_cta;                   // the CTA that records the timeline
   int l2_keep_layers;                 // layers whose weights are kept L2-resident (weight ring)
+  int test_drop_cta;                  // failure-path test only (-1 off): this CTA of the single-stream
+                                      // kernel withholds its layer-0 out-projection records, so every
+                                      // exchange-1 wait runs out its bound
   int cluster_size;                   // CTAs per cluster the buffers were sized for
   int clusters;                       // clusters in the grid (sizes dpart)
   // single-stream flow kernel (st_flow.cuh)

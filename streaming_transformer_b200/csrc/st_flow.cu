@@ -10,21 +10,25 @@
 namespace st {
 
 namespace {
-template <typename T>
+template <typename T, bool kDiag>
 const void* by_width(int width) {
   switch (width) {
-    case 256: return (const void*)k4_flow<T, 256>;
-    case 512: return (const void*)k4_flow<T, 512>;
-    case 1024: return (const void*)k4_flow<T, 1024>;
+    case 256: return (const void*)k4_flow<T, 256, kDiag>;
+    case 512: return (const void*)k4_flow<T, 512, kDiag>;
+    case 1024: return (const void*)k4_flow<T, 1024, kDiag>;
     default: return nullptr;
   }
 }
+template <bool kDiag>
+const void* by_mode(int mode, int width) {
+  if (mode == 1) return by_width<__half, kDiag>(width);
+  if (mode == 2) return by_width<__nv_bfloat16, kDiag>(width);
+  return by_width<float, kDiag>(width);
+}
 }  // namespace
 
-const void* flow_kernel(int mode, int width) {
-  if (mode == 1) return by_width<__half>(width);
-  if (mode == 2) return by_width<__nv_bfloat16>(width);
-  return by_width<float>(width);
+const void* flow_kernel(int mode, int width, bool diag) {
+  return diag ? by_mode<true>(mode, width) : by_mode<false>(mode, width);
 }
 
 size_t flow_smem_bytes() { return kFlowSmemBytes; }

@@ -160,6 +160,13 @@ __device__ inline FlowSpan flow_span(const StepArgs& a, const Where& w, int kind
 }
 
 // ---------------------------------------------------------------- shared memory
+enum FlowMark : int {
+  kFmStep = 1, kFmIn, kFmNorm1, kFmQkv, kFmQkvSync, kFmAttn, kFmPartSync, kFmMerge, kFmOut, kFmGather1,
+  kFmPub2, kFmNorm2, kFmGateUp, kFmDown, kFmDredSync, kFmDpub, kFmGather2, kFmPub1, kFmScore,
+  kFmAcqWait = 24  // not a phase: cycles spent waiting for ring chunks, inside the phases above
+};
+constexpr int kFlowTags = 32;
+
 struct FlowChunk {
   const char* src;
   unsigned bytes;
@@ -177,7 +184,8 @@ struct alignas(128) FlowRing {
   unsigned capacity, head_off;
   int next, nchunks, failed, ok;
   int stop;                              // the compute warps have left; the producer stops issuing
-  int tl_n;                              // timeline marks written (diagnostics)
+  long long tlast;                       // diagnostics: clock64() of the previous phase mark
+  unsigned long long tsum[kFlowTags];    // diagnostics: cycles per phase tag, tsum[0] = steps
   FlowChunk table[kFlowMaxChunks];
 };
 
@@ -220,41 +228,29 @@ struct alignas(128) FlowSmem {
 };
 
 // ---------------------------------------------------------------- timeline
-// Phase marks of thread 0 of CTA a.timeline_cta, (clock64() << 8) | tag, when
-// a timeline buffer is given (diagnostics; one predictable branch otherwise).
-// With a.timeline_cta < 0 every CTA records pairs {tag, globaltimer ns} into
-// its own region of a.timeline_capacity / gridDim.x entries, for cross-CTA
-// comparisons.
-enum FlowMark : int {
-  kFmStep = 1, kFmIn, kFmNorm1, kFmQkv, kFmQkvSync, kFmAttn, kFmPartSync, kFmMerge, kFmOut, kFmGather1,
-  kFmPub2, kFmNorm2, kFmGateUp, kFmDown, kFmDredSync, kFmDpub, kFmGather2, kFmPub1, kFmScore, kFmAcqStart,
-  kFmAcqEnd, kFmBarIn, kFmBarOut
-};
-// The step's code is long and runs once per layer, so everything that is off
-// the hot path (diagnostics, error reporting, slow waits) lives in functions
-// of its own, called with scalars (a call that took the kernel parameters by
-// reference would copy them to local memory); the hot path stays small enough
-// to keep its instructions cached.
-static __device__ __noinline__ void fmark_slow(long long* tl, int capacity, int cta, int* n, int tag) {
-  if ((int)blockIdx.x == cta) {
-    const int i = *n;
-    if (i < capacity / kWarps) {
-      tl[i] = (long long)((clock64() << 8) | (long long)tag);
-      *n = i + 1;
-    }
-  } else if (cta < 0) {
-    const int per = capacity / (int)gridDim.x;
-    const int i = *n;
-    if (2 * i + 1 < per) {
-      long long* r = tl + (size_t)blockIdx.x * per;
-      r[2 * i] = tag;
-      r[2 * i + 1] = (long long)globaltimer();
-      *n = i + 1;
+// Phase marks of the diagnostic instantiations (kDiag) only: thread 0 of every
+// CTA adds the clock64() cycles since its previous mark to fr.tsum[tag], in
+// shared memory (tens of cycles per mark), and at the end of every step stores
+// the running sums to a.timeline[cta * kFlowTags + tag] (tsum[0] counts the
+// steps). The production instantiations contain none of this code.
+
+// Everything off the hot path (error reporting, slow waits) lives in
+// functions of its own, called with scalars (a call that took the kernel
+// parameters by reference would copy them to local memory).
+
+template <bool kDiag>
+__device__ __forceinline__ void fmark(const StepArgs& a, FlowRing& fr, int tag) {
+  if constexpr (kDiag) {
+    if (threadIdx.x == 0) {
+      const long long now = clock64();
+      fr.tsum[tag] += (unsigned long long)(now - fr.tlast);
+      fr.tlast = now;
+      if (tag == kFmScore && a.timeline) {
+        fr.tsum[0] += 1;
+        for (int i = 0; i < kFlowTags; ++i) a.timeline[blockIdx.x * kFlowTags + i] = (long long)fr.tsum[i];
+      }
     }
   }
-}
-__device__ __forceinline__ void fmark(const StepArgs& a, FlowRing& fr, int tag) {
-  if (a.timeline != nullptr && threadIdx.x == 0) fmark_slow(a.timeline, a.timeline_capacity, a.timeline_cta, &fr.tl_n, tag);
 }
 
 // First error wins; mirrored to the host (set_error with scalars).
@@ -429,17 +425,24 @@ static __device__ __noinline__ bool flow_wait_slow(FlowRing& fr, int slot, unsig
 // Wait (bounded) for the next chunk; returns its bytes. After a failed wait
 // the ring is marked failed and every later acquire returns the start of the
 // buffer without waiting (the error word ends the launch at its next exchange).
-__device__ __forceinline__ const unsigned char* flow_acquire(const StepArgs& a, FlowRing& fr, const FlowCur& cur) {
+__device__ __forceinline__ const unsigned char* flow_acquire_plain(const StepArgs& a, FlowRing& fr, const FlowCur& cur) {
   const int slot = (int)(cur.consumed % kFlowSlots);
   const unsigned parity = (unsigned)((cur.consumed / kFlowSlots) & 1ull);
-  fmark(a, fr, kFmAcqStart);
   if (!mbar_try_wait(&fr.full[slot], parity) && !*reinterpret_cast<volatile int*>(&fr.failed) &&
       !flow_wait_slow(fr, slot, parity, a.bar_timeout_ns)) {
     fr.failed = 1;
     flow_error(a.error, a.host_error, kBarrierTimeout);
   }
-  fmark(a, fr, kFmAcqEnd);
   return fr.buf + (*reinterpret_cast<volatile int*>(&fr.failed) ? 0u : fr.off[slot]);
+}
+template <bool kDiag = false>
+__device__ __forceinline__ const unsigned char* flow_acquire(const StepArgs& a, FlowRing& fr, const FlowCur& cur) {
+  long long t0 = 0;
+  if constexpr (kDiag) t0 = clock64();
+  const unsigned char* p = flow_acquire_plain(a, fr, cur);
+  if constexpr (kDiag)
+    if (threadIdx.x == 0) fr.tsum[kFmAcqWait] += (unsigned long long)(clock64() - t0);
+  return p;
 }
 
 // Every thread of a compute warp, after the warp's last read of the chunk (or
@@ -567,7 +570,7 @@ __device__ __forceinline__ void flow_dot(const T* row, int sl, const FlowX<T, K>
 // 0 of each valid group (row relative to the span). Passes of RPP groups are
 // dealt to warps round robin across the span's chunks; a warp without a pass
 // in a chunk releases it without waiting.
-template <typename T, int K, int U, class Epi>
+template <typename T, int K, int U, bool kDiag, class Epi>
 __device__ __forceinline__ void flow_rows(const StepArgs& a, FlowRing& fr, FlowCur& cur, const FlowSpan sp,
                                           const FlowX<T, K>& x, Epi&& epi) {
   using R = FlowRow<T, K>;
@@ -581,7 +584,7 @@ __device__ __forceinline__ void flow_rows(const StepArgs& a, FlowRing& fr, FlowC
     const int passes = (n + pr - 1) / pr;
     const int first = (warp - pass0 % kWarps + kWarps) % kWarps;
     if (first < passes) {
-      const T* base = (const T*)flow_acquire(a, fr, cur);
+      const T* base = (const T*)flow_acquire<kDiag>(a, fr, cur);
       for (int p = first; p < passes; p += kWarps) {
         const int row = p * pr + sub * U;
         const bool valid = row < n;
@@ -617,9 +620,9 @@ __device__ __forceinline__ void flow_rows(const StepArgs& a, FlowRing& fr, FlowC
 }
 
 // A one-row span (a norm gain) read by every thread: g(i) for i < D.
-template <typename T, class Fn>
+template <typename T, bool kDiag, class Fn>
 __device__ __forceinline__ void flow_gain(const StepArgs& a, FlowRing& fr, FlowCur& cur, Fn&& fn) {
-  const T* g = (const T*)flow_acquire(a, fr, cur);
+  const T* g = (const T*)flow_acquire<kDiag>(a, fr, cur);
   fn(g);
   flow_release(fr, cur);
 }
@@ -784,9 +787,7 @@ __device__ __forceinline__ bool flow_receive_at(unsigned long long* bar, unsigne
 template <class Sm>
 __device__ __forceinline__ bool flow_receive(const StepArgs& a, FlowRing& fr, Sm& sm, int site, unsigned k,
                                              unsigned bytes) {
-  fmark(a, fr, kFmBarIn);
   const bool ok = flow_receive_at(&sm.sbar[site][k & 1u], k, bytes, a.error, a.host_error, a.bar_timeout_ns);
-  fmark(a, fr, kFmBarOut);
   return ok;
 }
 
@@ -821,10 +822,8 @@ template <class Sm>
 __device__ __forceinline__ bool flow_publish(const StepArgs& a, FlowRing& fr, Sm& sm, FlowCtx& cx, bool ok) {
   const unsigned k = cx.k[kSiteX]++;
   const unsigned b = k & 1u;
-  fmark(a, fr, kFmBarIn);
   const bool all = flow_publish_impl(sm.seg, sm.x[b], &sm.ssx[b][0][0], sm.okx[b], &sm.sbar[kSiteX][b], k, cx.rank,
                                      cx.cs, cx.seg0, cx.n, ok, a.error, a.host_error, a.bar_timeout_ns);
-  fmark(a, fr, kFmBarOut);
   cx.bx = b;
   return all;
 }
@@ -835,7 +834,7 @@ __device__ __forceinline__ float flow_norm_scale(const float (*ss)[8], unsigned 
   float t = 0.f;
   for (unsigned r = 0; r < cs; ++r)
     for (int w = 0; w < nw; ++w) t += ss[r][w];
-  return 1.0f / sqrtf(t / (float)d + eps);
+  return rsqrtf(t * (1.0f / (float)d) + eps);
 }
 
 // ---------------------------------------------------------------- attention
@@ -843,7 +842,7 @@ __device__ __forceinline__ float flow_norm_scale(const float (*ss)[8], unsigned 
 // the out-projection rows of this rank's segment, published as P[h].
 // Returns false when a wait ran out (the error word is set; the next
 // exchange's verdict ends the launch).
-template <typename T, int D>
+template <typename T, int D, bool kDiag>
 __device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSmem& sm,
                                           FlowCtx& cx, int l, int h, unsigned long long t, unsigned tag,
                                           bool first_head) {
@@ -874,11 +873,11 @@ __device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowC
   if (first_head) {
     const float scale = flow_norm_scale(sm.ssx[cx.bx], cx.cs, cx.n, D, a.epsilon);
     const float* x = sm.x[cx.bx];
-    flow_gain<T>(a, fr, cur, [&](const T* g) {
+    flow_gain<T, kDiag>(a, fr, cur, [&](const T* g) {
       for (int i = threadIdx.x; i < D; i += kThreads) sm.z[i] = Storage<T>::round(x[i] * scale * Storage<T>::load(g, i));
     });
     flow_bsync(fr);
-    fmark(a, fr, kFmNorm1);
+    fmark<kDiag>(a, fr, kFmNorm1);
   }
   // q, k, v row pairs of this rank, sent into every rank's q/k/v buffer
   const unsigned kq = cx.k[kSiteQkv]++, bq = kq & 1u;
@@ -888,7 +887,7 @@ __device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowC
     const int lo = sm.plan.qkv_lo;
     FlowX<T, D> xr;
     xr.load(sm.z);
-    flow_rows<T, D, 2>(a, fr, cur, sm.plan.qkv, xr,
+    flow_rows<T, D, 2, kDiag>(a, fr, cur, sm.plan.qkv, xr,
                        [&](int r, const float (&v)[2]) {
                          const int row = 2 * lo + r;
                          const int which = row / hd, dim = row - which * hd;
@@ -910,19 +909,19 @@ __device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowC
                          }
                        });
   }
-  fmark(a, fr, kFmQkv);
+  fmark<kDiag>(a, fr, kFmQkv);
   // this CTA's K/V copies, then every rank's q/k/v rows
   if (kv_smem) cp_async_wait_all();
   flow_bar();
   bool ok = flow_receive(a, fr, sm, kSiteQkv, kq, 3u * hd * 4u);
-  fmark(a, fr, kFmQkvSync);
+  fmark<kDiag>(a, fr, kFmQkvSync);
   // attention over this CTA's slots: an online softmax per warp
   {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const T* Ks = reinterpret_cast<const T*>(sm.u.kv);
     const T* Vs = Ks + (size_t)nj * hd;
     const float2 q = *reinterpret_cast<const float2*>(&qkv[2 * lane]);
-    const float root = sqrtf((float)hd);
+    const float rroot = 1.0f / 8.0f;  // 1 / sqrt(head_dim 64), exact
     float m = -INFINITY, lsum = 0.f, acc0 = 0.f, acc1 = 0.f;
     for (int j = j0 + warp; j < j1; j += kWarps) {
       float k0, k1, v0, v1;
@@ -942,7 +941,7 @@ __device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowC
         v0 = Storage<T>::load_cg(values + (size_t)j * hd, 2 * lane);
         v1 = Storage<T>::load_cg(values + (size_t)j * hd, 2 * lane + 1);
       }
-      const float s = warp_sum(fmaf(q.y, k1, q.x * k0)) / root;
+      const float s = warp_sum(fmaf(q.y, k1, q.x * k0)) * rroot;
       const float mn = fmaxf(m, s);
       const float c = expf(m - mn);
       const float p = expf(s - mn);
@@ -959,7 +958,7 @@ __device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowC
     }
   }
   flow_bsync(fr);
-  fmark(a, fr, kFmAttn);
+  fmark<kDiag>(a, fr, kFmAttn);
   const unsigned ka = cx.k[kSiteAtt]++, ba = ka & 1u;
   float(*apart)[kFlowHd + 2] = sm.apart[ba];
   if (threadIdx.x < 64) {
@@ -978,7 +977,7 @@ __device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowC
     if (threadIdx.x < cx.cs) st_async2(&apart[cx.rank][0], abar, threadIdx.x, M, L);
   }
   ok = flow_receive(a, fr, sm, kSiteAtt, ka, cx.cs * (unsigned)(4 * hd + 8)) && ok;
-  fmark(a, fr, kFmPartSync);
+  fmark<kDiag>(a, fr, kFmPartSync);
   if (threadIdx.x < 64) {
     // merge the cluster's partials in rank order -> o (cast)
     const int lane = threadIdx.x & 31, dim = threadIdx.x;
@@ -989,30 +988,33 @@ __device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowC
     const float L = warp_sum(lr * sr);
     float A = 0.f;
     for (unsigned r = 0; r < cx.cs; ++r) A = fmaf(apart[r][2 + dim], __shfl_sync(0xffffffffu, sr, r), A);
-    sm.o[dim] = Storage<T>::round(A / L);
+    sm.o[dim] = Storage<T>::round(__fdividef(A, L));
   }
   flow_bsync(fr);
-  fmark(a, fr, kFmMerge);
+  fmark<kDiag>(a, fr, kFmMerge);
   // out-projection rows of this rank's segment, published as P[h]
   {
     FlowX<T, hd> xr;
     xr.load(sm.o);
     unsigned long long* P = a.ll_heads + ((size_t)(tag & 1u) * a.heads + h) * D + cx.seg0;
-    flow_rows<T, hd, 2>(a, fr, cur, sm.plan.out, xr,
-                        [&](int r, const float (&v)[2]) { ll_store2(P + r, v[0], v[1], tag); });
+    // (a failure-path test may withhold this CTA's first layer-0 records)
+    const bool drop = (int)blockIdx.x == a.test_drop_cta && l == 0 && cx.steps == 0;
+    flow_rows<T, hd, 2, kDiag>(a, fr, cur, sm.plan.out, xr, [&](int r, const float (&v)[2]) {
+      if (!drop) ll_store2(P + r, v[0], v[1], tag);
+    });
   }
-  fmark(a, fr, kFmOut);
+  fmark<kDiag>(a, fr, kFmOut);
   return ok;
 }
 
 // ---------------------------------------------------------------- one step
 // One event through every layer; the score CTA writes the score to score_dst
 // (and score_copy when given). Returns the cluster-uniform verdict.
-template <typename T, int D>
+template <typename T, int D, bool kDiag>
 __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSmem& sm, FlowCtx& cx,
                           const float* event, unsigned long long t, float* score_dst, float* score_copy) {
   const int n = cx.n, seg0 = cx.seg0;
-  fmark(a, fr, kFmStep);
+  fmark<kDiag>(a, fr, kFmStep);
   cx.slot = (int)(t % (unsigned long long)a.window);
   cx.valid = t + 1 < (unsigned long long)a.window ? (int)(t + 1) : a.window;
   if (threadIdx.x < kFlowFeatures) sm.ev[threadIdx.x] = __ldcv(event + threadIdx.x);
@@ -1025,18 +1027,18 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
   {
     FlowX<T, kFlowFeatures> xr;
     xr.load(sm.ev);
-    flow_rows<T, kFlowFeatures, 1>(a, fr, cur, sm.plan.in, xr,
+    flow_rows<T, kFlowFeatures, 1, kDiag>(a, fr, cur, sm.plan.in, xr,
                                    [&](int r, const float (&v)[1]) { sm.seg[r] = Storage<T>::round(v[0]); });
     flow_bsync(fr);
     if (!flow_publish(a, fr, sm, cx, !fr.failed)) return false;
-    fmark(a, fr, kFmIn);
+    fmark<kDiag>(a, fr, kFmIn);
   }
   for (int l = 0; l < a.layers; ++l) {
     const unsigned tag = (unsigned)(cx.epoch + cx.steps * (unsigned long long)a.layers + (unsigned long long)l + 1ull);
     bool hok = true;
     if (cx.heads_here)
       for (int h = (int)cx.id; h < a.heads; h += (int)cx.nc)
-        hok = flow_head<T, D>(a, fr, cur, sm, cx, l, h, t, tag, h == (int)cx.id) && hok;
+        hok = flow_head<T, D, kDiag>(a, fr, cur, sm, cx, l, h, t, tag, h == (int)cx.id) && hok;
     // exchange 1 (whole width, no cluster handoff): x' = cast(x + cast(sum_h P[h]))
     float ssq = 0.f;
     bool ok1;
@@ -1044,29 +1046,29 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
       const unsigned long long* P = a.ll_heads + (size_t)(tag & 1u) * a.heads * D;
       ok1 = flow_gather_full<T, D>(P, a.heads, tag, sm.x[cx.bx], sm.x2, sm.u.red, sm.warp_scratch, &ssq, a.error,
                                    a.host_error, a.bar_timeout_ns) && hok && !fr.failed;
-      fmark(a, fr, kFmGather1);
+      fmark<kDiag>(a, fr, kFmGather1);
     }
     // FFN: norm2, gate/up -> SwiGLU, down partial
     bool dok = true;
     {
-      const float scale = 1.0f / sqrtf(ssq / (float)D + a.epsilon);
+      const float scale = rsqrtf(ssq * (1.0f / (float)D) + a.epsilon);
       const float* x2 = sm.x2;
-      flow_gain<T>(a, fr, cur, [&](const T* g) {
+      flow_gain<T, kDiag>(a, fr, cur, [&](const T* g) {
         for (int i = threadIdx.x; i < D; i += kThreads)
           sm.z[i] = Storage<T>::round(x2[i] * scale * Storage<T>::load(g, i));
       });
       flow_bsync(fr);
-      fmark(a, fr, kFmNorm2);
+      fmark<kDiag>(a, fr, kFmNorm2);
       FlowX<T, D> xr;
       xr.load(sm.z);
-      flow_rows<T, D, 2>(a, fr, cur, sm.plan.gateup, xr,
+      flow_rows<T, D, 2, kDiag>(a, fr, cur, sm.plan.gateup, xr,
                          [&](int r, const float (&v)[2]) {
                            const float gt = Storage<T>::round(v[0]);
                            const float up = Storage<T>::round(v[1]);
-                           sm.act[r >> 1] = Storage<T>::round((gt / (1.0f + expf(-gt))) * up);
+                           sm.act[r >> 1] = Storage<T>::round(__fdividef(gt, 1.0f + expf(-gt)) * up);
                          });
       flow_bsync(fr);
-      fmark(a, fr, kFmGateUp);
+      fmark<kDiag>(a, fr, kFmGateUp);
       // partial[col] = sum_f act[f] W_down^T[f][col]: thread t owns 16-byte
       // column vector t % NVd and rows f = g, g + G2, ... of the slice.
       using R = FlowRow<T, D>;
@@ -1079,7 +1081,7 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
       for (int c = 0; c < sp.chunks; ++c) {
         const int r0 = c * sp.rpc;
         const int rows = min(sp.rpc, sp.rows - r0);
-        const T* base = (const T*)flow_acquire(a, fr, cur);
+        const T* base = (const T*)flow_acquire<kDiag>(a, fr, cur);
         int f = ((g - r0) % G2 + G2) % G2;
         for (; f < rows; f += G2) {
           const float av = sm.act[r0 + f];
@@ -1090,7 +1092,7 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
         }
         flow_release(fr, cur);
       }
-      fmark(a, fr, kFmDown);
+      fmark<kDiag>(a, fr, kFmDown);
       // sm.u.red was last read by exchange 1, before its publish.
 #pragma unroll
       for (int k = 0; k < V; k += 4)
@@ -1110,7 +1112,7 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
         st_async4(&dred[cx.rank * n + (col - owner * n)], dbar, (unsigned)owner, s);
       }
       dok = flow_receive(a, fr, sm, kSiteDred, kd, cx.cs * (unsigned)n * 4u);
-      fmark(a, fr, kFmDredSync);
+      fmark<kDiag>(a, fr, kFmDredSync);
       // this rank's segment of the cluster partial, ranks added in order
       unsigned long long* Dp = a.ll_clusters + ((size_t)(tag & 1u) * cx.nc + cx.id) * D + seg0;
       if ((int)threadIdx.x < (n >> 1)) {
@@ -1122,13 +1124,13 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
         }
         ll_store2(Dp + i, s0, s1, tag);
       }
-      fmark(a, fr, kFmDpub);
+      fmark<kDiag>(a, fr, kFmDpub);
     }
     // exchange 2: x[seg] = cast(x'[seg] + cast(sum_c D[c][seg]))
     {
       const unsigned long long* Dq = a.ll_clusters + (size_t)(tag & 1u) * cx.nc * D;
       const bool ok = flow_gather<D>(a, fr, Dq, (int)cx.nc, seg0, n, tag, sm) && dok && ok1;
-      fmark(a, fr, kFmGather2);
+      fmark<kDiag>(a, fr, kFmGather2);
       const float* x2 = sm.x2;
       if ((int)threadIdx.x < n) {
         const float v = Storage<T>::round(x2[seg0 + threadIdx.x] + Storage<T>::round(sm.seg[threadIdx.x]));
@@ -1137,7 +1139,7 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
       }
       flow_bsync(fr);
       if (!flow_publish(a, fr, sm, cx, ok && !fr.failed)) return false;
-      fmark(a, fr, kFmPub1);
+      fmark<kDiag>(a, fr, kFmPub1);
     }
   }
   // final RMSNorm and score head (no cast), by the score CTA
@@ -1157,7 +1159,7 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
       if (score_copy) *score_copy = total;
     }
   }
-  fmark(a, fr, kFmScore);
+  fmark<kDiag>(a, fr, kFmScore);
   cx.steps += 1;
   return true;
 }
@@ -1169,10 +1171,9 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
 // CTA 0 polls the mapped mailbox, stages the event and publishes each command
 // on a tagged control word every CTA polls; the score CTA publishes RUN
 // completions; RESET ends with a count of CTAs on the barrier counter.
-// The body of the single-stream step kernels (k4_flow here, k5_chain in
-// st_chain.cuh): Sm is the kernel's shared-memory struct (the ring bookkeeping
-// follows it, the ring buffer starts at ring_offset), step(a, fr, cur, sm, cx,
-// event, t, score_dst, score_copy) runs one event.
+// The body of the single-stream step kernel: Sm is its shared-memory struct
+// (the ring bookkeeping follows it, the ring buffer starts at ring_offset),
+// step(a, fr, cur, sm, cx, event, t, score_dst, score_copy) runs one event.
 template <typename T, int D, class Sm, class Step>
 __device__ __forceinline__ void flow_run(const StepArgs& a, const FlowLaunch& f, unsigned char* flow_raw,
                                          size_t ring_offset, unsigned ring_capacity, Step&& step) {
@@ -1195,7 +1196,10 @@ __device__ __forceinline__ void flow_run(const StepArgs& a, const FlowLaunch& f,
   cx.steps = 0;
   for (int i = 0; i < kSites; ++i) cx.k[i] = 0;
   cx.bx = 0;
-  fr.tl_n = 0;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kFlowTags; ++i) fr.tsum[i] = 0;
+    fr.tlast = clock64();
+  }
   const unsigned long long t0 = ld_cg_u64(a.position);
   for (int i = threadIdx.x; i < kFlowHd / 2; i += kThreads) sm.rope[i] = a.rope_freq[i];
   if (cx.score_cluster && cx.rank == 0)
@@ -1400,13 +1404,13 @@ __device__ __forceinline__ void flow_run(const StepArgs& a, const FlowLaunch& f,
   if (blockIdx.x == 0) persistent_exit<T>(a, p);
 }
 
-template <typename T, int D>
+template <typename T, int D, bool kDiag>
 __global__ void __launch_bounds__(kFlowThreads, 1) k4_flow(StepArgs a, FlowLaunch f) {
   extern __shared__ __align__(128) unsigned char flow_raw[];
   flow_run<T, D, FlowSmem>(a, f, flow_raw, kFlowRingOffset, kFlowRingCapacity,
                            [](const StepArgs& a, FlowRing& fr, FlowCur& cur, FlowSmem& sm, FlowCtx& cx,
                               const float* event, unsigned long long t, float* dst, float* copy) {
-                             return flow_step<T, D>(a, fr, cur, sm, cx, event, t, dst, copy);
+                             return flow_step<T, D, kDiag>(a, fr, cur, sm, cx, event, t, dst, copy);
                            });
 }
 

@@ -10,12 +10,9 @@ namespace st {
 struct StepArgs;
 struct FlowLaunch;
 
-// k4_flow<T, width> for mode 0 fp32, 1 fp16, 2 bf16; null for other widths.
-const void* flow_kernel(int mode, int width);
-// k5_chain<T, width, diag> (st_chain.cu), same launch shape, arguments and
-// shared memory size as k4_flow; diag: the variant that records the phase
-// timeline.
-const void* chain_kernel(int mode, int width, bool diag);
+// k4_flow<T, width, diag> for mode 0 fp32, 1 fp16, 2 bf16; null for other
+// widths; diag: the variant that records per-phase cycle sums.
+const void* flow_kernel(int mode, int width, bool diag);
 // Dynamic shared memory and threads per CTA of k4_flow.
 size_t flow_smem_bytes();
 int flow_threads();

@@ -159,10 +159,7 @@ struct st_runtime {
   // cluster shape; ST_FLOW=0 selects the generic kernels.
   bool flow = false;
   const void* flow_fn = nullptr;
-  // The single-stream kernel: k5_chain (compact code, st_chain.cuh) unless
-  // ST_CHAIN=0 selects k4_flow (st_flow.cuh); flow_diag_fn records timelines.
-  bool chain = false;
-  const void* flow_diag_fn = nullptr;
+  const void* flow_diag_fn = nullptr;  // the same kernel with per-phase cycle sums (timelines)
   int fcluster = 0, fnclusters = 0, fgrid = 0;
   int bgrid = 0;
   int bsplit[4] = {1, 1, 1, 1};
@@ -875,10 +872,8 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   {
     const char* env = std::getenv("ST_FLOW");
     const int mode_index = m.mode == ST_MODE_FP16 ? 1 : m.mode == ST_MODE_BF16 ? 2 : 0;
-    const char* kenv = std::getenv("ST_CHAIN");
-    rt->chain = !(kenv && kenv[0] == '0');
-    rt->flow_fn = rt->chain ? chain_kernel(mode_index, d, false) : flow_kernel(mode_index, d);
-    rt->flow_diag_fn = rt->chain ? chain_kernel(mode_index, d, true) : rt->flow_fn;
+    rt->flow_fn = flow_kernel(mode_index, d, false);
+    rt->flow_diag_fn = flow_kernel(mode_index, d, true);
     const bool want = rt->flow_fn && S == 1 && hd == kFlowHd && m.features == kFlowFeatures && o.blocks == 0 &&
                       !rt->batched && coop && !(env && env[0] == '0');
     if (want) {
@@ -985,7 +980,15 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   a.bar_counter = (unsigned long long*)(rt->scratch + bar_at);
   a.error = (int*)(rt->scratch + err_at);
   a.host_error = &rt->mb_d->error;
+  // Bound on any single device-side wait. ST_DEVICE_TIMEOUT_MS shortens it
+  // and ST_TEST_DROP_RECORD=<cta> makes that CTA of the single-stream kernel
+  // withhold one exchange record: the failure-path test of the bounded waits
+  // (a flag nothing sets, no fault), which must end in ST_ERR_DEVICE_TIMEOUT.
   a.bar_timeout_ns = 2ull * 1000000000ull;
+  if (const char* env = std::getenv("ST_DEVICE_TIMEOUT_MS"))
+    a.bar_timeout_ns = (unsigned long long)std::max(1, std::atoi(env)) * 1000000ull;
+  a.test_drop_cta = -1;
+  if (const char* env = std::getenv("ST_TEST_DROP_RECORD")) a.test_drop_cta = std::atoi(env);
   a.cluster_size = rt->cluster;
   a.clusters = rt->nclusters;
   if (rt->batched) {
@@ -1376,8 +1379,15 @@ int st_device_timeline_cta(st_runtime* rt, const float* inputs, size_t count, in
                            size_t capacity, size_t* used) {
   if (!rt || !inputs || !marks || count == 0 || capacity == 0) return ST_ERR_INVALID;
   const int grid = rt->batched ? rt->bgrid : rt->flow ? rt->fgrid : rt->grid;
-  // cta -1: every CTA of the flow kernel records {tag, globaltimer} pairs
-  if (cta < (rt->flow ? -1 : 0) || cta >= grid) return rt->fail(ST_ERR_INVALID, "timeline CTA %d outside the grid of %d", cta, grid);
+  // The single-stream kernels record per-phase cycle sums of every CTA
+  // (cta -1, marks[cta * 32 + tag]); the others one CTA's clock marks.
+  if (rt->flow && !rt->batched) {
+    if (cta != -1 || capacity < (size_t)grid * kFlowTags)
+      return rt->fail(ST_ERR_INVALID, "the single-stream kernel records per-CTA phase sums: cta -1, capacity >= %d",
+                      grid * kFlowTags);
+  } else if (cta < 0 || cta >= grid) {
+    return rt->fail(ST_ERR_INVALID, "timeline CTA %d outside the grid of %d", cta, grid);
+  }
   if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
   if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
   if (rt->opt.backend == ST_BACKEND_PERSISTENT) ST_TRY(st_stop(rt));
@@ -1401,7 +1411,9 @@ int st_device_timeline_cta(st_runtime* rt, const float* inputs, size_t count, in
   if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "timeline run");
   if (st == ST_OK) st = check_device_error(rt);
   if (st == ST_OK) st = rt->cuda(cudaMemcpy(marks, tl, capacity * sizeof(long long), cudaMemcpyDeviceToHost), "timeline download");
-  if (st == ST_OK && used) {  // warp 0's entries
+  if (st == ST_OK && used && rt->flow && !rt->batched) {
+    *used = (size_t)grid * kFlowTags;
+  } else if (st == ST_OK && used) {  // warp 0's entries
     const size_t per_warp = capacity / kWarps;
     size_t u = 0;
     while (u < per_warp && marks[u] != 0) ++u;
@@ -1452,7 +1464,7 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
   const bool flow_loop = rt->flow && (rt->opt.backend == ST_BACKEND_FUSED || rt->opt.backend == ST_BACKEND_PERSISTENT);
   if (flow_loop) {
     kernel = rt->flow_fn;
-    name = rt->chain ? "k5_chain" : "k4_flow";
+    name = "k4_flow";
   }
   cudaFuncGetAttributes(&fa, kernel);
   static const char* backends[] = {"cuda", "graph", "cublas", "cublas-graph", "fused", "persistent"};

@@ -1,5 +1,4 @@
-"""GPU parity of the single-stream step kernels (k5_chain, csrc/st_chain.cuh, the
-default; k4_flow, csrc/st_flow.cuh, with ST_CHAIN=0) at the shapes the
+"""GPU parity of the single-stream flow kernel (csrc/st_flow.cuh) at the shapes the
 benchmark configurations use but the golden fixtures do not reach: the window
 extremes of the C3 sweep (32 and 512 slots, i.e. 4 and 64 slots per cluster rank)
 and the width-1024 instantiation with 4-CTA clusters (C4 bf16, C5 fp32). Each run is
@@ -17,7 +16,7 @@ pytestmark = pytest.mark.gpu
 def assert_flow(model, cluster=None):
     with Runtime(model, RuntimeOptions(backend=Backend.PERSISTENT, blocks=0)) as rt:
         info = rt.info()
-    assert info["flow"] and info["resource_kernel"] in ("k5_chain", "k4_flow"), info["resource_kernel"]
+    assert info["flow"] and info["resource_kernel"] == "k4_flow", info["resource_kernel"]
     if cluster is not None:
         assert info["cluster"] == cluster
 

@@ -127,3 +127,41 @@ def test_snapshot_during_persistent_run_and_reset_stream_errors():
     with pytest.raises(StreamError):
         rt.reset_stream(3)
     rt.close()
+
+
+@pytest.mark.parametrize("backend", [Backend.FUSED, Backend.PERSISTENT], ids=lambda b: b.name.lower())
+def test_bounded_device_wait_runs_out(backend, monkeypatch):
+    """A device-side wait whose flag nothing sets: CTA 0 of the single-stream
+    kernel withholds its layer-0 out-projection records (ST_TEST_DROP_RECORD),
+    so every CTA's exchange-1 wait runs out its bound (shortened to 50 ms by
+    ST_DEVICE_TIMEOUT_MS). The kernel must return with the error word set, the
+    host must report DEVICE_TIMEOUT, the runtime must then refuse work and be
+    destroyed cleanly, and the same context must serve a fresh runtime whose
+    results match the oracle (reference tests/Lifecycle.cu:50-73; host-side
+    detection src/cuda/Runtime.cu:417-426). Nothing faults or hangs the GPU."""
+    from streaming_transformer_b200 import synthetic
+    config, mode = synthetic.CONFIGS["c1-small-fp32"]
+    model = synthetic.make_model(config, mode, seed=3)
+    events = synthetic.make_events(3, config.features, seed=4)
+    monkeypatch.setenv("ST_DEVICE_TIMEOUT_MS", "50")
+    monkeypatch.setenv("ST_TEST_DROP_RECORD", "0")
+    rt = None
+    t0 = time.perf_counter()
+    with pytest.raises(StreamError) as info:
+        # FUSED meets the withheld record already in st_start's warm-up step
+        rt = Runtime(model, RuntimeOptions(backend=backend, blocks=0))
+        assert rt.info()["resource_kernel"] == "k4_flow"
+        rt.step(events[0])
+    assert info.value.status == "DEVICE_TIMEOUT", str(info.value)
+    assert time.perf_counter() - t0 < 20.0
+    if rt is not None:
+        with pytest.raises(StreamError):
+            rt.step(events[1])
+        rt.close()
+    monkeypatch.delenv("ST_DEVICE_TIMEOUT_MS")
+    monkeypatch.delenv("ST_TEST_DROP_RECORD")
+    o = Oracle(model)
+    with Runtime(model, RuntimeOptions(backend=backend, blocks=0)) as fresh:
+        got = np.array([fresh.step(e) for e in events])
+    want = np.array([o.step(e) for e in events])
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6)
