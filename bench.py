@@ -36,7 +36,11 @@ Unless --no-c4 is given (or the workload is C4 itself), the line also carries a
 "c4" record: Large bf16 with 256 streams in total partitioned over the N GPUs,
 stepped by the batched round from a full window, aggregate stream-steps/s
 against the per-GPU-count roofline (every GPU reads the whole weights once per
-round plus its own streams' K/V).
+round plus its own streams' K/V). With N >= 2 GPUs (unless --no-c5b) it also
+carries a "c5b" record: one Large fp32 stream (W512) tensor-parallel over the N
+GPUs (st_create_tp: each GPU its share of the heads and ffn rows, exchanges
+over NVLink inside the kernel), device steps/s from a full window, against the
+roofline of one GPU's shard of the bytes.
 """
 from __future__ import annotations
 
@@ -77,6 +81,8 @@ def parse_args():
                         "1 = one replica stream per GPU")
     p.add_argument("--no-c4", action="store_true", help="skip the C4 256-stream partition record")
     p.add_argument("--c4-rounds", type=int, default=100, help="timed rounds of the C4 record (at most --steps)")
+    p.add_argument("--no-c5b", action="store_true", help="skip the C5-B tensor-parallel record (N >= 2)")
+    p.add_argument("--c5b-steps", type=int, default=200, help="timed steps of the C5-B record (at most --steps)")
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU baseline sample budget")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
@@ -327,6 +333,36 @@ def run_rounds(model, config, S, rank, warm, timed, local, seed_base):
     return us, launches, info, stride
 
 
+def run_tp_stream(world, rank, local, steps, host):
+    """C5-B: one Large fp32 stream over all ranks' GPUs; (us per step, launches, info)."""
+    import torch
+    from streaming_transformer_b200.tp import torch_tensor_parallel
+    config, mode = synthetic.CONFIGS["c5-large-fp32"]
+    model = synthetic.make_model(config, mode, seed=42)
+    warm = config.window
+    events = synthetic.make_events(warm + steps, config.features, seed=321)  # one stream: the same on every GPU
+    dev = torch.from_numpy(events).cuda()
+    rt = Runtime(model, RuntimeOptions(backend=Backend.FUSED, blocks=0, device=local),
+                 tp=torch_tensor_parallel(host))
+    try:
+        rt.device_trace_resident(dev.data_ptr(), warm)
+        torch.cuda.synchronize()
+        us, launches = rt.device_trace_continue(dev[warm:].data_ptr(), steps)
+        info = rt.info()
+    finally:
+        rt.close()
+    return us, launches, info, config, mode
+
+
+def c5b_roofline(world, peak_gbs):
+    """Bytes one GPU of the tensor-parallel stream reads per step (its 1/N of
+    the weights and of the heads' K/V) at the measured peak."""
+    config, mode = synthetic.CONFIGS["c5-large-fp32"]
+    e = metrics.ELEM_BYTES[mode]
+    per_gpu = metrics.weight_bytes(config, mode) / world + 2 * config.layers * config.width * (config.window + 1) * e / world
+    return per_gpu / (peak_gbs * 1e9) * 1e6, int(per_gpu)
+
+
 def run_b200(args):
     import torch
     world, rank, local = dist_env()
@@ -405,8 +441,14 @@ def run_b200(args):
                                                         local, 7000)
             barrier()
             c4 = (c4_us, c4_K, c4_S, c4_launches, c4_info, c4_config, c4_mode)
+        c5b = None
+        if world > 1 and not args.no_c5b:
+            c5b_K = max(1, min(K, args.c5b_steps))
+            barrier()
+            c5b = run_tp_stream(world, rank, local, c5b_K, host) + (c5b_K,)
+            barrier()
     elapsed_s = us * K / 1e6
-    times = [elapsed_s, e2e_wall] + ([c4[0] * c4[1] / 1e6] if c4 else [])
+    times = [elapsed_s, e2e_wall] + ([c4[0] * c4[1] / 1e6] if c4 else []) + ([c5b[0]] if c5b else [])
     maxed = combine_ranks(times, dist, host)
     max_elapsed, max_e2e = maxed[0], maxed[1]
     if dist:
@@ -458,6 +500,22 @@ def run_b200(args):
             "per_gpu_bytes_per_round": per_gpu_bytes, "peak_source": peak_src,
             "kernel": kernel_label(c4_info, c4_mode, c4_S), "gpu_launches": c4_launches,
             "tensor_cores": c4_info.get("batched_tensor_cores"),
+        }
+    if c5b:
+        c5b_us, c5b_launches, c5b_info, c5b_config, c5b_mode, c5b_K = c5b
+        c5b_us = maxed[-1]
+        roof_us, per_gpu_bytes = c5b_roofline(world, peak)
+        line["c5b"] = {
+            "workload": (f"c5-large-fp32 phase B: one stream, d1024 L12 H16 F4096 W512 fp32, tensor-parallel over "
+                         f"{world} GPUs ({16 // world} heads and {4096 // world} ffn rows each), {c5b_config.window} "
+                         f"untimed steps then {c5b_K} timed"),
+            "value": 1e6 / c5b_us, "unit": "steps/s", "us_per_step": c5b_us, "scaling": "strong",
+            "roofline_us_per_step": roof_us, "roofline_frac": roof_us / c5b_us,
+            "per_gpu_bytes_per_step": per_gpu_bytes, "peak_source": peak_src,
+            "kernel": f"k4_flow tensor-parallel ({c5b_info.get('clusters')} clusters of {c5b_info.get('cluster')})",
+            "gpu_launches": c5b_launches,
+            "exchanges": "out-projection records and down sums stored into every GPU's buffers over NVLink, "
+                         "polled locally (no collective library on the step path)",
         }
     if world == 1 and not args.no_cpu_baseline:
         sps, n, dt = time_cpu_oracle(model, events[:, 0], 1, args.cpu_seconds, K)

@@ -99,6 +99,31 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
  * count must equal the tensor's element count. */
 int st_set_tensor(st_runtime* rt, const char* name, const float* data, size_t count);
 
+/* Tensor parallelism of one stream over tp_size GPUs of one node (1..8), one
+ * runtime per GPU in its own process: GPU tp_rank owns heads
+ * [tp_rank H/tp_size, +H/tp_size) and ffn rows [tp_rank F/tp_size, +F/tp_size)
+ * of every layer, and the single-stream kernels of all GPUs exchange the
+ * out-projection partials and the down-projection sums through each other's
+ * memory over NVLink (plain stores into the peers' record buffers, polled
+ * locally, every wait bounded). Needs the single-stream kernel's shapes,
+ * streams == 1, heads and ffn divisible by tp_size, and the FUSED or PERSISTENT
+ * backend. New; the reference runs one GPU per stream.
+ * Sequence: st_create_tp on every GPU; st_tp_handle on every GPU; give every
+ * GPU all tp_size handles in rank order with st_tp_connect; upload the tensors
+ * (every GPU keeps the full weights and reads its shard); st_start on all GPUs
+ * together. Every later call that runs the model (st_step, st_reset,
+ * st_device_trace*) is collective: all GPUs of the stream make it with the
+ * same inputs, in the same order, within the device wait bound (2 s).
+ * st_snapshot of a GPU returns its own heads' K/V (zeros elsewhere) and the
+ * full hidden state. */
+int st_create_tp(const st_model_desc* model, const st_options* options, int tp_rank, int tp_size,
+                 st_runtime** out);
+/* This GPU's connection handle (an opaque blob of at most 256 bytes; *needed
+ * receives its size). */
+int st_tp_handle(st_runtime* rt, void* blob, size_t capacity, size_t* needed);
+/* All tp_size handles, concatenated in rank order (this GPU's included). */
+int st_tp_connect(st_runtime* rt, const void* blobs, size_t count);
+
 /* Checks that every tensor is present, warms up, captures the graph (GRAPH) or
  * starts the resident worker (PERSISTENT) (reference src/cuda/Runtime.cu:263-291). */
 int st_start(st_runtime* rt);
@@ -121,6 +146,12 @@ int st_reset_stream(st_runtime* rt, int stream);
 /* STOP the resident worker and join it; idempotent (reference Runtime::stop,
  * src/cuda/Runtime.cu:466-474). No-op for the other backends. */
 int st_stop(st_runtime* rt);
+
+/* Start a new resident worker after st_stop (PERSISTENT backend; a no-op
+ * otherwise or while one runs). New: with st_load_state it hands a state to
+ * the persistent backend; the reference's stop is final. Collective for a
+ * tensor-parallel stream. */
+int st_resume(st_runtime* rt);
 
 /* Copy stream `stream`'s state to host: position, keys and values
  * [layers][heads][window][head_dim] widened to float, hidden [layers][width]

@@ -6,9 +6,9 @@ A drop-in for the per-event hot path of vishalkishore/streaming-transformer
 include/Runtime.hpp as the C++ one.
 """
 from .model import CheckpointError, Model, ModelConfig, tensor_shapes, write_checkpoint
-from .runtime import (Backend, BACKEND_NAMES, Runtime, RuntimeOptions, Snapshot, StreamError,
+from .runtime import (Backend, BACKEND_NAMES, Runtime, RuntimeOptions, Snapshot, StreamError, TensorParallel,
                       library, probe, transport_bench)
 
 __all__ = ["Backend", "BACKEND_NAMES", "CheckpointError", "Model", "ModelConfig", "Runtime",
-           "RuntimeOptions", "Snapshot", "StreamError", "library", "probe", "tensor_shapes", "transport_bench",
+           "RuntimeOptions", "Snapshot", "StreamError", "TensorParallel", "library", "probe", "tensor_shapes", "transport_bench",
            "write_checkpoint"]

@@ -38,6 +38,7 @@ constexpr int kMaxBlocksPerRow = kMaxCols / 4 / 32;  // fp32: 16-byte vectors / 
 constexpr int kAttChunk = 32;               // ring slots per attention work item
 constexpr int kMaxLayers = 16;
 constexpr int kUnroll = 8;                  // 16-byte loads in flight per lane
+constexpr int kMaxTp = 8;                   // GPUs one tensor-parallel stream may span
 
 enum ErrorCode : int { kOk = 0, kBarrierTimeout = 1, kAborted = 2, kClusterShape = 3, kRingTable = 4 };
 enum Command : int { kRun = 1, kReset = 2, kStop = 3, kPing = 4 };
@@ -85,6 +86,14 @@ struct StepArgs {
   int timeline_capacity;
   int timeline_cta;                   // the CTA that records the timeline
   int l2_keep_layers;                 // layers whose weights are kept L2-resident (weight ring)
+  // tensor parallelism of one stream over tp_size GPUs (single-stream kernel):
+  // this GPU owns heads [tp_rank H / tp_size, +H / tp_size) and ffn rows
+  // [tp_rank F / tp_size, +F / tp_size); record buffers of every GPU (this
+  // one at tp_rank), mapped into this GPU's address space
+  int tp_rank, tp_size;
+  unsigned long long* ll_heads_peer[kMaxTp];  // [2][H][d] out-projection records on each GPU
+  unsigned long long* ll_xd_peer[kMaxTp];     // [2][tp_size][d] GPU-local down sums on each GPU
+  unsigned long long* ll_xd;                  // this GPU's [2][tp_size][d] down-sum records
   int test_drop_cta;                  // failure-path test only (-1 off): this CTA of the single-stream
                                       // kernel withholds its layer-0 out-projection records, so every
                                       // exchange-1 wait runs out its bound

@@ -39,8 +39,8 @@ bool flow_shape_ok(const StepArgs& a, size_t elem, int cluster, int clusters) {
   if (a.streams != 1 || a.head_dim != kFlowHd || a.features != kFlowFeatures) return false;
   if (a.width != 256 && a.width != 512 && a.width != 1024) return false;
   if (cluster < 2 || cluster > kFlowMaxCluster || a.width % (2 * cluster) != 0) return false;
-  const int grid = cluster * clusters;
-  if ((a.ffn + grid - 1) / grid > kFlowMaxAct || a.ffn < grid) return false;
+  const int grid = cluster * clusters, ffn = a.ffn / a.tp_size;
+  if ((ffn + grid - 1) / grid > kFlowMaxAct || ffn < grid) return false;
   for (int id = 0; id < clusters; ++id)
     for (int rank = 0; rank < cluster; ++rank)
       if (flow_chunks_per_step(a, Where{rank, cluster, id, clusters}, elem) > kFlowMaxChunks) return false;

@@ -128,10 +128,11 @@ __host__ __device__ inline int flow_chunks_per_step(const StepArgs& a, const Whe
   int n = 0;
   auto count = [&](int kind, int l, int h) { n += flow_split(span_of(a, w, kind, l, h, elem), kind).chunks; };
   count(kSpanIn, -1, 0);
+  const int hl = a.heads / a.tp_size, hb = a.tp_rank * hl;
   for (int l = 0; l < a.layers; ++l) {
-    if (w.id < a.heads) {
+    if (w.id < hl) {
       count(kSpanNorm1, l, 0);
-      for (int h = w.id; h < a.heads; h += w.count) {
+      for (int h = hb + w.id; h < hb + hl; h += w.count) {
         count(kSpanQkv, l, h);
         count(kSpanOut, l, h);
       }
@@ -154,7 +155,8 @@ struct FlowPlan {
   int qkv_lo;   // first q/k/v row pair of this rank within the head
 };
 __device__ inline FlowSpan flow_span(const StepArgs& a, const Where& w, int kind, size_t elem) {
-  const Span s = span_of(a, w, kind, 0, w.id < a.heads ? w.id : 0, elem);
+  const int hl = a.heads / a.tp_size;
+  const Span s = span_of(a, w, kind, 0, a.tp_rank * hl + (w.id < hl ? w.id : 0), elem);
   const FlowSplit sp = flow_split(s, kind);
   return {s.rows, sp.chunks, sp.rows_per_chunk};
 }
@@ -274,8 +276,14 @@ __device__ __forceinline__ void ll_store2(unsigned long long* p, float v0, float
   asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(ll_pack(v0, tag)), "l"(ll_pack(v1, tag))
                : "memory");
 }
+// Records that cross GPUs (tensor parallelism): system scope, stored through
+// the peer's mapping over NVLink; each 8-byte record is single-copy atomic.
+__device__ __forceinline__ void ll_store2_sys(unsigned long long* p, float v0, float v1, unsigned tag) {
+  asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(ll_pack(v0, tag)), "l"(ll_pack(v1, tag))
+               : "memory");
+}
 __device__ __forceinline__ void ll_load2(const unsigned long long* p, unsigned long long& r0, unsigned long long& r1) {
-  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(r0), "=l"(r1) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(r0), "=l"(r1) : "l"(p) : "memory");
 }
 __device__ __forceinline__ unsigned ll_tag(unsigned long long r) { return (unsigned)(r >> 32); }
 __device__ __forceinline__ float ll_value(unsigned long long r) { return __uint_as_float((unsigned)r); }
@@ -482,11 +490,12 @@ __device__ inline bool flow_ring_begin(const StepArgs& a, FlowRing& fr, unsigned
       }
     };
     add(kSpanIn, -1, 0);
+    const int hl = a.heads / a.tp_size, hb = a.tp_rank * hl;
     for (int l = 0; l < a.layers; ++l) {
       keep = l < a.l2_keep_layers ? 1u : 0u;
-      if (w.id < a.heads) {
+      if (w.id < hl) {
         add(kSpanNorm1, l, 0);
-        for (int h = w.id; h < a.heads; h += w.count) {
+        for (int h = hb + w.id; h < hb + hl; h += w.count) {
           add(kSpanQkv, l, h);
           add(kSpanOut, l, h);
         }
@@ -996,11 +1005,17 @@ __device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowC
   {
     FlowX<T, hd> xr;
     xr.load(sm.o);
-    unsigned long long* P = a.ll_heads + ((size_t)(tag & 1u) * a.heads + h) * D + cx.seg0;
+    const size_t at = ((size_t)(tag & 1u) * a.heads + h) * D + cx.seg0;
     // (a failure-path test may withhold this CTA's first layer-0 records)
     const bool drop = (int)blockIdx.x == a.test_drop_cta && l == 0 && cx.steps == 0;
     flow_rows<T, hd, 2, kDiag>(a, fr, cur, sm.plan.out, xr, [&](int r, const float (&v)[2]) {
-      if (!drop) ll_store2(P + r, v[0], v[1], tag);
+      if (drop) return;
+      if (a.tp_size == 1) {
+        ll_store2(a.ll_heads + at + r, v[0], v[1], tag);
+      } else {
+        // every GPU gathers every head: the record into each GPU's buffer
+        for (int g = 0; g < a.tp_size; ++g) ll_store2_sys(a.ll_heads_peer[g] + at + r, v[0], v[1], tag);
+      }
     });
   }
   fmark<kDiag>(a, fr, kFmOut);
@@ -1036,9 +1051,11 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
   for (int l = 0; l < a.layers; ++l) {
     const unsigned tag = (unsigned)(cx.epoch + cx.steps * (unsigned long long)a.layers + (unsigned long long)l + 1ull);
     bool hok = true;
-    if (cx.heads_here)
-      for (int h = (int)cx.id; h < a.heads; h += (int)cx.nc)
-        hok = flow_head<T, D, kDiag>(a, fr, cur, sm, cx, l, h, t, tag, h == (int)cx.id) && hok;
+    if (cx.heads_here) {
+      const int hl = a.heads / a.tp_size, hb = a.tp_rank * hl;
+      for (int h = hb + (int)cx.id; h < hb + hl; h += (int)cx.nc)
+        hok = flow_head<T, D, kDiag>(a, fr, cur, sm, cx, l, h, t, tag, h == hb + (int)cx.id) && hok;
+    }
     // exchange 1 (whole width, no cluster handoff): x' = cast(x + cast(sum_h P[h]))
     float ssq = 0.f;
     bool ok1;
@@ -1129,7 +1146,19 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
     // exchange 2: x[seg] = cast(x'[seg] + cast(sum_c D[c][seg]))
     {
       const unsigned long long* Dq = a.ll_clusters + (size_t)(tag & 1u) * cx.nc * D;
-      const bool ok = flow_gather<D>(a, fr, Dq, (int)cx.nc, seg0, n, tag, sm) && dok && ok1;
+      bool ok = flow_gather<D>(a, fr, Dq, (int)cx.nc, seg0, n, tag, sm) && dok && ok1;
+      if (a.tp_size > 1) {
+        // sm.seg holds this GPU's ffn share of the segment; cluster 0 sends it to
+        // every GPU, and every rank sums the GPUs' shares in GPU order
+        const size_t at = ((size_t)(tag & 1u) * a.tp_size + a.tp_rank) * D + seg0;
+        if (cx.id == 0)
+          for (int i = 2 * (int)threadIdx.x; i < n; i += 2 * kThreads)
+            for (int g = 0; g < a.tp_size; ++g)
+              ll_store2_sys(a.ll_xd_peer[g] + at + i, sm.seg[i], sm.seg[i + 1], tag);
+        flow_bsync(fr);  // sm.seg is read above before the gather overwrites it
+        const unsigned long long* X = a.ll_xd + (size_t)(tag & 1u) * a.tp_size * D;
+        ok = flow_gather<D>(a, fr, X, a.tp_size, seg0, n, tag, sm) && ok;
+      }
       fmark<kDiag>(a, fr, kFmGather2);
       const float* x2 = sm.x2;
       if ((int)threadIdx.x < n) {
@@ -1190,7 +1219,7 @@ __device__ __forceinline__ void flow_run(const StepArgs& a, const FlowLaunch& f,
   cx.nc = cluster_count();
   cx.n = D / (int)cx.cs;
   cx.seg0 = (int)cx.rank * cx.n;
-  cx.heads_here = (int)cx.id < a.heads;
+  cx.heads_here = (int)cx.id < a.heads / a.tp_size;
   cx.score_cluster = cx.id == cx.nc - 1;
   cx.epoch = ld_cg_u64(a.flow_epoch);
   cx.steps = 0;

@@ -165,17 +165,27 @@ __host__ __device__ inline Span span_of(const StepArgs& a, const Where& w, int k
       s.base = (const char*)L.out + ((size_t)head * d + lo) * s.row_bytes;
       s.rows = hi - lo;
       break;
-    case kSpanGateUp:
-      split_range(F, w.id * w.size + w.rank, w.count * w.size, lo, hi);
+    case kSpanGateUp: {
+      // this GPU's ffn shard (all of F without tensor parallelism), split over its CTAs
+      const int tps = a.tp_size > 0 ? a.tp_size : 1, fl = F / tps, fb = a.tp_rank * fl;
+      split_range(fl, w.id * w.size + w.rank, w.count * w.size, lo, hi);
+      lo += fb;
+      hi += fb;
       s.row_bytes = (int)(d * elem);
       s.base = (const char*)L.gateup + 2 * (size_t)lo * s.row_bytes;
       s.rows = 2 * (hi - lo);
+    }
       break;
-    case kSpanDown:
-      split_range(F, w.id * w.size + w.rank, w.count * w.size, lo, hi);
+    case kSpanDown: {
+      // this GPU's ffn shard (all of F without tensor parallelism), split over its CTAs
+      const int tps = a.tp_size > 0 ? a.tp_size : 1, fl = F / tps, fb = a.tp_rank * fl;
+      split_range(fl, w.id * w.size + w.rank, w.count * w.size, lo, hi);
+      lo += fb;
+      hi += fb;
       s.row_bytes = (int)(d * elem);
       s.base = (const char*)L.down + (size_t)lo * s.row_bytes;
       s.rows = hi - lo;
+    }
       break;
     default:
       break;

@@ -159,6 +159,10 @@ struct st_runtime {
   // cluster shape; ST_FLOW=0 selects the generic kernels.
   bool flow = false;
   const void* flow_fn = nullptr;
+  // tensor parallelism of the one stream over tp_size GPUs (st_create_tp)
+  int tp_rank = 0, tp_size = 1;
+  size_t llh_at = 0, llx_at = 0;          // record buffers' offsets in the scratch allocation
+  char* tp_peer_base[kMaxTp] = {};        // peers' scratch allocations opened through IPC
   const void* flow_diag_fn = nullptr;  // the same kernel with per-phase cycle sums (timelines)
   int fcluster = 0, fnclusters = 0, fgrid = 0;
   int bgrid = 0;
@@ -618,7 +622,33 @@ const char* st_last_error(const st_runtime* rt) { return rt ? rt->error.c_str() 
 
 uint64_t st_kernel_launches(const st_runtime* rt) { return rt ? rt->launches : 0; }
 
+static int create_impl(const st_model_desc* model, const st_options* options, int tp_rank, int tp_size,
+                       st_runtime** out);
+
 int st_create(const st_model_desc* model, const st_options* options, st_runtime** out) {
+  return create_impl(model, options, 0, 1, out);
+}
+
+int st_create_tp(const st_model_desc* model, const st_options* options, int tp_rank, int tp_size,
+                 st_runtime** out) {
+  if (!model || !options || !out) { g_create_error = "null argument"; return ST_ERR_INVALID; }
+  if (tp_size < 1 || tp_size > kMaxTp || tp_rank < 0 || tp_rank >= tp_size) {
+    g_create_error = "tensor-parallel rank or size out of range (1..8 GPUs)";
+    return ST_ERR_INVALID;
+  }
+  if (model->streams != 1 || model->heads % tp_size || model->ffn % tp_size) {
+    g_create_error = "tensor parallelism needs one stream and heads and ffn divisible by the GPU count";
+    return ST_ERR_INVALID;
+  }
+  if (options->backend != ST_BACKEND_FUSED && options->backend != ST_BACKEND_PERSISTENT) {
+    g_create_error = "tensor parallelism runs the single-stream device loop: FUSED or PERSISTENT backend";
+    return ST_ERR_UNSUPPORTED;
+  }
+  return create_impl(model, options, tp_rank, tp_size, out);
+}
+
+static int create_impl(const st_model_desc* model, const st_options* options, int tp_rank, int tp_size,
+                       st_runtime** out) {
   if (!model || !options || !out) { g_create_error = "null argument"; return ST_ERR_INVALID; }
   *out = nullptr;
   if (!validate_desc(model)) { g_create_error = "Invalid or unsupported model dimensions"; return ST_ERR_INVALID; }
@@ -641,6 +671,8 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   rt->desc = *model;
   rt->opt = o;
   rt->device = o.device;
+  rt->tp_rank = tp_rank;
+  rt->tp_size = tp_size;
   auto bail = [&](int code) {
     g_create_error = rt->error;
     st_destroy(rt);
@@ -904,11 +936,12 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
           return bail(ST_ERR_CUDA);
         const int nc = std::min(nmax, rt->sms / cs);
         if (nc < 1) continue;
-        if (best_cs == 0 || (best_nc < m.heads && nc >= m.heads)) {
+        const int local_heads = m.heads / tp_size;
+        if (best_cs == 0 || (best_nc < local_heads && nc >= local_heads)) {
           best_cs = cs;
           best_nc = nc;
         }
-        if (best_nc >= m.heads) break;
+        if (best_nc >= local_heads) break;
       }
       if (best_cs > 0) {
         rt->flow = true;
@@ -918,7 +951,15 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
       }
     }
   }
+  if (tp_size > 1 && !rt->flow) {
+    rt->fail(ST_ERR_UNSUPPORTED, "tensor parallelism needs the single-stream kernel's shapes (head_dim 64, 32 "
+                                 "features, width 256/512/1024, blocks 0)");
+    return bail(ST_ERR_UNSUPPORTED);
+  }
   const size_t llh_at = take(rt->flow ? 2 * (size_t)m.heads * d * 8 : 0);
+  const size_t llx_at = take(tp_size > 1 ? 2 * (size_t)tp_size * d * 8 : 0);
+  rt->llh_at = llh_at;
+  rt->llx_at = llx_at;
   const size_t llc_at = take(rt->flow ? 2 * (size_t)rt->fnclusters * d * 8 : 0);
   const size_t fwords_at = take(3 * sizeof(unsigned long long));
   rt->scratch_bytes = co;
@@ -1055,6 +1096,11 @@ int st_create(const st_model_desc* model, const st_options* options, st_runtime*
   rt->control = (Control*)(rt->scratch + ctl_at);
   a.ll_heads = (unsigned long long*)(rt->scratch + llh_at);
   a.ll_clusters = (unsigned long long*)(rt->scratch + llc_at);
+  a.tp_rank = tp_rank;
+  a.tp_size = tp_size;
+  a.ll_xd = (unsigned long long*)(rt->scratch + llx_at);
+  a.ll_heads_peer[tp_rank] = a.ll_heads;  // peers' entries arrive with st_tp_connect
+  a.ll_xd_peer[tp_rank] = a.ll_xd;
   a.flow_epoch = (unsigned long long*)(rt->scratch + fwords_at);
   a.flow_ctl = a.flow_epoch + 1;
   a.flow_seq = a.flow_epoch + 2;
@@ -1103,11 +1149,16 @@ int st_start(st_runtime* rt) {
   if (rt->started) return rt->fail(ST_ERR_STATE, "runtime already started");
   for (const auto& kv : rt->slots)
     if (!rt->have[kv.second.index]) return rt->fail(ST_ERR_INVALID, "Missing tensor %s", kv.first.c_str());
+  for (int g = 0; g < rt->tp_size; ++g)
+    if (!rt->args.ll_heads_peer[g] || !rt->args.ll_xd_peer[g])
+      return rt->fail(ST_ERR_STATE, "tensor-parallel GPU %d is not connected (st_tp_connect)", g);
   ST_CUDA(rt, cudaSetDevice(rt->device));
   ST_TRY(preload(rt));
   // Warm every kernel once (lazy module loading), then restore the initial state.
   if (rt->opt.backend != ST_BACKEND_PERSISTENT) {
-    ST_TRY(launch_sequence(rt, rt->args));
+    // (a tensor-parallel stream runs only the sharded single-stream kernel;
+    // its warm-up step is collective: every GPU of the stream takes it)
+    if (rt->tp_size == 1) ST_TRY(launch_sequence(rt, rt->args));
     if (rt->opt.backend == ST_BACKEND_FUSED) ST_TRY(launch_fused(rt, rt->args));
   }
   ST_TRY(launch_reset(rt, 0, rt->desc.streams));
@@ -1169,6 +1220,14 @@ int st_stop(st_runtime* rt) {
   return ST_OK;
 }
 
+int st_resume(st_runtime* rt) {
+  if (!rt) return ST_ERR_INVALID;
+  if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
+  if (!rt->started) return rt->fail(ST_ERR_STATE, "st_start has not been called");
+  if (rt->opt.backend != ST_BACKEND_PERSISTENT || rt->running) return ST_OK;
+  return start_persistent(rt);
+}
+
 int st_snapshot(st_runtime* rt, int stream, uint64_t* position, float* keys, float* values, float* hidden) {
   if (!rt) return ST_ERR_INVALID;
   if (rt->failed) return rt->fail(ST_ERR_STATE, "runtime failed earlier: %s", rt->error.c_str());
@@ -1203,6 +1262,59 @@ int st_snapshot(st_runtime* rt, int stream, uint64_t* position, float* keys, flo
     const size_t n = (size_t)m.layers * m.width;
     ST_CUDA(rt, cudaMemcpyAsync(hidden, rt->args.hidden + (size_t)stream * n, n * 4, cudaMemcpyDeviceToHost, s));
     ST_CUDA(rt, cudaStreamSynchronize(s));
+  }
+  return ST_OK;
+}
+
+// What one GPU of a tensor-parallel stream tells the others: the layout it was
+// built with (which must match theirs) and the IPC handle of the allocation
+// holding its record buffers.
+struct TpBlob {
+  unsigned long long magic;
+  int tp_rank, tp_size, heads, width, clusters, pad;
+  unsigned long long scratch_bytes, llh_at, llx_at;
+  cudaIpcMemHandle_t handle;
+};
+constexpr unsigned long long kTpMagic = 0x7374747062303031ull;
+
+int st_tp_handle(st_runtime* rt, void* blob, size_t capacity, size_t* needed) {
+  if (!rt) return ST_ERR_INVALID;
+  if (needed) *needed = sizeof(TpBlob);
+  if (!blob || capacity < sizeof(TpBlob)) return rt->fail(ST_ERR_INVALID, "handle buffer smaller than %zu bytes", sizeof(TpBlob));
+  TpBlob b{};
+  b.magic = kTpMagic;
+  b.tp_rank = rt->tp_rank;
+  b.tp_size = rt->tp_size;
+  b.heads = rt->desc.heads;
+  b.width = rt->desc.width;
+  b.clusters = rt->fnclusters;
+  b.scratch_bytes = rt->scratch_bytes;
+  b.llh_at = rt->llh_at;
+  b.llx_at = rt->llx_at;
+  ST_CUDA(rt, cudaSetDevice(rt->device));
+  ST_CUDA(rt, cudaIpcGetMemHandle(&b.handle, rt->scratch));
+  std::memcpy(blob, &b, sizeof b);
+  return ST_OK;
+}
+
+int st_tp_connect(st_runtime* rt, const void* blobs, size_t count) {
+  if (!rt || !blobs) return ST_ERR_INVALID;
+  if (rt->started) return rt->fail(ST_ERR_STATE, "connect the tensor-parallel GPUs before st_start");
+  if ((int)count != rt->tp_size) return rt->fail(ST_ERR_INVALID, "expected %d handles, got %zu", rt->tp_size, count);
+  ST_CUDA(rt, cudaSetDevice(rt->device));
+  const TpBlob* all = static_cast<const TpBlob*>(blobs);
+  for (int g = 0; g < rt->tp_size; ++g) {
+    const TpBlob& b = all[g];
+    if (b.magic != kTpMagic || b.tp_rank != g || b.tp_size != rt->tp_size || b.heads != rt->desc.heads ||
+        b.width != rt->desc.width || b.clusters != rt->fnclusters || b.scratch_bytes != rt->scratch_bytes ||
+        b.llh_at != rt->llh_at || b.llx_at != rt->llx_at)
+      return rt->fail(ST_ERR_INVALID, "tensor-parallel GPU %d was built with another layout", g);
+    if (g == rt->tp_rank) continue;
+    void* base = nullptr;
+    ST_CUDA(rt, cudaIpcOpenMemHandle(&base, b.handle, cudaIpcMemLazyEnablePeerAccess));
+    rt->tp_peer_base[g] = static_cast<char*>(base);
+    rt->args.ll_heads_peer[g] = reinterpret_cast<unsigned long long*>(rt->tp_peer_base[g] + b.llh_at);
+    rt->args.ll_xd_peer[g] = reinterpret_cast<unsigned long long*>(rt->tp_peer_base[g] + b.llx_at);
   }
   return ST_OK;
 }
@@ -1512,6 +1624,8 @@ void st_destroy(st_runtime* rt) {
   } else if (rt->stream) {
     cudaStreamSynchronize(rt->stream);
   }
+  for (int g = 0; g < kMaxTp; ++g)
+    if (rt->tp_peer_base[g]) cudaIpcCloseMemHandle(rt->tp_peer_base[g]);
   if (rt->graph_exec) cudaGraphExecDestroy(rt->graph_exec);
   if (rt->graph) cudaGraphDestroy(rt->graph);
   if (rt->ev_start) cudaEventDestroy(rt->ev_start);

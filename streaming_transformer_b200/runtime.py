@@ -69,6 +69,17 @@ class RuntimeOptions:
 
 
 @dataclass
+class TensorParallel:
+    """One stream split over ``size`` GPUs (st_create_tp): this process owns GPU
+    ``rank`` of the stream. ``exchange(blob)`` must return every rank's blob in
+    rank order (an all-gather among the stream's processes; see
+    streaming_transformer_b200.tp.torch_exchange)."""
+    rank: int
+    size: int
+    exchange: object
+
+
+@dataclass
 class Snapshot:
     """reference include/Runtime.hpp:20-23."""
     position: int
@@ -123,6 +134,10 @@ def library() -> ctypes.CDLL:
                                              ctypes.POINTER(U64)]),
             "st_device_trace_continue": (I, [P, ctypes.c_void_p, S, ctypes.POINTER(ctypes.c_double),
                                              ctypes.POINTER(U64)]),
+            "st_create_tp": (I, [ctypes.POINTER(_ModelDesc), ctypes.POINTER(_Options), I, I, ctypes.POINTER(P)]),
+            "st_resume": (I, [P]),
+            "st_tp_handle": (I, [P, ctypes.c_void_p, S, ctypes.POINTER(S)]),
+            "st_tp_connect": (I, [P, ctypes.c_void_p, S]),
             "st_info": (I, [P, ctypes.c_char_p, S, ctypes.POINTER(S)]),
             "st_probe": (I, [I, ctypes.c_char_p, S, ctypes.POINTER(S)]),
             "st_kernel_launches": (U64, [P]),
@@ -194,7 +209,8 @@ class Runtime:
     streams instead.
     """
 
-    def __init__(self, model: Model, options: RuntimeOptions | None = None, streams: int = 1):
+    def __init__(self, model: Model, options: RuntimeOptions | None = None, streams: int = 1,
+                 tp: "TensorParallel | None" = None):
         self.model = model
         self.options = options or RuntimeOptions()
         self.streams = int(streams)
@@ -208,7 +224,11 @@ class Runtime:
                         int(bool(o.vector_matvec)), int(bool(o.fused_attention)), int(o.max_events),
                         int(o.initial_sequence), float(o.idle_seconds), int(o.device))
         handle = ctypes.c_void_p()
-        code = lib.st_create(ctypes.byref(desc), ctypes.byref(opts), ctypes.byref(handle))
+        if tp is None:
+            code = lib.st_create(ctypes.byref(desc), ctypes.byref(opts), ctypes.byref(handle))
+        else:
+            code = lib.st_create_tp(ctypes.byref(desc), ctypes.byref(opts), int(tp.rank), int(tp.size),
+                                    ctypes.byref(handle))
         if code != ST_OK:
             raise StreamError(code, lib.st_last_error(None).decode())
         self._h = handle
@@ -216,6 +236,16 @@ class Runtime:
             for name in model.names():
                 data = np.ascontiguousarray(model.get(name), dtype=np.float32).ravel()
                 _check(lib.st_set_tensor(self._h, name.encode(), _fptr(data), data.size), self._h)
+            if tp is not None:
+                # every GPU of the stream maps every other GPU's record buffers;
+                # the exchange also lines the ranks up for st_start's collective
+                # warm-up step
+                need = ctypes.c_size_t(0)
+                blob = ctypes.create_string_buffer(256)
+                _check(lib.st_tp_handle(self._h, blob, 256, ctypes.byref(need)), self._h)
+                blobs = tp.exchange(blob.raw[: need.value])
+                joined = b"".join(blobs)
+                _check(lib.st_tp_connect(self._h, ctypes.c_char_p(joined), len(blobs)), self._h)
             _check(lib.st_start(self._h), self._h)
         except Exception:
             self.close()
@@ -272,6 +302,10 @@ class Runtime:
 
     def stop(self) -> None:
         _check(library().st_stop(self._h), self._h)
+
+    def start_worker(self) -> None:
+        """A new persistent worker after stop() (st_resume), e.g. after load_state."""
+        _check(library().st_resume(self._h), self._h)
 
     def snapshot(self, stream: int = 0) -> Snapshot:
         c = self.config
