@@ -251,6 +251,36 @@ int st_attention_static(int device, int mode, int heads, int head_dim, int windo
                         const float* q, const void* keys, const void* values, float* out, void* stream);
 const char* st_attention_static_error(void);
 
+/* Scheduled-arrival replay (reference bench/Main.cpp:282-343, statistics
+ * 416-447): event i of `inputs` ([count][features]) arrives at
+ * i / rate seconds after the start (bursty: in groups of 16 arriving at the
+ * group's first time) and is appended by a producer thread to a queue of
+ * `queue` events, or dropped when the queue is full; the calling thread takes
+ * events off the queue in order and steps them. */
+typedef struct {
+  double rate;          /* arrivals per second, > 0 */
+  int bursty;           /* 1: arrivals in groups of 16 */
+  size_t queue;         /* queue capacity, >= 1 */
+  double deadline_us;   /* an arrival-to-completion time above it counts as a miss */
+  int producer_core;    /* CPU the producer thread is pinned to, -1 for none */
+} st_schedule;
+/* One step: score the event `input`; returns ST_OK or an error code. */
+typedef int (*st_step_fn)(void* user, const float* input, float* score);
+/* The replay through any step function. samples ([count][4], may be NULL)
+ * receive each event's intended, enqueue, submit and completion times in
+ * steady-clock nanoseconds (submit and completion 0 when dropped); scores
+ * ([count], may be NULL) the scores (NaN when dropped); json the report:
+ * completed, dropped, service rate, deadline misses and the service,
+ * arrival-to-completion, queueing and injection distributions. A failing step
+ * ends the replay with its code; st_replay_error() has the message. */
+int st_replay_scheduled_with(st_step_fn step, void* user, const float* inputs, size_t count, size_t features,
+                             const st_schedule* schedule, double* samples, float* scores, char* json,
+                             size_t capacity, size_t* needed);
+/* The same through st_step of a one-stream runtime. */
+int st_replay_scheduled(st_runtime* rt, const float* inputs, size_t count, const st_schedule* schedule,
+                        double* samples, float* scores, char* json, size_t capacity, size_t* needed);
+const char* st_replay_error(void);
+
 /* JSON description of the runtime: options, grid, kernel resources, layout
  * (reference Runtime::info, src/cuda/Runtime.cu:570-594). Writes at most
  * capacity bytes including the terminator; *needed gets the full length. */

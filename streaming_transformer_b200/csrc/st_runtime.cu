@@ -1599,6 +1599,9 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     << ",\"poll_policy\":\"" << (rt->opt.backoff ? "bounded-device-backoff-host-yield" : "tight") << "\""
     << ",\"workspace_storage\":\"FP32 with explicit rounding to the storage type\""
     << ",\"weights_and_kv_storage\":\"" << modes[rt->desc.mode] << "\""
+    << ",\"layers\":" << rt->desc.layers << ",\"width\":" << rt->desc.width << ",\"heads\":" << rt->desc.heads
+    << ",\"ffn\":" << rt->desc.ffn << ",\"window\":" << rt->desc.window << ",\"features\":" << rt->desc.features
+    << ",\"tp_rank\":" << rt->tp_rank << ",\"tp_size\":" << rt->tp_size
     << ",\"streams\":" << rt->desc.streams << ",\"batched\":" << (rt->batched ? "true" : "false")
     << ",\"batched_tensor_cores\":" << (rt->tc ? "true" : "false") << ",\"tc_stages\":" << rt->args.tc_stages
     << ",\"tc_stage_bytes\":" << rt->args.tc_stage_bytes << ",\"tc_tmem_columns\":" << rt->args.tc_ncols

@@ -190,6 +190,61 @@ def transport_bench(mode: str, count: int, backoff: bool = False, device: int = 
     return json.loads(buf.value.decode())
 
 
+class Schedule(ctypes.Structure):
+    """st_schedule: arrivals per second, bursty (groups of 16), queue capacity,
+    deadline (us) and the producer thread's CPU (-1: unpinned)."""
+    _fields_ = [("rate", ctypes.c_double), ("bursty", ctypes.c_int), ("queue", ctypes.c_size_t),
+                ("deadline_us", ctypes.c_double), ("producer_core", ctypes.c_int)]
+
+
+STEP_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_float),
+                           ctypes.POINTER(ctypes.c_float))
+
+
+def _replay_call(call, inputs, rate, bursty, queue, deadline_us, producer_core):
+    """Run call(inputs_ptr, count, schedule, samples, scores, json, capacity,
+    needed) for one of the replay entry points; returns (report, samples, scores)."""
+    lib = library()
+    lib.st_replay_error.restype = ctypes.c_char_p
+    x = np.ascontiguousarray(inputs, dtype=np.float32)
+    count = x.shape[0]
+    sc = Schedule(float(rate), int(bool(bursty)), int(queue), float(deadline_us), int(producer_core))
+    samples = np.zeros((count, 4), dtype=np.float64)
+    scores = np.full(count, np.nan, dtype=np.float32)
+    buf = ctypes.create_string_buffer(1 << 14)
+    need = ctypes.c_size_t(0)
+    code = call(_fptr(x), count, ctypes.byref(sc), samples.ctypes.data_as(ctypes.POINTER(ctypes.c_double)),
+                _fptr(scores), buf, len(buf), ctypes.byref(need))
+    report = json.loads(buf.value.decode()) if buf.value else {}
+    if code != ST_OK:
+        raise StreamError(code, lib.st_replay_error().decode())
+    return report, samples, scores
+
+
+def replay_scheduled_with(step, inputs, rate: float, bursty: bool = False, queue: int = 4096,
+                          deadline_us: float = 1000.0, producer_core: int = -1):
+    """Scheduled-arrival replay through a Python step(event) -> score callable
+    (st_replay_scheduled_with). Returns (report, samples [n][4] ns, scores)."""
+    lib = library()
+    fn = lib.st_replay_scheduled_with
+    fn.restype = ctypes.c_int
+    fn.argtypes = [STEP_FN, ctypes.c_void_p, F, ctypes.c_size_t, ctypes.c_size_t, ctypes.POINTER(Schedule),
+                   ctypes.POINTER(ctypes.c_double), F, ctypes.c_char_p, ctypes.c_size_t,
+                   ctypes.POINTER(ctypes.c_size_t)]
+    features = np.asarray(inputs).shape[1]
+
+    def trampoline(_user, inp, out):
+        try:
+            out[0] = float(step(np.ctypeslib.as_array(inp, shape=(features,)).copy()))
+            return ST_OK
+        except Exception:  # a failing step ends the replay with an error code
+            return -1
+
+    cb = STEP_FN(trampoline)
+    return _replay_call(lambda x, n, *rest: fn(cb, None, x, n, features, *rest), inputs, rate, bursty, queue,
+                        deadline_us, producer_core)
+
+
 def probe(device: int = 0) -> dict:
     """reference probe() (src/cuda/Runtime.cu:134-161, 664)."""
     return _json_call(library().st_probe, device)
@@ -389,6 +444,23 @@ class Runtime:
         _check(library().st_device_trace_continue(self._h, ctypes.c_void_p(device_ptr), int(count),
                                                   ctypes.byref(us), ctypes.byref(launches)), self._h)
         return us.value, int(launches.value)
+
+    def replay_scheduled(self, inputs, rate: float, bursty: bool = False, queue: int = 4096,
+                         deadline_us: float = 1000.0, producer_core: int = -1):
+        """Scheduled-arrival replay of a one-stream trace through st_step
+        (st_replay_scheduled; reference bench/Main.cpp:282-343): events arrive
+        at `rate` per second (bursty: groups of 16) into a queue of `queue`
+        events, dropped when full, and are stepped in order by a native loop.
+        Returns (report, samples [n][4] steady-clock ns: intended, enqueue,
+        submit, complete; scores, NaN where dropped)."""
+        lib = library()
+        fn = lib.st_replay_scheduled
+        fn.restype = ctypes.c_int
+        fn.argtypes = [ctypes.c_void_p, F, ctypes.c_size_t, ctypes.POINTER(Schedule),
+                       ctypes.POINTER(ctypes.c_double), F, ctypes.c_char_p, ctypes.c_size_t,
+                       ctypes.POINTER(ctypes.c_size_t)]
+        return _replay_call(lambda *args: fn(self._h, *args), inputs, rate, bursty, queue, deadline_us,
+                            producer_core)
 
     @property
     def kernel_launches(self) -> int:
