@@ -64,10 +64,24 @@ struct AttSmem {
   float part_acc[kAttWarps][kBatchMaxHeadDim];
 };
 
+// Staged attention (attention_phase_staged): one (stream, head) unit at a
+// time per CTA, its K and V rows in shared memory.
+constexpr int kAttBuffers = 3;                    // K/V staging buffers in flight per CTA
+struct AttStageSmem {
+  float q[kBatchMaxHeadDim];                      // the unit's rotated, cast q, k, v
+  float k[kBatchMaxHeadDim];
+  float v[kBatchMaxHeadDim];
+  float wm[kWarps], wl[kWarps];                   // warp softmax partials of the current chunk
+  float wacc[kWarps][kBatchMaxHeadDim];
+  float um, ul;                                   // the unit's running (max, sum)
+  float uacc[kBatchMaxHeadDim];                   // and value sum
+};
+
 struct BatchSmem {
   float red[kWarps];                              // block reductions (16-byte aligned)
   union {
-    AttSmem att[kAttGroups];                      // attention phase
+    AttSmem att[kAttGroups];                      // attention phase (direct loads)
+    AttStageSmem ast;                             // attention phase (staged)
     float zt[kWarps][kBatchStreams * 8];          // GEMM phases: each warp's stream-input tile
     float xs[kMaxCols];                           // row phases: per-stream input vector
   } u;
@@ -79,6 +93,9 @@ struct BatchSmem {
   unsigned long long tc_tempty;                   // unit's accumulator read (4 epilogue warps)
   unsigned long long tc_done;                     // every MMA issued has completed (teardown)
   unsigned tc_tmem;                               // tensor-memory base address
+  // staged attention
+  unsigned long long att_full[kAttBuffers];       // staging buffer landed (bulk-copy bytes)
+  unsigned long long att_items;                   // staging items this launch so far (buffer, parity)
 };
 constexpr int kTcMaxStages = 8;
 constexpr int kTcProducer = kThreads - 32;        // lane 0 of the last warp: bulk copies
@@ -122,6 +139,16 @@ __device__ __forceinline__ void put_z(const StepArgs& a, int s, int k, int K, fl
 }
 
 // Two consecutive cache elements (K/V rows are 16-byte aligned, dim even).
+template <typename T> __device__ __forceinline__ float2 load2_shared(const T* p);
+template <> __device__ __forceinline__ float2 load2_shared<float>(const float* p) {
+  return *reinterpret_cast<const float2*>(p);
+}
+template <> __device__ __forceinline__ float2 load2_shared<__half>(const __half* p) {
+  return __half22float2(*reinterpret_cast<const __half2*>(p));
+}
+template <> __device__ __forceinline__ float2 load2_shared<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
 template <typename T> __device__ __forceinline__ float2 load2_cg(const T* p);
 template <> __device__ __forceinline__ float2 load2_cg<float>(const float* p) {
   return __ldcg(reinterpret_cast<const float2*>(p));
@@ -529,6 +556,185 @@ __device__ void attention_phase(const StepArgs& a, BatchSmem& sm, int l, unsigne
     attention_unit<T, kTc>(a, sm.u.att[group], group, l, u / a.heads, u % a.heads, event, a.bsplit[0]);
 }
 
+// The attention phase with K/V staged in shared memory. Each CTA walks the
+// (stream, head) units u = blockIdx.x, + gridDim.x, ..., each in chunks of
+// a.att_chunk ring slots ("items"). Thread 0 copies an item's K rows and V
+// rows with cp.async.bulk (this GPU's memory into this CTA's shared memory, no
+// multicast) into one of kAttBuffers buffers of a.att_buf_bytes, completing
+// on the buffer's mbarrier, kAttBuffers - 1 items ahead of the compute, so the
+// copies stream while earlier units are computed. Per item, warp w takes the
+// chunk's slots w, w + 16, ... (lanes over the head dimensions: conflict-free,
+// coalesced shared-memory rows), an online softmax per warp; the warps'
+// partials merge into the unit's running (max, sum, value sum) in warp order;
+// after the unit's last chunk, out = cast(value sum / sum) (reference
+// src/cpu/Cpu.cpp:97-111). Slots at or past the retained window are skipped;
+// the slot this step writes comes from the unit's own k and v.
+template <typename T, bool kTc>
+__device__ void attention_phase_staged(const StepArgs& a, BatchSmem& sm, unsigned char* buf, int l,
+                                       unsigned long long event) {
+  AttStageSmem& as = sm.u.ast;
+  const int hd = a.head_dim, W = a.window, H = a.heads, S = a.streams, d = a.width, M = 3 * d;
+  const int C = a.att_chunk, nch = (W + C - 1) / C;
+  const int units = S * H;
+  const int mine = units > (int)blockIdx.x ? (units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int total = mine * nch;
+  const unsigned long long base = sm.att_items;
+  const unsigned half = a.att_buf_bytes / 2;
+  const int warp = (int)threadIdx.x >> 5, lane = (int)threadIdx.x & 31;
+  const int pairs = hd / 2;
+  constexpr int kPairRegs = kBatchMaxHeadDim / 64;
+  const float rroot = 1.0f / sqrtf((float)hd);
+  bool failed = false;
+  auto issue = [&](int i) {  // thread 0: item i into its buffer
+    const int u = (int)blockIdx.x + (i / nch) * (int)gridDim.x, c = i % nch;
+    const int su = u / H, hu = u - su * H;
+    const size_t head_base = ((((size_t)su * a.layers + l) * H + hu) * (size_t)W) * hd;
+    const int c0 = c * C, n = min(C, W - c0);
+    const int b = (int)((base + (unsigned long long)i) % kAttBuffers);
+    unsigned char* dst = buf + (size_t)b * a.att_buf_bytes;
+    const unsigned bytes = (unsigned)(n * hd * (int)sizeof(T));
+    const unsigned long long pol = policy_evict_first();
+    mbar_expect_tx(&sm.att_full[b], 2 * bytes);
+    bulk_copy(dst, (const T*)a.keys + head_base + (size_t)c0 * hd, bytes, &sm.att_full[b], pol);
+    bulk_copy(dst + half, (const T*)a.values + head_base + (size_t)c0 * hd, bytes, &sm.att_full[b], pol);
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < total && i < kAttBuffers; ++i) issue(i);
+  int s = 0, h = 0, slot = 0, valid = 0;
+  for (int i = 0; i < total; ++i) {
+    const int c = i % nch;
+    if (c == 0) {
+      // the unit's q, k, v: sums of the split partials, cast, RoPE on q and k
+      // (adjacent pairs, angle float(t) * 10000^(-i/hd)), cast, K/V insert at
+      // slot t % W (reference src/cpu/Cpu.cpp:76-89)
+      const int u = (int)blockIdx.x + (i / nch) * (int)gridDim.x;
+      s = u / H;
+      h = u - s * H;
+      const unsigned long long t = __ldcg(a.position + s) + event;
+      slot = (int)(t % (unsigned long long)W);
+      valid = valid_length(t, W);
+      const size_t head_base = ((((size_t)s * a.layers + l) * H + h) * (size_t)W) * hd;
+      const float* P = a.bpart + (size_t)s * M + (size_t)h * 3 * hd;
+      const size_t stride = (size_t)S * M;
+      const float tf = (float)t;
+      for (int p = threadIdx.x; p < 3 * hd / 2; p += kThreads) {
+        const int row = 2 * p, which = row / hd, dim = row - which * hd;
+        float v0 = Storage<T>::round(sum_splits(P + row, a.bsplit[0], stride));
+        float v1 = Storage<T>::round(sum_splits(P + row + 1, a.bsplit[0], stride));
+        if (which < 2) {
+          const float angle = tf * a.rope_freq[dim >> 1];
+          const float co = cosf(angle), sn = sinf(angle);
+          const float r0 = v0 * co - v1 * sn;
+          const float r1 = v0 * sn + v1 * co;
+          v0 = Storage<T>::round(r0);
+          v1 = Storage<T>::round(r1);
+        }
+        float* dst = which == 0 ? as.q : which == 1 ? as.k : as.v;
+        dst[dim] = v0;
+        dst[dim + 1] = v1;
+        if (which > 0) {
+          T* ring = (T*)(which == 1 ? a.keys : a.values) + head_base;
+          Storage<T>::store(ring, (size_t)slot * hd + dim, v0);
+          Storage<T>::store(ring, (size_t)slot * hd + dim + 1, v1);
+        }
+      }
+      if (threadIdx.x == 0) {
+        as.um = -INFINITY;
+        as.ul = 0.f;
+      }
+      for (int e = threadIdx.x; e < hd; e += kThreads) as.uacc[e] = 0.f;
+      __syncthreads();
+    }
+    const unsigned long long g = base + (unsigned long long)i;
+    const int b = (int)(g % kAttBuffers);
+    if (!failed && !mbar_wait_bounded(&sm.att_full[b], (unsigned)((g / kAttBuffers) & 1ull), a.bar_timeout_ns)) {
+      failed = true;
+      if (threadIdx.x == 0) set_error(a, kBarrierTimeout);
+    }
+    const T* Kc = reinterpret_cast<const T*>(buf + (size_t)b * a.att_buf_bytes);
+    const T* Vc = reinterpret_cast<const T*>(buf + (size_t)b * a.att_buf_bytes + half);
+    const int c0 = c * C, n = min(C, W - c0);
+    // this warp's slots of the chunk: online softmax over them
+    float m = -INFINITY, lsum = 0.f;
+    float acc[kPairRegs][2];
+#pragma unroll
+    for (int k = 0; k < kPairRegs; ++k) acc[k][0] = acc[k][1] = 0.f;
+    for (int jj = warp; jj < n && c0 + jj < valid; jj += kWarps) {
+      const int j = c0 + jj;
+      const bool own = j == slot;
+      float dot = 0.f;
+#pragma unroll
+      for (int k = 0; k < kPairRegs; ++k) {
+        const int pi = lane + 32 * k;
+        if (pi < pairs) {
+          const float2 kv = own ? make_float2(as.k[2 * pi], as.k[2 * pi + 1])
+                                : load2_shared<T>(Kc + (size_t)jj * hd + 2 * pi);
+          dot = fmaf(as.q[2 * pi], kv.x, dot);
+          dot = fmaf(as.q[2 * pi + 1], kv.y, dot);
+        }
+      }
+      const float lg = warp_sum(dot) * rroot;
+      const float mn = fmaxf(m, lg);
+      const float sc = expf(m - mn), pj = expf(lg - mn);
+      lsum = fmaf(lsum, sc, pj);
+#pragma unroll
+      for (int k = 0; k < kPairRegs; ++k) {
+        const int pi = lane + 32 * k;
+        if (pi < pairs) {
+          const float2 vv = own ? make_float2(as.v[2 * pi], as.v[2 * pi + 1])
+                                : load2_shared<T>(Vc + (size_t)jj * hd + 2 * pi);
+          acc[k][0] = fmaf(acc[k][0], sc, pj * vv.x);
+          acc[k][1] = fmaf(acc[k][1], sc, pj * vv.y);
+        }
+      }
+      m = mn;
+    }
+    if (lane == 0) {
+      as.wm[warp] = m;
+      as.wl[warp] = lsum;
+    }
+#pragma unroll
+    for (int k = 0; k < kPairRegs; ++k) {
+      const int pi = lane + 32 * k;
+      if (pi < pairs) {
+        as.wacc[warp][2 * pi] = acc[k][0];
+        as.wacc[warp][2 * pi + 1] = acc[k][1];
+      }
+    }
+    __syncthreads();
+    // merge the warps' partials into the unit's state, warps in order
+    float nm = 0.f, nl = 0.f, na = 0.f;
+    const int e = (int)threadIdx.x;
+    if (e < hd) {
+      nm = as.um;
+      for (int w = 0; w < kWarps; ++w)
+        if (as.wl[w] > 0.f) nm = fmaxf(nm, as.wm[w]);
+      const float so = as.ul > 0.f ? expf(as.um - nm) : 0.f;
+      nl = as.ul * so;
+      na = as.uacc[e] * so;
+      for (int w = 0; w < kWarps; ++w) {
+        if (as.wl[w] > 0.f) {
+          const float sw = expf(as.wm[w] - nm);
+          nl = fmaf(as.wl[w], sw, nl);
+          na = fmaf(as.wacc[w][e], sw, na);
+        }
+      }
+    }
+    __syncthreads();  // the buffer and the unit state are read; both may be rewritten
+    if (threadIdx.x == 0) {
+      if (i + kAttBuffers < total) issue(i + kAttBuffers);
+      as.um = nm;
+      as.ul = nl;
+    }
+    if (e < hd) {
+      as.uacc[e] = na;
+      if (c == nch - 1) put_z<T, kTc>(a, s, h * hd + e, d, Storage<T>::round(na / nl));
+    }
+  }
+  // every issued copy was waited for above (or the wait ran out: the error word ends the round)
+  if (threadIdx.x == 0) sm.att_items = base + (unsigned long long)total;
+}
+
 // ---------------------------------------------------------------- tensor-core GEMM phase
 // Per-thread pipeline counters of the roles below; they persist across the
 // GEMM phases, layers and rounds of one launch (every role thread walks the
@@ -702,7 +908,8 @@ __device__ bool round_batched(const StepArgs& a, BatchSmem& sm, unsigned char* s
     const LayerPtrs& w = a.layer[l];
     gemm_any<T, kTc, kViewRows>(a, sm, stages, tr, w.qkv, a.tqkv[l], 3 * d, d, a.bsplit[0]);
     if (!sync(kBtlQkv)) return false;
-    attention_phase<T, kTc>(a, sm, l, event);
+    if (a.att_buf_bytes) attention_phase_staged<T, kTc>(a, sm, stages, l, event);
+    else attention_phase<T, kTc>(a, sm, l, event);
     if (!sync(kBtlAttention)) return false;
     gemm_any<T, kTc, kViewOutHeads>(a, sm, stages, tr, w.out, a.tout[l], d, d, a.bsplit[1]);
     if (!sync(kBtlOut)) return false;
@@ -734,7 +941,13 @@ __device__ void batched_rounds(const StepArgs& a, const float* inputs, unsigned 
                                unsigned long long base) {
   __shared__ BatchSmem sm;
   extern __shared__ __align__(1024) unsigned char tc_stage_smem[];
-  if (threadIdx.x == 0) sm.tl_n = 0;
+  if (threadIdx.x == 0) {
+    sm.tl_n = 0;
+    sm.att_items = 0;
+    for (int b = 0; b < kAttBuffers; ++b) mbar_init(&sm.att_full[b], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
   TcRoles tr;
   if constexpr (kTc) tc_setup(a, sm);
   GridSync gs{base, 0};

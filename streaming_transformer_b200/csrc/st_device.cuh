@@ -121,6 +121,8 @@ struct StepArgs {
   int tc_stages;                      // shared-memory stages of the MMA pipeline
   unsigned tc_stage_bytes;            // bytes per stage: A tile 16 KB + B tile (<= 256 streams x 128 B)
   unsigned tc_ncols;                  // tensor-memory columns allocated (power of two >= 32)
+  unsigned att_buf_bytes;             // staged batched attention: bytes per K/V staging buffer (0: direct loads)
+  int att_chunk;                      // ring slots per staging item (K and V each half a buffer)
 };
 
 // ---------------------------------------------------------------- storage types

@@ -865,6 +865,26 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
                    "cudaFuncSetAttribute rounds") != ST_OK)
         return bail(ST_ERR_CUDA);
     }
+    // Staged attention: kAttBuffers K/V buffers in the round's dynamic shared
+    // memory -- the tensor-core stages (idle during the attention phase) or,
+    // for the CUDA-core round, an allocation of their size. ST_ATT_STAGE=0
+    // selects the direct-load attention phase.
+    {
+      const char* aenv = std::getenv("ST_ATT_STAGE");
+      const size_t dyn = rt->tc ? rt->tc_smem : ((size_t)192 << 10);
+      const unsigned buf = (unsigned)(dyn / kAttBuffers / 1024 * 1024);
+      const int chunk = std::min<int>(m.window, (int)(buf / (2u * (unsigned)hd * (unsigned)rt->elem)));
+      if (chunk >= 16 && !(aenv && aenv[0] == '0')) {
+        rt->args.att_buf_bytes = buf;
+        rt->args.att_chunk = chunk;
+        if (!rt->tc) {
+          rt->tc_smem = dyn;
+          if (rt->cuda(cudaFuncSetAttribute(rounds_fn(rt), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn),
+                       "cudaFuncSetAttribute rounds") != ST_OK)
+            return bail(ST_ERR_CUDA);
+        }
+      }
+    }
     int occ = 0;
     if (rt->cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, rounds_fn(rt), kThreads, rt->tc_smem),
                  "cudaOccupancyMaxActiveBlocksPerMultiprocessor") != ST_OK)
@@ -1605,6 +1625,7 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     << ",\"streams\":" << rt->desc.streams << ",\"batched\":" << (rt->batched ? "true" : "false")
     << ",\"batched_tensor_cores\":" << (rt->tc ? "true" : "false") << ",\"tc_stages\":" << rt->args.tc_stages
     << ",\"tc_stage_bytes\":" << rt->args.tc_stage_bytes << ",\"tc_tmem_columns\":" << rt->args.tc_ncols
+    << ",\"attention_stage_bytes\":" << rt->args.att_buf_bytes << ",\"attention_stage_slots\":" << rt->args.att_chunk
     << ",\"tiled_weights_bytes\":" << rt->tweights_bytes
     << ",\"batched_grid\":" << rt->bgrid << ",\"batched_splits\":[" << rt->bsplit[0] << "," << rt->bsplit[1] << ","
     << rt->bsplit[2] << "," << rt->bsplit[3] << "],\"batched_barriers_per_round\":"
