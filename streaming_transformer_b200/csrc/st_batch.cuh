@@ -64,24 +64,23 @@ struct AttSmem {
   float part_acc[kAttWarps][kBatchMaxHeadDim];
 };
 
-// Staged attention (attention_phase_staged): one (stream, head) unit at a
-// time per CTA, its K and V rows in shared memory.
-constexpr int kAttBuffers = 3;                    // K/V staging buffers in flight per CTA
-struct AttStageSmem {
-  float q[kBatchMaxHeadDim];                      // the unit's rotated, cast q, k, v
-  float k[kBatchMaxHeadDim];
-  float v[kBatchMaxHeadDim];
-  float wm[kWarps], wl[kWarps];                   // warp softmax partials of the current chunk
-  float wacc[kWarps][kBatchMaxHeadDim];
-  float um, ul;                                   // the unit's running (max, sum)
-  float uacc[kBatchMaxHeadDim];                   // and value sum
-};
+// Staged attention (attention_phase_staged): each warp walks whole (stream,
+// head) units through its own ring of K/V stages in dynamic shared memory.
+constexpr int kAttMaxStages = 8;                  // stages per warp at most (cp.async groups pending <= 7)
+constexpr int kAttMaxChunk = 16;                  // ring slots per stage at most
+
+// Bytes of the staged attention's q/k/v table for `units` units of head_dim
+// hd: the final q, k, v rows (fp32), then each unit's {slot, valid}; the
+// stages start at the next 128-byte boundary (host and device).
+__host__ __device__ inline unsigned att_table_bytes(int units, int hd) {
+  const unsigned rows = ((unsigned)units * 3u * (unsigned)hd * 4u + 15u) / 16u * 16u;
+  return (rows + (unsigned)units * 8u + 127u) / 128u * 128u;
+}
 
 struct BatchSmem {
   float red[kWarps];                              // block reductions (16-byte aligned)
   union {
     AttSmem att[kAttGroups];                      // attention phase (direct loads)
-    AttStageSmem ast;                             // attention phase (staged)
     float zt[kWarps][kBatchStreams * 8];          // GEMM phases: each warp's stream-input tile
     float xs[kMaxCols];                           // row phases: per-stream input vector
   } u;
@@ -93,9 +92,6 @@ struct BatchSmem {
   unsigned long long tc_tempty;                   // unit's accumulator read (4 epilogue warps)
   unsigned long long tc_done;                     // every MMA issued has completed (teardown)
   unsigned tc_tmem;                               // tensor-memory base address
-  // staged attention
-  unsigned long long att_full[kAttBuffers];       // staging buffer landed (bulk-copy bytes)
-  unsigned long long att_items;                   // staging items this launch so far (buffer, parity)
 };
 constexpr int kTcMaxStages = 8;
 constexpr int kTcProducer = kThreads - 32;        // lane 0 of the last warp: bulk copies
@@ -107,7 +103,8 @@ constexpr int kTcMaxN = 256;                      // streams per MMA (N)
 // every phase end and barrier exit (warp 0's row of the timeline buffer).
 enum BatchTag : int {
   kBtlInput = 40, kBtlQkv = 41, kBtlAttention = 42, kBtlOut = 43, kBtlResidual2 = 44, kBtlGateUp = 45,
-  kBtlSwiglu = 46, kBtlDown = 47, kBtlResidual1 = 48, kBtlSync = 49
+  kBtlSwiglu = 46, kBtlDown = 47, kBtlResidual1 = 48, kBtlSync = 49,
+  kBtlAttPrepare = 50
 };
 __device__ __forceinline__ void btl(const StepArgs& a, BatchSmem& sm, int tag) {
   if (a.timeline && blockIdx.x == a.timeline_cta && threadIdx.x == 0 && sm.tl_n < a.timeline_capacity / kWarps)
@@ -556,183 +553,405 @@ __device__ void attention_phase(const StepArgs& a, BatchSmem& sm, int l, unsigne
     attention_unit<T, kTc>(a, sm.u.att[group], group, l, u / a.heads, u % a.heads, event, a.bsplit[0]);
 }
 
-// The attention phase with K/V staged in shared memory. Each CTA walks the
-// (stream, head) units u = blockIdx.x, + gridDim.x, ..., each in chunks of
-// a.att_chunk ring slots ("items"). Thread 0 copies an item's K rows and V
-// rows with cp.async.bulk (this GPU's memory into this CTA's shared memory, no
-// multicast) into one of kAttBuffers buffers of a.att_buf_bytes, completing
-// on the buffer's mbarrier, kAttBuffers - 1 items ahead of the compute, so the
-// copies stream while earlier units are computed. Per item, warp w takes the
-// chunk's slots w, w + 16, ... (lanes over the head dimensions: conflict-free,
-// coalesced shared-memory rows), an online softmax per warp; the warps'
-// partials merge into the unit's running (max, sum, value sum) in warp order;
-// after the unit's last chunk, out = cast(value sum / sum) (reference
-// src/cpu/Cpu.cpp:97-111). Slots at or past the retained window are skipped;
-// the slot this step writes comes from the unit's own k and v.
+// The attention phase with K/V staged in shared memory, one warp per unit.
+// The CTA owns a contiguous range of (stream, head) units u = lo + k
+// (k < mine; consecutive units are adjacent K/V regions, so a CTA's reads stay
+// within a few pages); warp w takes k = w, w + kWarps, ... and walks each unit's ring
+// in chunks of C = a.att_chunk slots through its own a.att_stages stages.
+//  * The warp's lanes copy a chunk's K rows and V rows into its next stage
+//    with 16-byte cp.async (one commit group per chunk), a.att_stages - 1
+//    chunks ahead of the compute; a chunk is read after its group completes
+//    and a warp barrier. (One bulk copy per chunk would cost the copy engine
+//    a request per 1-2 KB: measured slower at these chunk sizes.) Every chunk
+//    of the window is copied; chunks past the retained slots are skipped.
+//  * First, all threads finish every owned unit's q, k, v at once: sums of the
+//    K-split partials, cast, RoPE on q and k (adjacent pairs, angle float(t) *
+//    10000^(-i/hd)), cast, K/V insert at slot t % W (reference
+//    src/cpu/Cpu.cpp:76-89), into a shared-memory table with each unit's
+//    {slot, valid}.
+//  * Per chunk, G = 32 / C lanes take each slot: a lane's dimension pairs are
+//    rotated by its slot so the row reads hit distinct banks; the key dot sums
+//    over the slot's lanes; the warp's online softmax takes the chunk; the
+//    value rows accumulate with lanes over dimension pairs. After the unit's
+//    last chunk, out = cast(value sum / sum) (reference src/cpu/Cpu.cpp:97-111).
+// The slot this step writes comes from the unit's own k and v in the table,
+// whatever its staged copy holds. No block barrier inside the unit loop.
 template <typename T, bool kTc>
-__device__ void attention_phase_staged(const StepArgs& a, BatchSmem& sm, unsigned char* buf, int l,
+__device__ void attention_phase_staged(const StepArgs& a, BatchSmem& sm, unsigned char* dyn, int l,
                                        unsigned long long event) {
-  AttStageSmem& as = sm.u.ast;
   const int hd = a.head_dim, W = a.window, H = a.heads, S = a.streams, d = a.width, M = 3 * d;
-  const int C = a.att_chunk, nch = (W + C - 1) / C;
-  const int units = S * H;
-  const int mine = units > (int)blockIdx.x ? (units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int total = mine * nch;
-  const unsigned long long base = sm.att_items;
-  const unsigned half = a.att_buf_bytes / 2;
+  const int C = a.att_chunk, NB = a.att_stages, nch = (W + C - 1) / C;
+  int lo, hi;
+  split(S * H, (int)blockIdx.x, (int)gridDim.x, lo, hi);
+  const int mine = hi - lo;
+  if (mine <= 0) return;
+  if (att_table_bytes(mine, hd) > a.att_table_bytes) {  // the host sized the table for this grid
+    if (threadIdx.x == 0) set_error(a, kClusterShape);
+    return;
+  }
   const int warp = (int)threadIdx.x >> 5, lane = (int)threadIdx.x & 31;
+  const int rowf = 3 * hd;
+  float* table = reinterpret_cast<float*>(dyn);
+  int2* meta = reinterpret_cast<int2*>(dyn + ((unsigned)mine * (unsigned)rowf * 4u + 15u) / 16u * 16u);
+  unsigned char* stages = dyn + a.att_table_bytes;
+  const unsigned sbytes = a.att_buf_bytes, half = sbytes / 2;
+  const int nu = mine > warp ? (mine - 1 - warp) / kWarps + 1 : 0;
+  const int total = nu * nch;
+  auto unit_of = [&](int k) { return lo + k; };
+  auto issue = [&](int i) {  // every lane: its 16-byte pieces of chunk i into stage i % NB, one group
+    if (i < total) {
+      const int u = unit_of(warp + (i / nch) * kWarps), c = i % nch;
+      const int su = u / H, hu = u - su * H;
+      const size_t head_base = ((((size_t)su * a.layers + l) * H + hu) * (size_t)W) * hd;
+      const int c0 = c * C, n = min(C, W - c0);
+      unsigned char* dst = stages + (size_t)(warp * NB + i % NB) * sbytes;
+      const unsigned char* ks = reinterpret_cast<const unsigned char*>((const T*)a.keys + head_base + (size_t)c0 * hd);
+      const unsigned char* vs = reinterpret_cast<const unsigned char*>((const T*)a.values + head_base + (size_t)c0 * hd);
+      const unsigned bytes = (unsigned)(n * hd * (int)sizeof(T));
+      for (unsigned o = (unsigned)lane * 16u; o < bytes; o += 512u) {
+        cp_async16(dst + o, ks + o);
+        cp_async16(dst + half + o, vs + o);
+      }
+    }
+    cp_async_commit();  // empty past the last chunk: the group count stays uniform
+  };
+  for (int i = 0; i < NB - 1; ++i) issue(i);
+  // every owned unit's final q, k, v (and the K/V insert), all units at once
+  const int per_unit = 3 * hd / 2;
+  for (int x = threadIdx.x; x < mine * per_unit; x += kThreads) {
+    const int k = x / per_unit, p = x - k * per_unit;
+    const int u = unit_of(k), su = u / H, hu = u - su * H;
+    const unsigned long long t = __ldcg(a.position + su) + event;
+    const int row = 2 * p, which = row / hd, dim = row - which * hd;
+    const float* P = a.bpart + (size_t)su * M + (size_t)hu * 3 * hd + row;
+    float v0 = Storage<T>::round(sum_splits(P, a.bsplit[0], (size_t)S * M));
+    float v1 = Storage<T>::round(sum_splits(P + 1, a.bsplit[0], (size_t)S * M));
+    if (which < 2) {
+      const float angle = (float)t * a.rope_freq[dim >> 1];
+      const float co = cosf(angle), sn = sinf(angle);
+      const float r0 = v0 * co - v1 * sn;
+      const float r1 = v0 * sn + v1 * co;
+      v0 = Storage<T>::round(r0);
+      v1 = Storage<T>::round(r1);
+    }
+    table[(size_t)k * rowf + row] = v0;
+    table[(size_t)k * rowf + row + 1] = v1;
+    const int slot = (int)(t % (unsigned long long)W);
+    if (p == 0) meta[k] = make_int2(slot, valid_length(t, W));
+    if (which > 0) {
+      const size_t head_base = ((((size_t)su * a.layers + l) * H + hu) * (size_t)W) * hd;
+      T* ring = (T*)(which == 1 ? a.keys : a.values) + head_base;
+      Storage<T>::store(ring, (size_t)slot * hd + dim, v0);
+      Storage<T>::store(ring, (size_t)slot * hd + dim + 1, v1);
+    }
+  }
+  __syncthreads();
+  btl(a, sm, kBtlAttPrepare);
   const int pairs = hd / 2;
   constexpr int kPairRegs = kBatchMaxHeadDim / 64;
   const float rroot = 1.0f / sqrtf((float)hd);
-  bool failed = false;
-  auto issue = [&](int i) {  // thread 0: item i into its buffer
-    const int u = (int)blockIdx.x + (i / nch) * (int)gridDim.x, c = i % nch;
-    const int su = u / H, hu = u - su * H;
-    const size_t head_base = ((((size_t)su * a.layers + l) * H + hu) * (size_t)W) * hd;
-    const int c0 = c * C, n = min(C, W - c0);
-    const int b = (int)((base + (unsigned long long)i) % kAttBuffers);
-    unsigned char* dst = buf + (size_t)b * a.att_buf_bytes;
-    const unsigned bytes = (unsigned)(n * hd * (int)sizeof(T));
-    const unsigned long long pol = policy_evict_first();
-    mbar_expect_tx(&sm.att_full[b], 2 * bytes);
-    bulk_copy(dst, (const T*)a.keys + head_base + (size_t)c0 * hd, bytes, &sm.att_full[b], pol);
-    bulk_copy(dst + half, (const T*)a.values + head_base + (size_t)c0 * hd, bytes, &sm.att_full[b], pol);
-  };
-  if (threadIdx.x == 0)
-    for (int i = 0; i < total && i < kAttBuffers; ++i) issue(i);
+  const int G = 32 / C;                      // lanes per slot (C is a power of two <= 16)
+  const int nq = (pairs + G - 1) / G;        // dimension pairs per lane in the key dot
+  const int g = lane / G, r = lane - g * G;  // this lane's slot in the chunk and its part
+  const int rot = g % nq;                    // the slot's first dimension pair (bank rotation)
   int s = 0, h = 0, slot = 0, valid = 0;
+  const float* qrow = table;
+  float m = -INFINITY, lsum = 0.f;
+  float acc[kPairRegs][2];
   for (int i = 0; i < total; ++i) {
-    const int c = i % nch;
+    const int c = i % nch, k = warp + (i / nch) * kWarps;
     if (c == 0) {
-      // the unit's q, k, v: sums of the split partials, cast, RoPE on q and k
-      // (adjacent pairs, angle float(t) * 10000^(-i/hd)), cast, K/V insert at
-      // slot t % W (reference src/cpu/Cpu.cpp:76-89)
-      const int u = (int)blockIdx.x + (i / nch) * (int)gridDim.x;
+      const int u = unit_of(k);
       s = u / H;
       h = u - s * H;
-      const unsigned long long t = __ldcg(a.position + s) + event;
-      slot = (int)(t % (unsigned long long)W);
-      valid = valid_length(t, W);
-      const size_t head_base = ((((size_t)s * a.layers + l) * H + h) * (size_t)W) * hd;
-      const float* P = a.bpart + (size_t)s * M + (size_t)h * 3 * hd;
-      const size_t stride = (size_t)S * M;
-      const float tf = (float)t;
-      for (int p = threadIdx.x; p < 3 * hd / 2; p += kThreads) {
-        const int row = 2 * p, which = row / hd, dim = row - which * hd;
-        float v0 = Storage<T>::round(sum_splits(P + row, a.bsplit[0], stride));
-        float v1 = Storage<T>::round(sum_splits(P + row + 1, a.bsplit[0], stride));
-        if (which < 2) {
-          const float angle = tf * a.rope_freq[dim >> 1];
-          const float co = cosf(angle), sn = sinf(angle);
-          const float r0 = v0 * co - v1 * sn;
-          const float r1 = v0 * sn + v1 * co;
-          v0 = Storage<T>::round(r0);
-          v1 = Storage<T>::round(r1);
-        }
-        float* dst = which == 0 ? as.q : which == 1 ? as.k : as.v;
-        dst[dim] = v0;
-        dst[dim + 1] = v1;
-        if (which > 0) {
-          T* ring = (T*)(which == 1 ? a.keys : a.values) + head_base;
-          Storage<T>::store(ring, (size_t)slot * hd + dim, v0);
-          Storage<T>::store(ring, (size_t)slot * hd + dim + 1, v1);
-        }
-      }
-      if (threadIdx.x == 0) {
-        as.um = -INFINITY;
-        as.ul = 0.f;
-      }
-      for (int e = threadIdx.x; e < hd; e += kThreads) as.uacc[e] = 0.f;
-      __syncthreads();
-    }
-    const unsigned long long g = base + (unsigned long long)i;
-    const int b = (int)(g % kAttBuffers);
-    if (!failed && !mbar_wait_bounded(&sm.att_full[b], (unsigned)((g / kAttBuffers) & 1ull), a.bar_timeout_ns)) {
-      failed = true;
-      if (threadIdx.x == 0) set_error(a, kBarrierTimeout);
-    }
-    const T* Kc = reinterpret_cast<const T*>(buf + (size_t)b * a.att_buf_bytes);
-    const T* Vc = reinterpret_cast<const T*>(buf + (size_t)b * a.att_buf_bytes + half);
-    const int c0 = c * C, n = min(C, W - c0);
-    // this warp's slots of the chunk: online softmax over them
-    float m = -INFINITY, lsum = 0.f;
-    float acc[kPairRegs][2];
+      const int2 mt = meta[k];
+      slot = mt.x;
+      valid = mt.y;
+      qrow = table + (size_t)k * rowf;
+      m = -INFINITY;
+      lsum = 0.f;
 #pragma unroll
-    for (int k = 0; k < kPairRegs; ++k) acc[k][0] = acc[k][1] = 0.f;
-    for (int jj = warp; jj < n && c0 + jj < valid; jj += kWarps) {
-      const int j = c0 + jj;
-      const bool own = j == slot;
+      for (int e = 0; e < kPairRegs; ++e) acc[e][0] = acc[e][1] = 0.f;
+    }
+    issue(i + NB - 1);  // into the stage chunk i - 1 used (read before the warp barrier below)
+    cp_async_wait_pending(NB - 1);  // chunk i's group is complete
+    __syncwarp();
+    const int b = i % NB;
+    const T* Kc = reinterpret_cast<const T*>(stages + (size_t)(warp * NB + b) * sbytes);
+    const T* Vc = reinterpret_cast<const T*>(stages + (size_t)(warp * NB + b) * sbytes + half);
+    const int c0 = c * C, n = min(min(C, W - c0), valid - c0);  // retained slots of this chunk
+    if (n > 0) {
+      const bool ok = g < n;
       float dot = 0.f;
-#pragma unroll
-      for (int k = 0; k < kPairRegs; ++k) {
-        const int pi = lane + 32 * k;
-        if (pi < pairs) {
-          const float2 kv = own ? make_float2(as.k[2 * pi], as.k[2 * pi + 1])
-                                : load2_shared<T>(Kc + (size_t)jj * hd + 2 * pi);
-          dot = fmaf(as.q[2 * pi], kv.x, dot);
-          dot = fmaf(as.q[2 * pi + 1], kv.y, dot);
+      if (ok) {
+        const bool own = c0 + g == slot;
+        const T* krow = Kc + (size_t)g * hd;
+        const float* kown = qrow + hd;
+        for (int e = 0; e < nq; ++e) {
+          int qq = e + rot;
+          qq -= (qq >= nq) ? nq : 0;
+          const int p = r + G * qq;
+          if (p < pairs) {
+            const float2 kv = own ? *reinterpret_cast<const float2*>(kown + 2 * p) : load2_shared<T>(krow + 2 * p);
+            const float2 qv = *reinterpret_cast<const float2*>(qrow + 2 * p);
+            dot = fmaf(qv.x, kv.x, dot);
+            dot = fmaf(qv.y, kv.y, dot);
+          }
         }
       }
-      const float lg = warp_sum(dot) * rroot;
-      const float mn = fmaxf(m, lg);
-      const float sc = expf(m - mn), pj = expf(lg - mn);
-      lsum = fmaf(lsum, sc, pj);
+      for (int o = 1; o < G; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      const float lg = ok ? dot * rroot : -INFINITY;
+      float mx = lg;
+      for (int o = G; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mn = fmaxf(m, mx);  // finite: the chunk's first slot is retained
+      const float sc = expf(m - mn);
+      const float pj = ok ? expf(lg - mn) : 0.f;
+      float ps = pj;
+      for (int o = G; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      lsum = fmaf(lsum, sc, ps);
+      const float* vown = qrow + 2 * hd;
 #pragma unroll
-      for (int k = 0; k < kPairRegs; ++k) {
-        const int pi = lane + 32 * k;
-        if (pi < pairs) {
-          const float2 vv = own ? make_float2(as.v[2 * pi], as.v[2 * pi + 1])
-                                : load2_shared<T>(Vc + (size_t)jj * hd + 2 * pi);
-          acc[k][0] = fmaf(acc[k][0], sc, pj * vv.x);
-          acc[k][1] = fmaf(acc[k][1], sc, pj * vv.y);
+      for (int e = 0; e < kPairRegs; ++e) {
+        acc[e][0] *= sc;
+        acc[e][1] *= sc;
+      }
+#pragma unroll 4
+      for (int x = 0; x < n; ++x) {
+        const float px = __shfl_sync(0xffffffffu, pj, x * G);
+        const bool own = c0 + x == slot;
+        const T* vrow = Vc + (size_t)x * hd;
+#pragma unroll
+        for (int e = 0; e < kPairRegs; ++e) {
+          const int pi = lane + 32 * e;
+          if (pi < pairs) {
+            const float2 vv = own ? *reinterpret_cast<const float2*>(vown + 2 * pi) : load2_shared<T>(vrow + 2 * pi);
+            acc[e][0] = fmaf(px, vv.x, acc[e][0]);
+            acc[e][1] = fmaf(px, vv.y, acc[e][1]);
+          }
         }
       }
       m = mn;
     }
-    if (lane == 0) {
-      as.wm[warp] = m;
-      as.wl[warp] = lsum;
-    }
+    __syncwarp();  // the stage is read: the next issue may refill it
+    if (c == nch - 1) {
 #pragma unroll
-    for (int k = 0; k < kPairRegs; ++k) {
-      const int pi = lane + 32 * k;
-      if (pi < pairs) {
-        as.wacc[warp][2 * pi] = acc[k][0];
-        as.wacc[warp][2 * pi + 1] = acc[k][1];
-      }
-    }
-    __syncthreads();
-    // merge the warps' partials into the unit's state, warps in order
-    float nm = 0.f, nl = 0.f, na = 0.f;
-    const int e = (int)threadIdx.x;
-    if (e < hd) {
-      nm = as.um;
-      for (int w = 0; w < kWarps; ++w)
-        if (as.wl[w] > 0.f) nm = fmaxf(nm, as.wm[w]);
-      const float so = as.ul > 0.f ? expf(as.um - nm) : 0.f;
-      nl = as.ul * so;
-      na = as.uacc[e] * so;
-      for (int w = 0; w < kWarps; ++w) {
-        if (as.wl[w] > 0.f) {
-          const float sw = expf(as.wm[w] - nm);
-          nl = fmaf(as.wl[w], sw, nl);
-          na = fmaf(as.wacc[w][e], sw, na);
+      for (int e = 0; e < kPairRegs; ++e) {
+        const int pi = lane + 32 * e;
+        if (pi < pairs) {
+          put_z<T, kTc>(a, s, h * hd + 2 * pi, d, Storage<T>::round(acc[e][0] / lsum));
+          put_z<T, kTc>(a, s, h * hd + 2 * pi + 1, d, Storage<T>::round(acc[e][1] / lsum));
         }
       }
     }
-    __syncthreads();  // the buffer and the unit state are read; both may be rewritten
-    if (threadIdx.x == 0) {
-      if (i + kAttBuffers < total) issue(i + kAttBuffers);
-      as.um = nm;
-      as.ul = nl;
+  }
+  // every chunk's group was waited for above; later groups are empty
+}
+
+// Head dimension 64 (every benchmark shape): the same per-warp walk as
+// attention_phase_staged, with 16-byte shared-memory reads throughout.
+//  * A row is kNch 16-byte pieces (8 for 16-bit storage, 16 for fp32). A
+//    chunk holds kC = 32 / kG slots; kG lanes take each slot's key dot, two
+//    pieces per lane, with this lane's q pieces held in registers.
+//  * 16-bit rows are stored with piece p of row j at p ^ (4 (j & 1)), so the
+//    8 lanes of a quarter-warp (two slots, pieces 0-3 or 4-7) read 8 distinct
+//    bank groups; fp32 quarter-warps read one row's 8 consecutive pieces.
+//  * Value rows: lane (y, c) accumulates piece c of slots y, y + kY, ... into
+//    kVec partial sums; the kY slot groups are summed once per unit.
+//  * The chunk copies start after the q/k/v inserts and a block barrier
+//    (cp.async reads are ordered after it), so the staged rows include the
+//    slot this step writes.
+template <typename T>
+struct Att64 {
+  static constexpr int kVec = Storage<T>::kVec;       // elements per 16-byte piece
+  static constexpr int kNch = 64 / kVec;              // pieces per row
+  static constexpr int kG = sizeof(T) == 2 ? 4 : 8;   // lanes per slot in the key dot
+  static constexpr int kC = 32 / kG;                  // slots per chunk
+  static constexpr int kY = 32 / kNch;                // slot groups in the value sums
+  static constexpr unsigned kRowBytes = 64u * sizeof(T);
+  __device__ static int swz(int row) { return sizeof(T) == 2 ? ((row & 1) << 2) : 0; }
+};
+
+template <typename T, bool kTc>
+__device__ void attention_phase_hd64(const StepArgs& a, BatchSmem& sm, unsigned char* dyn, int l,
+                                     unsigned long long event) {
+  using A = Att64<T>;
+  constexpr int E = A::kVec, NCH = A::kNch, G = A::kG, C = A::kC, Y = A::kY;
+  const int W = a.window, H = a.heads, S = a.streams, d = a.width, M = 3 * d;
+  const int NB = a.att_stages, nch = (W + C - 1) / C;
+  int lo, hi;
+  split(S * H, (int)blockIdx.x, (int)gridDim.x, lo, hi);
+  const int mine = hi - lo;
+  if (mine <= 0) return;
+  if (att_table_bytes(mine, 64) > a.att_table_bytes || a.att_chunk != C) {  // the host sized both
+    if (threadIdx.x == 0) set_error(a, kClusterShape);
+    return;
+  }
+  const int warp = (int)threadIdx.x >> 5, lane = (int)threadIdx.x & 31;
+  constexpr int rowf = 3 * 64;
+  float* table = reinterpret_cast<float*>(dyn);
+  int2* meta = reinterpret_cast<int2*>(dyn + ((unsigned)mine * (unsigned)rowf * 4u + 15u) / 16u * 16u);
+  unsigned char* stages = dyn + a.att_table_bytes;
+  const unsigned sbytes = a.att_buf_bytes, half = sbytes / 2;
+  const int nu = mine > warp ? (mine - 1 - warp) / kWarps + 1 : 0;
+  const int total = nu * nch;
+  const size_t head_stride = (size_t)W * 64;  // elements per (stream, layer, head) ring
+  auto ring_base = [&](int k) {               // element offset of owned unit k's ring in layer l
+    const int u = lo + k, su = u / H, hu = u - su * H;
+    return (((size_t)su * a.layers + l) * H + hu) * head_stride;
+  };
+  // issue state: the next chunk to copy (unit k_i of this warp's list, chunk c_i)
+  int ik = warp, ic = 0, issued = 0;
+  size_t ibase = nu > 0 ? ring_base(warp) : 0;
+  auto issue = [&]() {  // every lane: its pieces of the next chunk into stage issued % NB, one group
+    if (issued < total) {
+      unsigned char* dst = stages + (size_t)(warp * NB + issued % NB) * sbytes;
+      const int c0 = ic * C, n = min(C, W - c0);
+      const unsigned char* ks = reinterpret_cast<const unsigned char*>((const T*)a.keys + ibase + (size_t)c0 * 64);
+      const unsigned char* vs = reinterpret_cast<const unsigned char*>((const T*)a.values + ibase + (size_t)c0 * 64);
+      for (int q = lane; q < n * NCH; q += 32) {
+        const int row = q / NCH, pc = q - row * NCH;
+        const unsigned so = (unsigned)row * A::kRowBytes + (unsigned)pc * 16u;
+        const unsigned dp = (unsigned)row * A::kRowBytes + (unsigned)(pc ^ A::swz(row)) * 16u;
+        cp_async16(dst + dp, ks + so);
+        cp_async16(dst + half + dp, vs + so);
+      }
+      ++issued;
+      if (++ic == nch) {
+        ic = 0;
+        ik += kWarps;
+        if (ik < mine) ibase = ring_base(ik);
+      }
     }
-    if (e < hd) {
-      as.uacc[e] = na;
-      if (c == nch - 1) put_z<T, kTc>(a, s, h * hd + e, d, Storage<T>::round(na / nl));
+    cp_async_commit();  // empty past the last chunk: the group count stays uniform
+  };
+  // every owned unit's final q, k, v (and the K/V insert), all units at once
+  constexpr int per_unit = 3 * 64 / 2;
+  for (int x = threadIdx.x; x < mine * per_unit; x += kThreads) {
+    const int k = x / per_unit, p = x - k * per_unit;
+    const int u = lo + k, su = u / H, hu = u - su * H;
+    const unsigned long long t = __ldcg(a.position + su) + event;
+    const int row = 2 * p, which = row >> 6, dim = row & 63;
+    const float* P = a.bpart + (size_t)su * M + (size_t)hu * rowf + row;
+    float v0 = Storage<T>::round(sum_splits(P, a.bsplit[0], (size_t)S * M));
+    float v1 = Storage<T>::round(sum_splits(P + 1, a.bsplit[0], (size_t)S * M));
+    if (which < 2) {
+      const float angle = (float)t * a.rope_freq[dim >> 1];
+      const float co = cosf(angle), sn = sinf(angle);
+      const float r0 = v0 * co - v1 * sn;
+      const float r1 = v0 * sn + v1 * co;
+      v0 = Storage<T>::round(r0);
+      v1 = Storage<T>::round(r1);
+    }
+    table[(size_t)k * rowf + row] = v0;
+    table[(size_t)k * rowf + row + 1] = v1;
+    const int slot = (int)(t % (unsigned long long)W);
+    if (p == 0) meta[k] = make_int2(slot, valid_length(t, W));
+    if (which > 0) {
+      T* ring = (T*)(which == 1 ? a.keys : a.values) + ring_base(k);
+      Storage<T>::store(ring, (size_t)slot * 64 + dim, v0);
+      Storage<T>::store(ring, (size_t)slot * 64 + dim + 1, v1);
     }
   }
-  // every issued copy was waited for above (or the wait ran out: the error word ends the round)
-  if (threadIdx.x == 0) sm.att_items = base + (unsigned long long)total;
+  __syncthreads();  // the inserts are in the ring before any chunk is copied
+  btl(a, sm, kBtlAttPrepare);
+  for (int i = 0; i < NB - 1; ++i) issue();
+  const float rroot = 0.125f;                 // 1 / sqrt(64)
+  const int g = lane / G, r = lane - g * G;   // key dot: slot g of the chunk, pieces r and r + G
+  const int vy = lane / NCH, vc = lane - vy * NCH;  // value sums: slot group vy, piece vc
+  int k = warp, c = 0, s = 0, h = 0, valid = 0;
+  const float* qrow = table;
+  float qv[2][E];
+  float m = -INFINITY, lsum = 0.f;
+  float acc[E];
+  for (int i = 0; i < total; ++i) {
+    if (c == 0) {
+      const int u = lo + k;
+      s = u / H;
+      h = u - s * H;
+      valid = meta[k].y;
+      qrow = table + (size_t)k * rowf;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < E; e += 4) {
+          const float4 f = *reinterpret_cast<const float4*>(qrow + (r + G * j) * E + e);
+          qv[j][e] = f.x;
+          qv[j][e + 1] = f.y;
+          qv[j][e + 2] = f.z;
+          qv[j][e + 3] = f.w;
+        }
+      m = -INFINITY;
+      lsum = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] = 0.f;
+    }
+    issue();                        // into the stage chunk i - 1 used (read before the warp barrier below)
+    cp_async_wait_pending(NB - 1);  // chunk i's group is complete
+    __syncwarp();
+    const unsigned char* Kc = stages + (size_t)(warp * NB + i % NB) * sbytes;
+    const unsigned char* Vc = Kc + half;
+    const int c0 = c * C, n = min(min(C, W - c0), valid - c0);  // retained slots of this chunk
+    if (n > 0) {
+      const bool ok = g < n;
+      float dot = 0.f;
+      if (ok) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int pc = r + G * j;
+          float kf[E];
+          const uint4 w = *reinterpret_cast<const uint4*>(Kc + (unsigned)g * A::kRowBytes +
+                                                          (unsigned)(pc ^ A::swz(g)) * 16u);
+          Storage<T>::unpack(w, kf);
+#pragma unroll
+          for (int e = 0; e < E; ++e) dot = fmaf(qv[j][e], kf[e], dot);
+        }
+      }
+#pragma unroll
+      for (int o = 1; o < G; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      const float lg = ok ? dot * rroot : -INFINITY;
+      float mx = lg;
+#pragma unroll
+      for (int o = G; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mn = fmaxf(m, mx);  // finite: the chunk's first slot is retained
+      const float sc = expf(m - mn);
+      const float pj = ok ? expf(lg - mn) : 0.f;
+      float ps = pj;
+#pragma unroll
+      for (int o = G; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      lsum = fmaf(lsum, sc, ps);
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] *= sc;
+#pragma unroll
+      for (int x0 = 0; x0 < C; x0 += Y) {
+        const int x = x0 + vy;
+        const float px = __shfl_sync(0xffffffffu, pj, x * G);  // 0 past the retained slots
+        if (x < n) {
+          float vf[E];
+          const uint4 w = *reinterpret_cast<const uint4*>(Vc + (unsigned)x * A::kRowBytes +
+                                                          (unsigned)(vc ^ A::swz(x)) * 16u);
+          Storage<T>::unpack(w, vf);
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[e] = fmaf(px, vf[e], acc[e]);
+        }
+      }
+      m = mn;
+    }
+    __syncwarp();  // the stage is read: the next issue may refill it
+    if (++c == nch) {
+      // the unit's value sums over the slot groups, in a fixed order
+#pragma unroll
+      for (int o = NCH; o < 32; o <<= 1)
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+      if (vy == 0) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) put_z<T, kTc>(a, s, h * 64 + vc * E + e, d, Storage<T>::round(acc[e] / lsum));
+      }
+      c = 0;
+      k += kWarps;
+    }
+  }
+  // every chunk's group was waited for above; later groups are empty
 }
 
 // ---------------------------------------------------------------- tensor-core GEMM phase
@@ -908,7 +1127,8 @@ __device__ bool round_batched(const StepArgs& a, BatchSmem& sm, unsigned char* s
     const LayerPtrs& w = a.layer[l];
     gemm_any<T, kTc, kViewRows>(a, sm, stages, tr, w.qkv, a.tqkv[l], 3 * d, d, a.bsplit[0]);
     if (!sync(kBtlQkv)) return false;
-    if (a.att_buf_bytes) attention_phase_staged<T, kTc>(a, sm, stages, l, event);
+    if (a.att_buf_bytes && a.head_dim == 64) attention_phase_hd64<T, kTc>(a, sm, stages, l, event);
+    else if (a.att_buf_bytes) attention_phase_staged<T, kTc>(a, sm, stages, l, event);
     else attention_phase<T, kTc>(a, sm, l, event);
     if (!sync(kBtlAttention)) return false;
     gemm_any<T, kTc, kViewOutHeads>(a, sm, stages, tr, w.out, a.tout[l], d, d, a.bsplit[1]);
@@ -941,12 +1161,7 @@ __device__ void batched_rounds(const StepArgs& a, const float* inputs, unsigned 
                                unsigned long long base) {
   __shared__ BatchSmem sm;
   extern __shared__ __align__(1024) unsigned char tc_stage_smem[];
-  if (threadIdx.x == 0) {
-    sm.tl_n = 0;
-    sm.att_items = 0;
-    for (int b = 0; b < kAttBuffers; ++b) mbar_init(&sm.att_full[b], 1);
-    fence_mbar_init();
-  }
+  if (threadIdx.x == 0) sm.tl_n = 0;
   __syncthreads();
   TcRoles tr;
   if constexpr (kTc) tc_setup(a, sm);

@@ -121,8 +121,10 @@ struct StepArgs {
   int tc_stages;                      // shared-memory stages of the MMA pipeline
   unsigned tc_stage_bytes;            // bytes per stage: A tile 16 KB + B tile (<= 256 streams x 128 B)
   unsigned tc_ncols;                  // tensor-memory columns allocated (power of two >= 32)
-  unsigned att_buf_bytes;             // staged batched attention: bytes per K/V staging buffer (0: direct loads)
-  int att_chunk;                      // ring slots per staging item (K and V each half a buffer)
+  unsigned att_buf_bytes;             // staged batched attention: bytes per warp stage, K then V (0: direct loads)
+  int att_chunk;                      // ring slots per stage (a power of two <= 16)
+  int att_stages;                     // stages per warp
+  unsigned att_table_bytes;           // the q/k/v table ahead of the stages in dynamic shared memory
 };
 
 // ---------------------------------------------------------------- storage types

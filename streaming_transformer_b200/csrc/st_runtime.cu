@@ -865,24 +865,54 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
                    "cudaFuncSetAttribute rounds") != ST_OK)
         return bail(ST_ERR_CUDA);
     }
-    // Staged attention: kAttBuffers K/V buffers in the round's dynamic shared
-    // memory -- the tensor-core stages (idle during the attention phase) or,
-    // for the CUDA-core round, an allocation of their size. ST_ATT_STAGE=0
-    // selects the direct-load attention phase.
+    // Staged attention: per warp, a ring of K/V stages in the round's dynamic
+    // shared memory behind the q/k/v table of the CTA's units -- the largest
+    // dynamic allocation the kernel takes beside its static shared memory
+    // (the tensor-core GEMM stages reuse the same bytes). C ring slots per
+    // stage (a power of two <= 16): the largest C that leaves at least 4
+    // stages per warp, else 2 (more stages keep more bytes in flight). At
+    // head_dim 64 the chunk is fixed by the storage type (8 slots of 16-bit
+    // rows, 4 of fp32). ST_ATT_STAGE=0 selects the direct-load attention phase.
     {
       const char* aenv = std::getenv("ST_ATT_STAGE");
-      const size_t dyn = rt->tc ? rt->tc_smem : ((size_t)192 << 10);
-      const unsigned buf = (unsigned)(dyn / kAttBuffers / 1024 * 1024);
-      const int chunk = std::min<int>(m.window, (int)(buf / (2u * (unsigned)hd * (unsigned)rt->elem)));
-      if (chunk >= 16 && !(aenv && aenv[0] == '0')) {
-        rt->args.att_buf_bytes = buf;
-        rt->args.att_chunk = chunk;
-        if (!rt->tc) {
-          rt->tc_smem = dyn;
-          if (rt->cuda(cudaFuncSetAttribute(rounds_fn(rt), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn),
-                       "cudaFuncSetAttribute rounds") != ST_OK)
-            return bail(ST_ERR_CUDA);
+      cudaFuncAttributes fa{};
+      int optin = 0;
+      if (rt->cuda(cudaFuncGetAttributes(&fa, rounds_fn(rt)), "cudaFuncGetAttributes rounds") != ST_OK ||
+          rt->cuda(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, rt->device),
+                   "cudaDeviceGetAttribute smem") != ST_OK)
+        return bail(ST_ERR_CUDA);
+      const size_t dyn = (size_t)optin > fa.sharedSizeBytes ? ((size_t)optin - fa.sharedSizeBytes) / 1024 * 1024 : 0;
+      const int mine = (int)((S * (size_t)m.heads + (size_t)rt->bgrid - 1) / (size_t)rt->bgrid);
+      const unsigned table = att_table_bytes(mine, hd);
+      int chunk = 0, nb = 0;
+      if (hd == 64) {  // the head-dim-64 phase: fixed chunks, 2 KB stages (as many as fit, >= 2)
+        const int c = rt->elem == 2 ? 8 : 4;
+        const size_t stage = 2ull * (size_t)c * 64u * (size_t)rt->elem;
+        const size_t fit = dyn > table ? (dyn - table) / ((size_t)kWarps * stage) : 0;
+        if (fit >= 2) {
+          chunk = c;
+          nb = (int)std::min<size_t>(fit, kAttMaxStages);
         }
+      }
+      for (int want = 4; want >= 2 && !chunk && hd != 64; want -= 2)
+        for (int c = kAttMaxChunk; c >= 1 && !chunk; c /= 2) {
+          const size_t stage = 2ull * (size_t)c * (size_t)hd * (size_t)rt->elem;
+          const size_t fit = dyn > table ? (dyn - table) / ((size_t)kWarps * stage) : 0;
+          if (fit >= (size_t)want) {
+            chunk = c;
+            nb = (int)std::min<size_t>(fit, kAttMaxStages);
+          }
+        }
+      if (chunk && !(aenv && aenv[0] == '0')) {
+        const unsigned stage = 2u * (unsigned)chunk * (unsigned)hd * (unsigned)rt->elem;
+        rt->args.att_chunk = chunk;
+        rt->args.att_stages = nb;
+        rt->args.att_buf_bytes = stage;
+        rt->args.att_table_bytes = table;
+        rt->tc_smem = std::max(rt->tc_smem, (size_t)table + (size_t)kWarps * nb * stage);
+        if (rt->cuda(cudaFuncSetAttribute(rounds_fn(rt), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rt->tc_smem),
+                     "cudaFuncSetAttribute rounds") != ST_OK)
+          return bail(ST_ERR_CUDA);
       }
     }
     int occ = 0;
@@ -1625,7 +1655,7 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     << ",\"streams\":" << rt->desc.streams << ",\"batched\":" << (rt->batched ? "true" : "false")
     << ",\"batched_tensor_cores\":" << (rt->tc ? "true" : "false") << ",\"tc_stages\":" << rt->args.tc_stages
     << ",\"tc_stage_bytes\":" << rt->args.tc_stage_bytes << ",\"tc_tmem_columns\":" << rt->args.tc_ncols
-    << ",\"attention_stage_bytes\":" << rt->args.att_buf_bytes << ",\"attention_stage_slots\":" << rt->args.att_chunk
+    << ",\"attention_stage_bytes\":" << rt->args.att_buf_bytes << ",\"attention_stage_slots\":" << rt->args.att_chunk << ",\"attention_stages_per_warp\":" << rt->args.att_stages
     << ",\"tiled_weights_bytes\":" << rt->tweights_bytes
     << ",\"batched_grid\":" << rt->bgrid << ",\"batched_splits\":[" << rt->bsplit[0] << "," << rt->bsplit[1] << ","
     << rt->bsplit[2] << "," << rt->bsplit[3] << "],\"batched_barriers_per_round\":"
