@@ -116,16 +116,25 @@ __global__ void k_convert(const float* src, T* dst, int rows, int cols, int kind
 // The tensor-core copy of one checkpoint tensor: element (r, c) goes to row m,
 // column k of its GEMM matrix (q/k/v fused head-major [3d, d], out [d, d],
 // gate/up interleaved [2F, d], down [d, F]) in the MMA's tiled layout
-// (umma_tile_offset, 128-row tiles).
+// (umma_tile_offset, 128-row tiles). fp32: tf32 hi at the tiled offset
+// (umma_tile_offset32) and tf32 lo `lo` floats further (the padded matrix size).
 template <typename T>
-__global__ void k_convert_tiled(const float* src, T* dst, int rows, int cols, int kind, int p0, int p1, int gemm_cols) {
+__global__ void k_convert_tiled(const float* src, T* dst, int rows, int cols, int kind, int p0, int p1, int gemm_cols,
+                                size_t lo) {
   const size_t n = (size_t)rows * cols;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / cols, c = i - r * cols;
     size_t m = r;
     if (kind == kQkvHead) m = ((r / p1) * 3 + p0) * p1 + r % p1;
     else if (kind == kPlain) m = r * p0 + p1;
-    Storage<T>::store(dst, umma_tile_offset(m, c, kUmmaM, (size_t)gemm_cols / kTileK), src[i]);
+    if constexpr (std::is_same<T, float>::value) {
+      const size_t at = umma_tile_offset32(m, c, kUmmaM, (size_t)gemm_cols / kTileK32);
+      const float hi = to_tf32(src[i]);
+      dst[at] = hi;
+      dst[lo + at] = to_tf32(src[i] - hi);
+    } else {
+      Storage<T>::store(dst, umma_tile_offset(m, c, kUmmaM, (size_t)gemm_cols / kTileK), src[i]);
+    }
   }
 }
 
@@ -153,7 +162,7 @@ struct st_runtime {
   // one CTA per SM, every weight read once per round for all streams. Chosen
   // for 4 or more streams when the model allows it; ST_BATCHED=0/1 overrides.
   bool batched = false;
-  bool tc = false;        // batched GEMM phases on the tensor cores (16-bit modes)
+  bool tc = false;        // batched GEMM phases on the tensor cores (fp32 as three tf32 products)
   // One stream at the benchmark shapes: the device-loop backends (FUSED,
   // PERSISTENT, device traces) run the flow kernel (st_flow.cuh) on its own
   // cluster shape; ST_FLOW=0 selects the generic kernels.
@@ -253,10 +262,7 @@ struct Kernels {
     return ring ? (const void*)k2_persistent<T, true> : (const void*)k2_persistent<T, false>;
   }
   static const void* convert() { return (const void*)k_convert<T>; }
-  static const void* rounds(bool tc) {
-    if constexpr (std::is_same<T, float>::value) return (const void*)k3_rounds<T, false>;  // fp32: CUDA cores only
-    else return tc ? (const void*)k3_rounds<T, true> : (const void*)k3_rounds<T, false>;
-  }
+  static const void* rounds(bool tc) { return tc ? (const void*)k3_rounds<T, true> : (const void*)k3_rounds<T, false>; }
 };
 
 #define ST_KERNEL(rt, name) \
@@ -276,7 +282,7 @@ const void* persistent_fn(const st_runtime* rt) { return ST_LOOP_KERNEL(rt, pers
 const void* rounds_fn(const st_runtime* rt) {
   if (rt->desc.mode == ST_MODE_FP16) return Kernels<__half>::rounds(rt->tc);
   if (rt->desc.mode == ST_MODE_BF16) return Kernels<__nv_bfloat16>::rounds(rt->tc);
-  return Kernels<float>::rounds(false);
+  return Kernels<float>::rounds(rt->tc);
 }
 
 // Launch with this runtime's cluster shape. `cooperative` requests the
@@ -833,7 +839,7 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
   const size_t act_at = take(S * F * 4), score_at = take(S * 4), input_at = take(S * m.features * 4);
   const size_t pout_at = take(S * m.heads * (size_t)d * 4), dpart_at = take(S * (size_t)rt->nclusters * d * 4);
   // batched round: selection, grid (one CTA per SM) and K-splits. On the
-  // tensor cores (16-bit modes, d and F multiples of 64; ST_TC=0 disables) a
+  // tensor cores (d and F multiples of 64; fp32 as 3xTF32; ST_TC=0 disables) a
   // GEMM unit is a 128-row tile x K split x up to 256 streams, and each phase
   // gets about one unit per CTA. On the CUDA cores a unit is 64 rows x 32
   // streams, about one per warp, with at most 16 splits. Splits never exceed
@@ -845,7 +851,7 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
     if (env && env[0] == '1') want = true;
     rt->batched = want && S >= 2 && batch_supported(d, m.heads, F, m.features);
     const char* tenv = std::getenv("ST_TC");
-    rt->tc = rt->batched && m.mode != ST_MODE_FP32 && d % kTileK == 0 && F % kTileK == 0 && !(tenv && tenv[0] == '0');
+    rt->tc = rt->batched && d % kTileK == 0 && F % kTileK == 0 && !(tenv && tenv[0] == '0');
   }
   const size_t spad = (S + 15) / 16 * 16;
   size_t bpart_floats = 0;
@@ -853,13 +859,16 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
     rt->bgrid = rt->sms;
     const size_t nmax = std::min<size_t>(spad, kTcMaxN);
     if (rt->tc) {
-      const size_t stage = kTcTileBytes + nmax * kCoreBytes;
+      // a stage: the A tile and the B tile of one chunk (fp32: hi and lo of each)
+      const size_t planes = m.mode == ST_MODE_FP32 ? 2 : 1;
+      const size_t stage = planes * (kTcTileBytes + nmax * kCoreBytes);
       const int stages = (int)std::min<size_t>(kTcMaxStages, ((size_t)192 << 10) / stage);
       rt->args.tc_stages = stages;
       rt->args.tc_stage_bytes = (unsigned)stage;
       rt->tc_smem = (size_t)stages * stage;
       unsigned ncols = 32;
       while (ncols < nmax) ncols *= 2;
+      if (m.mode == ST_MODE_FP32) ncols = 2 * kTcMaxN;  // fp32: main and correction accumulators
       rt->args.tc_ncols = ncols;
       if (rt->cuda(cudaFuncSetAttribute(rounds_fn(rt), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rt->tc_smem),
                    "cudaFuncSetAttribute rounds") != ST_OK)
@@ -946,7 +955,8 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
   }
   const size_t bx_at = take(rt->batched ? S * d * 4 : 0), bx2_at = take(rt->batched ? S * d * 4 : 0);
   const size_t bz_at = take(rt->batched && !rt->tc ? S * (size_t)std::max(d, F) * 4 : 0), bpart_at = take(bpart_floats * 4);
-  const size_t bz16_at = take(rt->tc ? spad * (size_t)std::max(d, F) * 2 : 0);
+  // the tensor cores' tiled input: storage type, or tf32 hi and lo planes for fp32
+  const size_t bz16_at = take(rt->tc ? spad * (size_t)std::max(d, F) * (m.mode == ST_MODE_FP32 ? 8 : 2) : 0);
   const size_t bar_at = take(sizeof(unsigned long long)), err_at = take(sizeof(int));
   const size_t rope_at = take((hd / 2) * sizeof(float)), ctl_at = take(sizeof(Control));
   // flow kernel: choose it and its cluster shape (largest cluster whose
@@ -1095,9 +1105,10 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
     a.bz16 = rt->scratch + bz16_at;
     auto pad = [](size_t rows) { return (rows + kUmmaM - 1) / kUmmaM * kUmmaM; };
     size_t to = 0;
+    const size_t tbytes = m.mode == ST_MODE_FP32 ? 8 : 2;  // fp32: tf32 hi and lo planes
     auto matrix = [&](size_t rows, size_t cols) {
       const size_t at = to;
-      to = align_up(to + pad(rows) * cols * 2, 256);
+      to = align_up(to + pad(rows) * cols * tbytes, 256);
       return at;
     };
     std::vector<size_t> tq(L), tout(L), tgu(L), tdn(L);
@@ -1180,10 +1191,13 @@ int st_set_tensor(st_runtime* rt, const char* name, const float* data, size_t co
     else k_convert<float><<<blocks, 256, 0, rt->stream>>>(tmp, (float*)dst, s.rows, s.cols, s.kind, s.p0, s.p1);
     if (rt->tc && s.tiled_rows) {
       void* tdst = rt->tweights + s.tiled_offset;
+      const size_t lo = (size_t)(s.tiled_rows + kUmmaM - 1) / kUmmaM * kUmmaM * (size_t)s.tiled_cols;
       if (rt->desc.mode == ST_MODE_FP16)
-        k_convert_tiled<__half><<<blocks, 256, 0, rt->stream>>>(tmp, (__half*)tdst, s.rows, s.cols, s.kind, s.p0, s.p1, s.tiled_cols);
+        k_convert_tiled<__half><<<blocks, 256, 0, rt->stream>>>(tmp, (__half*)tdst, s.rows, s.cols, s.kind, s.p0, s.p1, s.tiled_cols, lo);
+      else if (rt->desc.mode == ST_MODE_BF16)
+        k_convert_tiled<__nv_bfloat16><<<blocks, 256, 0, rt->stream>>>(tmp, (__nv_bfloat16*)tdst, s.rows, s.cols, s.kind, s.p0, s.p1, s.tiled_cols, lo);
       else
-        k_convert_tiled<__nv_bfloat16><<<blocks, 256, 0, rt->stream>>>(tmp, (__nv_bfloat16*)tdst, s.rows, s.cols, s.kind, s.p0, s.p1, s.tiled_cols);
+        k_convert_tiled<float><<<blocks, 256, 0, rt->stream>>>(tmp, (float*)tdst, s.rows, s.cols, s.kind, s.p0, s.p1, s.tiled_cols, lo);
     }
     st = rt->cuda(cudaGetLastError(), "convert launch");
     if (st == ST_OK) st = rt->cuda(cudaStreamSynchronize(rt->stream), "convert");

@@ -4,12 +4,20 @@
 // mbarriers, and the tensor-memory loads of the epilogue. Hand-written PTX.
 //
 // Operand layout: "no swizzle, K-major" core matrices. A core matrix is 8 rows
-// x 16 bytes (8 bf16/fp16 elements of K), stored as 128 contiguous bytes. A
-// tile of R rows x 64 K is stored as [R/8 row groups][8 K groups][8 rows][8]
-// so that, in the shared-memory descriptor, the K-adjacent core matrices are
-// 128 bytes apart (leading-dimension byte offset) and the row-group-adjacent
-// ones 1024 bytes apart (stride-dimension byte offset). One MMA consumes K = 16
-// (two core matrices); the next starts 256 bytes further.
+// x 16 bytes (8 bf16/fp16 elements of K, or 4 tf32), stored as 128 contiguous
+// bytes. A tile of R rows x 128 bytes of K (64 16-bit or 32 tf32 elements) is
+// stored as [R/8 row groups][8 K groups][8 rows][16 bytes] so that, in the
+// shared-memory descriptor, the K-adjacent core matrices are 128 bytes apart
+// (leading-dimension byte offset) and the row-group-adjacent ones 1024 bytes
+// apart (stride-dimension byte offset). One MMA consumes 32 bytes of K (two
+// core matrices: K = 16 of kind::f16, K = 8 of kind::tf32); the next starts
+// 256 bytes further.
+//
+// fp32 GEMMs run as three TF32 products ("3xTF32"): each operand x is split
+// into hi = tf32(x) and lo = tf32(x - hi), and A B = Ahi Bhi + Ahi Blo +
+// Alo Bhi accumulates in fp32; the dropped Alo Blo and the rounding of lo are
+// about 2^-22 of each product, below fp32's own accumulation error at these
+// lengths.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -23,7 +31,8 @@ namespace st {
 
 constexpr int kUmmaM = 128;          // rows of A (weight rows) per MMA tile
 constexpr int kUmmaK = 16;           // K per MMA instruction (16-bit operands)
-constexpr int kTileK = 64;           // K per staged chunk (four MMAs)
+constexpr int kTileK = 64;           // K per staged chunk (four MMAs), 16-bit operands
+constexpr int kTileK32 = 32;         // K per staged chunk, tf32 operands
 constexpr unsigned kCoreBytes = 128; // one 8 x 16-byte core matrix
 constexpr unsigned kLbo = 128;       // K-adjacent core matrices
 constexpr unsigned kSbo = 1024;      // row-group-adjacent core matrices (8 K groups of 128 bytes)
@@ -37,6 +46,21 @@ __host__ __device__ inline size_t umma_tile_offset(size_t r, size_t k, size_t ti
   return tile * tile_rows * kTileK + (((rr >> 3) * 8 + ((k >> 3) & 7)) * 64) + (rr & 7) * 8 + (k & 7);
 }
 
+// The same layout for 32-bit elements (tf32 operands, 32 columns per tile).
+__host__ __device__ inline size_t umma_tile_offset32(size_t r, size_t k, size_t tile_rows, size_t kchunks) {
+  const size_t tile = (r / tile_rows) * kchunks + k / kTileK32;
+  const size_t rr = r % tile_rows;
+  return tile * tile_rows * kTileK32 + (((rr >> 3) * 8 + ((k >> 2) & 7)) * 32) + (rr & 7) * 4 + (k & 3);
+}
+
+// x rounded to tf32 (10 explicit mantissa bits, nearest, ties away from zero),
+// as an fp32 bit pattern whose low 13 bits are zero.
+__device__ __forceinline__ float to_tf32(float x) {
+  unsigned r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 // Shared-memory matrix descriptor (tcgen05 format): start address >> 4 in
 // bits 0-13, leading-dimension byte offset >> 4 in 16-29, stride-dimension
 // byte offset >> 4 in 32-45, descriptor version 1 in bits 46-47, base offset
@@ -47,12 +71,13 @@ __device__ __forceinline__ unsigned long long umma_desc(const void* smem) {
          ((unsigned long long)(kSbo >> 4) << 32) | (1ull << 46);
 }
 
-// Instruction descriptor of kind::f16: fp32 accumulator (bits 4-5 = 1), A and
-// B both bf16 (bits 7-9 and 10-12 = 1) or both fp16 (0), both K-major (bits
-// 15, 16 = 0), N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+// Instruction descriptor of kind::f16 / kind::tf32: fp32 accumulator (bits
+// 4-5 = 1), A and B both bf16 (bits 7-9 and 10-12 = 1), both fp16 (0) or both
+// tf32 (2, for fp32 storage), both K-major (bits 15, 16 = 0), N >> 3 in bits
+// 17-22, M >> 4 in bits 24-28.
 template <typename T>
 __device__ __forceinline__ unsigned umma_idesc(int m, int n) {
-  const unsigned ab = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  const unsigned ab = std::is_same<T, __nv_bfloat16>::value ? 1u : std::is_same<T, float>::value ? 2u : 0u;
   return (1u << 4) | (ab << 7) | (ab << 10) | ((unsigned)(n >> 3) << 17) | ((unsigned)(m >> 4) << 24);
 }
 
@@ -77,6 +102,17 @@ __device__ __forceinline__ void umma_f16(unsigned d_tmem, unsigned long long ade
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The same with tf32 operands (kind::tf32, K = 8 per instruction).
+__device__ __forceinline__ void umma_tf32(unsigned d_tmem, unsigned long long adesc, unsigned long long bdesc,
+                                          unsigned idesc, unsigned accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

@@ -4,7 +4,9 @@ configurations, which the small-shape stream tests do not reach:
 * C4, Large bf16 (d1024 L12 H16 F4096 W256) with 256 streams: the GEMM phases
   run on the tensor cores with a 256-column TMEM accumulator and N = 256 MMAs.
 * C5-A, Large fp32 (W512) with 256 streams on one GPU (2048 over 8 GPUs): the
-  GEMM phases run on the CUDA cores.
+  GEMM phases run on the tensor cores as three tf32 products per fp32 product
+  (hi/lo split), and, with ST_TC=0, on the CUDA cores in fp32; both are held
+  to the fp32 policy (1e-5 relative per tensor).
 
 Stepping 256 Large streams past a ring revolution on the CPU would take hours,
 so the sampled streams start from a seeded random state at a position past the
@@ -42,8 +44,11 @@ def random_state(config, mode, seed):
     return keys, values, hidden
 
 
-@pytest.mark.parametrize("name", ["c4-large-bf16", "c5-large-fp32"])
-def test_batched_round_at_benchmark_shape(name):
+@pytest.mark.parametrize("name,engine", [("c4-large-bf16", "tensor"), ("c5-large-fp32", "tensor"),
+                                         ("c5-large-fp32", "cuda-cores")])
+def test_batched_round_at_benchmark_shape(name, engine, monkeypatch):
+    if engine == "cuda-cores":
+        monkeypatch.setenv("ST_TC", "0")
     config, mode = synthetic.CONFIGS[name]
     model = synthetic.make_model(config, mode, seed=31)
     events = np.stack([synthetic.make_events(ROUNDS, config.features, seed=5000 + s) for s in range(STREAMS)],
@@ -53,8 +58,9 @@ def test_batched_round_at_benchmark_shape(name):
     try:
         info = rt.info()
         assert info["batched"], info
-        if mode == "bf16":
-            assert info["batched_tensor_cores"] and info["tc_tmem_columns"] == 256, info
+        if engine == "tensor":
+            # fp32: a second 256-column accumulator takes the tf32 correction products
+            assert info["batched_tensor_cores"] and info["tc_tmem_columns"] == (512 if mode == "fp32" else 256), info
         else:
             assert not info["batched_tensor_cores"], info
         for k, s in enumerate(SAMPLED):
