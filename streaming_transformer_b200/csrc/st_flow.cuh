@@ -165,6 +165,7 @@ __device__ inline FlowSpan flow_span(const StepArgs& a, const Where& w, int kind
 enum FlowMark : int {
   kFmStep = 1, kFmIn, kFmNorm1, kFmQkv, kFmQkvSync, kFmAttn, kFmPartSync, kFmMerge, kFmOut, kFmGather1,
   kFmPub2, kFmNorm2, kFmGateUp, kFmDown, kFmDredSync, kFmDpub, kFmGather2, kFmPub1, kFmScore,
+  kFmKvIssue = 20, kFmNormScale = 21, kFmNormGain = 22,  // parts of the first head's norm1
   kFmAcqWait = 24  // not a phase: cycles spent waiting for ring chunks, inside the phases above
 };
 constexpr int kFlowTags = 32;
@@ -879,12 +880,15 @@ __device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowC
     }
     cp_async_commit();
   }
+  fmark<kDiag>(a, fr, kFmKvIssue);
   if (first_head) {
     const float scale = flow_norm_scale(sm.ssx[cx.bx], cx.cs, cx.n, D, a.epsilon);
     const float* x = sm.x[cx.bx];
+    fmark<kDiag>(a, fr, kFmNormScale);
     flow_gain<T, kDiag>(a, fr, cur, [&](const T* g) {
       for (int i = threadIdx.x; i < D; i += kThreads) sm.z[i] = Storage<T>::round(x[i] * scale * Storage<T>::load(g, i));
     });
+    fmark<kDiag>(a, fr, kFmNormGain);
     flow_bsync(fr);
     fmark<kDiag>(a, fr, kFmNorm1);
   }

@@ -27,8 +27,13 @@ def main() -> None:
     p.add_argument("--warmup", type=int, default=2)
     p.add_argument("--window", type=int, default=0)
     p.add_argument("--blocks", type=int, default=0)
+    p.add_argument("--streams", type=int, default=1, help="streams (more than 1: the batched round)")
+    p.add_argument("--steady", action="store_true",
+                   help="the timed launch continues from the warm-up's state (device-resident events) instead of "
+                        "starting from reset; with --warmup >= window every timed step attends a full window")
     p.add_argument("--timeline", action="store_true",
-                   help="per-phase breakdown from CTA 0's clock64() marks (scaled to the measured step time)")
+                   help="per-phase breakdown from CTA 0's clock64() marks (scaled to the measured step time); "
+                        "with --streams > 1, the batched round's phases over its last rounds")
     p.add_argument("--phases", action="store_true",
                    help="flow kernel: per-phase cycle sums of every CTA (diagnostic build), median over the "
                         "CTAs that own a head and over the FFN-only CTAs, us per step at --sm-mhz")
@@ -41,14 +46,28 @@ def main() -> None:
     if backend == Backend.PERSISTENT:
         backend = Backend.FUSED  # same device loop, no host-driven worker
     model = synthetic.make_model(config, mode, seed=42)
-    events = synthetic.make_events(a.warmup + a.events, config.features, seed=123)
-    with Runtime(model, RuntimeOptions(backend=backend, blocks=a.blocks)) as rt:
-        if a.warmup:
-            rt.device_trace(events[: a.warmup])
-        us = rt.device_trace(events[a.warmup:])
-        out = {"config": a.config, "backend": backend.name.lower(), "events": a.events,
+    if a.streams > 1:
+        events = synthetic.make_stream_events(a.streams, a.warmup + a.events, config.features)
+    else:
+        events = synthetic.make_events(a.warmup + a.events, config.features, seed=123)
+    with Runtime(model, RuntimeOptions(backend=backend, blocks=a.blocks), streams=a.streams) as rt:
+        if a.steady:
+            import numpy as np
+            import torch
+            dev = torch.from_numpy(np.ascontiguousarray(events, dtype=np.float32)).cuda()
+            if a.warmup:
+                rt.device_trace_resident(dev.data_ptr(), a.warmup)
+            torch.cuda.synchronize()
+            us, _ = rt.device_trace_continue(dev[a.warmup:].data_ptr(), a.events)
+        else:
+            if a.warmup:
+                rt.device_trace(events[: a.warmup])
+            us = rt.device_trace(events[a.warmup:])
+        out = {"config": a.config, "backend": backend.name.lower(), "events": a.events, "streams": a.streams,
                "us_per_step": us, "blocks": rt.info()["blocks"]}
-        if a.timeline:
+        if a.timeline and a.streams > 1:
+            out.update(round_breakdown(rt, events, config, a.sm_mhz))
+        elif a.timeline:
             out["phases_us"] = timeline_breakdown(rt, events[a.warmup:], config, us)
         if a.phases:
             out.update(phase_sums(rt, events[a.warmup:], config, a.sm_mhz))
@@ -66,9 +85,10 @@ TAGS = {1: "step_start", 2: "input", 3: "norm1", 4: "ring_wait", 5: "warp_gemv",
 
 # Phase tags of the flow kernel's cycle sums (FlowMark in csrc/st_flow.cuh); slot 0
 # holds the step count, slot 24 the ring waits already inside the phases.
-FLOW_TAGS = {1: "step", 2: "input", 3: "norm1", 4: "qkv", 5: "qkv_recv", 6: "attention", 7: "partials_recv",
+FLOW_TAGS = {1: "step", 2: "input", 4: "qkv", 5: "qkv_recv", 6: "attention", 7: "partials_recv",
              8: "merge", 9: "out", 10: "gather1", 11: "publish2", 12: "norm2", 13: "gate_up", 14: "down",
              15: "down_reduce_recv", 16: "down_publish", 17: "gather2", 18: "publish1", 19: "score",
+             20: "kv_prefetch_issue", 21: "norm1_scale", 22: "norm1_gain", 3: "norm1_barrier",
              24: "(ring_wait, inside the phases)"}
 
 
@@ -106,6 +126,39 @@ def phase_sums(rt, events, config, sm_mhz):
         total = float(sum(v for k, v in phases.items() if not k.startswith("(")))
         out[label] = {"ctas": len(ctas), "total_us": round(total, 2), "phases_us": phases}
     return out
+
+
+# Phase tags of the batched round (BatchTag in csrc/st_batch.cuh): each mark
+# ends the named phase; "sync" is the wait at a grid barrier.
+ROUND_TAGS = {40: "input", 41: "qkv_gemm", 42: "attention", 43: "out_gemm", 44: "residual_norm2",
+              45: "gate_up_gemm", 46: "swiglu", 47: "down_gemm", 48: "residual_norm1", 49: "grid_barrier_wait",
+              50: "attention_qkv_finish"}
+
+
+def round_breakdown(rt, events, config, sm_mhz, rounds_kept=40):
+    """Per-phase us per round of the batched round from thread 0 of CTA 0, over
+    the last ``rounds_kept`` rounds of a run of all ``events`` from reset (the
+    windows are full when the run is longer than the window)."""
+    import numpy as np
+    count = events.shape[0]
+    per_round = 12 * config.layers + 4
+    cap = 16 * max(1 << 16, count * per_round * 2)
+    row = rt.device_timeline(events, capacity=cap, cta=0, warp=0)
+    tags = (row & 0xFF).astype(int)
+    clocks = row >> 8
+    starts = np.flatnonzero(tags == 40)
+    if len(starts) < 2:
+        return {"round_phases_us": {}}
+    keep = min(rounds_kept, len(starts) - 1)
+    lo, hi = starts[-keep - 1], starts[-1]
+    acc = {}
+    for k in range(lo + 1, hi + 1):
+        name = ROUND_TAGS.get(int(tags[k]), f"tag{int(tags[k])}")
+        acc[name] = acc.get(name, 0) + int(clocks[k] - clocks[k - 1])
+    scale = 1.0 / (keep * sm_mhz)
+    phases = {n: round(v * scale, 1) for n, v in sorted(acc.items(), key=lambda kv: -kv[1])}
+    return {"rounds_kept": keep, "round_us": round((clocks[hi] - clocks[lo]) * scale, 1),
+            "round_phases_us": phases}
 
 
 def timeline_breakdown(rt, events, config, us_per_step):
