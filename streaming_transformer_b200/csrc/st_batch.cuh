@@ -976,7 +976,7 @@ struct TcRoles {
 };
 
 // P[ks][s][m] = sum over split ks's K chunks of W[m][k] z[s][k] on the tensor
-// cores. A unit is (128-row tile, K split, group of up to 256 streams): the
+// cores. A unit is (128-row tile, K split, group of nu <= 256 streams): the
 // producer thread copies each 64-column chunk's A tile (16 KB of pre-tiled
 // weights) and B tile (the streams' inputs, N x 128 bytes) into a stage with
 // one mbarrier completion; the issuer thread runs four 128 x N x 16 MMAs per
@@ -992,12 +992,12 @@ struct TcRoles {
 // oracle where the CUDA-core fp32 round stays within the policy.)
 template <typename T>
 __device__ void tc_gemm_phase(const StepArgs& a, BatchSmem& sm, unsigned char* stages, TcRoles& tr, const T* Wt,
-                              int M, int K, int ksplit, float* P) {
+                              int M, int K, int ksplit, int nu, float* P) {
   constexpr bool kX3 = std::is_same<T, float>::value;  // fp32 as three tf32 products
   constexpr int kK = kX3 ? kTileK32 : kTileK;           // K elements per 128-byte chunk row
   const int S = a.streams, spad = a.spad;
   const int mtiles = (M + kUmmaM - 1) / kUmmaM, kchunks = K / kK;
-  const int sgroups = (spad + kTcMaxN - 1) / kTcMaxN;
+  const int sgroups = (spad + nu - 1) / nu;  // nu: streams per unit (MMA N), a multiple of 16
   const int units = mtiles * ksplit * sgroups;
   const int warp = (int)threadIdx.x >> 5, lane = (int)threadIdx.x & 31;
   const T* Bt = (const T*)a.bz16;
@@ -1008,7 +1008,7 @@ __device__ void tc_gemm_phase(const StepArgs& a, BatchSmem& sm, unsigned char* s
     const int mt = u % mtiles, rest = u / mtiles, ks = rest % ksplit, sg = rest / ksplit;
     int c0, c1;
     split(kchunks, ks, ksplit, c0, c1);
-    const int s0 = sg * kTcMaxN, n = min(kTcMaxN, spad - s0);
+    const int s0 = sg * nu, n = min(nu, spad - s0);
     if (threadIdx.x == kTcProducer) {
       const unsigned long long wpol = policy_evict_first(), zpol = policy_evict_last();
       for (int kc = c0; kc < c1 && !tr.failed; ++kc) {
@@ -1158,8 +1158,8 @@ __device__ inline void tc_teardown(const StepArgs& a, BatchSmem& sm, const TcRol
 // One GEMM phase on the CUDA cores or the tensor cores.
 template <typename T, bool kTc, int kView>
 __device__ __forceinline__ void gemm_any(const StepArgs& a, BatchSmem& sm, unsigned char* stages, TcRoles& tr,
-                                         const void* W, const void* Wt, int M, int K, int ksplit) {
-  if constexpr (kTc) tc_gemm_phase<T>(a, sm, stages, tr, (const T*)Wt, M, K, ksplit, a.bpart);
+                                         const void* W, const void* Wt, int M, int K, int ksplit, int nu) {
+  if constexpr (kTc) tc_gemm_phase<T>(a, sm, stages, tr, (const T*)Wt, M, K, ksplit, nu, a.bpart);
   else gemm_phase<T, kView>(a, sm, (const T*)W, M, K, ksplit, a.bz, a.bpart);
 }
 
@@ -1179,22 +1179,22 @@ __device__ bool round_batched(const StepArgs& a, BatchSmem& sm, unsigned char* s
   if (!sync(kBtlInput)) return false;
   for (int l = 0; l < L; ++l) {
     const LayerPtrs& w = a.layer[l];
-    gemm_any<T, kTc, kViewRows>(a, sm, stages, tr, w.qkv, a.tqkv[l], 3 * d, d, a.bsplit[0]);
+    gemm_any<T, kTc, kViewRows>(a, sm, stages, tr, w.qkv, a.tqkv[l], 3 * d, d, a.bsplit[0], a.tc_n[0]);
     if (!sync(kBtlQkv)) return false;
     if (a.att_buf_bytes && a.head_dim == 64) attention_phase_hd64<T, kTc>(a, sm, stages, l, event);
     else if (a.att_buf_bytes) attention_phase_staged<T, kTc>(a, sm, stages, l, event);
     else attention_phase<T, kTc>(a, sm, l, event);
     if (!sync(kBtlAttention)) return false;
-    gemm_any<T, kTc, kViewOutHeads>(a, sm, stages, tr, w.out, a.tout[l], d, d, a.bsplit[1]);
+    gemm_any<T, kTc, kViewOutHeads>(a, sm, stages, tr, w.out, a.tout[l], d, d, a.bsplit[1], a.tc_n[1]);
     if (!sync(kBtlOut)) return false;
     for (int s = blockIdx.x; s < S; s += gridDim.x)
       row_residual<T, kTc>(a, sm, s, a.bx, a.bx2, a.bpart, a.bsplit[1], nullptr, (const T*)w.norm2, false, nullptr);
     if (!sync(kBtlResidual2)) return false;
-    gemm_any<T, kTc, kViewRows>(a, sm, stages, tr, w.gateup, a.tgateup[l], 2 * F, d, a.bsplit[2]);
+    gemm_any<T, kTc, kViewRows>(a, sm, stages, tr, w.gateup, a.tgateup[l], 2 * F, d, a.bsplit[2], a.tc_n[2]);
     if (!sync(kBtlGateUp)) return false;
     swiglu_phase<T, kTc>(a, a.bsplit[2]);
     if (!sync(kBtlSwiglu)) return false;
-    gemm_any<T, kTc, kViewColumns>(a, sm, stages, tr, w.down, a.tdown[l], d, F, a.bsplit[3]);
+    gemm_any<T, kTc, kViewColumns>(a, sm, stages, tr, w.down, a.tdown[l], d, F, a.bsplit[3], a.tc_n[3]);
     if (!sync(kBtlDown)) return false;
     const bool last = l + 1 == L;
     for (int s = blockIdx.x; s < S; s += gridDim.x)

@@ -111,6 +111,7 @@ struct StepArgs {
   float* bz;                          // [S][K] input of the next GEMM phase (K = d or F)
   float* bpart;                       // [split][S][rows] K-split partials of the last GEMM phase
   int bsplit[4];                      // K-splits of the q/k/v, out, gate/up and down GEMMs
+  int tc_n[4];                        // streams per tensor-core unit (MMA N) of the same GEMMs
   // batched round on the tensor cores (16-bit modes)
   const void* tqkv[kMaxLayers];       // weights pre-tiled for the MMA (128-row x 64-column core-matrix tiles)
   const void* tout[kMaxLayers];

@@ -176,6 +176,7 @@ struct st_runtime {
   int fcluster = 0, fnclusters = 0, fgrid = 0;
   int bgrid = 0;
   int bsplit[4] = {1, 1, 1, 1};
+  int tcn[4] = {0, 0, 0, 0};  // streams per tensor-core GEMM unit
   size_t tc_smem = 0;     // dynamic shared memory of the tensor-core rounds kernel
   char* tweights = nullptr;
   size_t tweights_bytes = 0;
@@ -841,7 +842,7 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
   // batched round: selection, grid (one CTA per SM) and K-splits. On the
   // tensor cores (d and F multiples of 64; fp32 as 3xTF32; ST_TC=0 disables) a
   // GEMM unit is a 128-row tile x K split x up to 256 streams, and each phase
-  // gets about one unit per CTA. On the CUDA cores a unit is 64 rows x 32
+  // gets at most one unit per CTA. On the CUDA cores a unit is 64 rows x 32
   // streams, about one per warp, with at most 16 splits. Splits never exceed
   // one per 64 columns, and partials stay within 64 MB.
   {
@@ -932,26 +933,57 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
       rt->fail(ST_ERR_UNSUPPORTED, "batched round kernel does not fit on an SM");
       return bail(ST_ERR_UNSUPPORTED);
     }
-    auto pick = [&](size_t M, size_t K) {
-      size_t units1, target;
+    // Tensor cores: per GEMM, the streams per unit (MMA N: 256, 128 or 64) and
+    // the K-split that minimise (waves of units over the grid) x (bytes one unit
+    // moves: its chunks' A and B tiles plus its partial store), plus the
+    // partials' share per CTA. CUDA cores: about one unit per warp.
+    // ST_TC_N forces N.
+    const char* nenv = std::getenv("ST_TC_N");
+    const size_t planes = m.mode == ST_MODE_FP32 ? 2 : 1;  // tf32 hi and lo
+    const size_t kk = m.mode == ST_MODE_FP32 ? kTileK32 : kTileK;
+    auto pick = [&](size_t M, size_t K, int which) {
+      size_t best_ks = 1;
       if (rt->tc) {
-        units1 = ((M + kUmmaM - 1) / kUmmaM) * ((spad + kTcMaxN - 1) / kTcMaxN);
-        target = (size_t)rt->bgrid;
+        const size_t mt = (M + kUmmaM - 1) / kUmmaM, kch = K / kk;
+        double best = 1e300;
+        size_t best_n = kTcMaxN;
+        for (size_t n = std::min<size_t>(spad, kTcMaxN); n >= 16; n /= 2) {
+          if (n % 16 || (nenv && (size_t)std::atoi(nenv) != n)) {
+            if (n < 64) break;
+            continue;
+          }
+          const size_t sg = (spad + n - 1) / n;
+          for (size_t ks = 1; ks <= std::min(K / 64, (size_t)16); ++ks) {
+            if (ks > 1 && ks * S * M * 4 > ((size_t)64 << 20)) break;
+            const size_t units = mt * sg * ks, waves = (units + rt->bgrid - 1) / rt->bgrid;
+            const size_t chunks = (kch + ks - 1) / ks;
+            const double unit_bytes = (double)chunks * planes * (kTcTileBytes + n * kCoreBytes) + 512.0 * n;
+            const double part = 0.5 * (double)(ks * S * M * 8) / (double)rt->bgrid;
+            const double cost = (double)waves * unit_bytes + part;
+            if (cost < best) {
+              best = cost;
+              best_ks = ks;
+              best_n = n;
+            }
+          }
+          if (n <= 64) break;
+        }
+        rt->tcn[which] = (int)best_n;
       } else {
-        units1 = ((M + kBatchRows - 1) / kBatchRows) * ((S + kBatchStreams - 1) / kBatchStreams);
-        target = (size_t)rt->bgrid * kWarps;
+        const size_t units1 = ((M + kBatchRows - 1) / kBatchRows) * ((S + kBatchStreams - 1) / kBatchStreams);
+        const size_t target = (size_t)rt->bgrid * kWarps;
+        best_ks = (target + units1 - 1) / units1;
+        best_ks = std::min(best_ks, std::min(K / 64, (size_t)16));
+        while (best_ks > 1 && best_ks * S * M * 4 > ((size_t)64 << 20)) --best_ks;
+        best_ks = std::max(best_ks, (size_t)1);
       }
-      size_t ks = (target + units1 - 1) / units1;
-      ks = std::min(ks, std::min(K / 64, (size_t)16));
-      while (ks > 1 && ks * S * M * 4 > ((size_t)64 << 20)) --ks;
-      ks = std::max(ks, (size_t)1);
-      bpart_floats = std::max(bpart_floats, ks * S * M);
-      return (int)ks;
+      bpart_floats = std::max(bpart_floats, best_ks * S * M);
+      return (int)best_ks;
     };
-    rt->bsplit[0] = pick(3 * (size_t)d, d);
-    rt->bsplit[1] = pick(d, d);
-    rt->bsplit[2] = pick(2 * (size_t)F, d);
-    rt->bsplit[3] = pick(d, F);
+    rt->bsplit[0] = pick(3 * (size_t)d, d, 0);
+    rt->bsplit[1] = pick(d, d, 1);
+    rt->bsplit[2] = pick(2 * (size_t)F, d, 2);
+    rt->bsplit[3] = pick(d, F, 3);
   }
   const size_t bx_at = take(rt->batched ? S * d * 4 : 0), bx2_at = take(rt->batched ? S * d * 4 : 0);
   const size_t bz_at = take(rt->batched && !rt->tc ? S * (size_t)std::max(d, F) * 4 : 0), bpart_at = take(bpart_floats * 4);
@@ -1097,7 +1129,10 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
     a.bx2 = (float*)(rt->scratch + bx2_at);
     a.bz = (float*)(rt->scratch + bz_at);
     a.bpart = (float*)(rt->scratch + bpart_at);
-    for (int i = 0; i < 4; ++i) a.bsplit[i] = rt->bsplit[i];
+    for (int i = 0; i < 4; ++i) {
+      a.bsplit[i] = rt->bsplit[i];
+      a.tc_n[i] = rt->tcn[i];
+    }
     a.spad = (int)spad;
   }
   if (rt->tc) {
@@ -1672,7 +1707,8 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     << ",\"attention_stage_bytes\":" << rt->args.att_buf_bytes << ",\"attention_stage_slots\":" << rt->args.att_chunk << ",\"attention_stages_per_warp\":" << rt->args.att_stages
     << ",\"tiled_weights_bytes\":" << rt->tweights_bytes
     << ",\"batched_grid\":" << rt->bgrid << ",\"batched_splits\":[" << rt->bsplit[0] << "," << rt->bsplit[1] << ","
-    << rt->bsplit[2] << "," << rt->bsplit[3] << "],\"batched_barriers_per_round\":"
+    << rt->bsplit[2] << "," << rt->bsplit[3] << "],\"batched_tc_streams_per_unit\":[" << rt->tcn[0] << ","
+    << rt->tcn[1] << "," << rt->tcn[2] << "," << rt->tcn[3] << "],\"batched_barriers_per_round\":"
     << (rt->batched ? round_barriers(rt->desc.layers) : 0) << ",\"weights_bytes\":" << rt->weights_bytes
     << ",\"state_bytes\":" << rt->state_bytes << ",\"scratch_bytes\":" << rt->scratch_bytes << "}";
   return copy_json(o.str(), json, capacity, needed);

@@ -40,6 +40,27 @@ class StreamingBF16(Streaming):
         return x.bfloat16().to(self.dtype)
 
 
+def score_drift(name, config, mode, model, c, weights) -> None:
+    """The score sequences of the two implementations for the streams that
+    tests/test_gpu_batched_shapes.py samples (its seeds and positions): the
+    normalized RMSE RMS(diff) / max(1, RMS(ref)) that the score gate bounds."""
+    for k, s in enumerate((0, 131, 255)):
+        position = config.window + 37 * (k + 1)
+        keys, values, hidden = random_state(config, mode, seed=900 + s)
+        events = synthetic.make_events(3, config.features, seed=5000 + s)
+        oracle = Oracle(model)
+        oracle.load_state(position, keys, values, hidden)
+        want = np.array([oracle.step(e) for e in events], dtype=np.float64)
+        oracle.close()
+        ref = (StreamingBF16 if mode == "bf16" else Streaming)(c, weights, "mixed" if mode == "bf16" else "fp32")
+        ref.position = position
+        ref.k = torch.from_numpy(keys.copy())
+        ref.v = torch.from_numpy(values.copy())
+        got = np.array([float(ref.step(torch.from_numpy(e))) for e in events], dtype=np.float64)
+        nrmse = np.sqrt(np.mean((got - want) ** 2)) / max(1.0, np.sqrt(np.mean(want ** 2)))
+        print(f"{name} stream {s} scores: normalized RMSE {nrmse:.3g}, max |diff| {np.max(np.abs(got - want)):.3g}")
+
+
 def main() -> None:
     for name in ("c4-large-bf16", "c5-large-fp32"):
         config, mode = synthetic.CONFIGS[name]
@@ -61,6 +82,7 @@ def main() -> None:
         for e in events:
             ref.step(torch.from_numpy(e))
         want = oracle.hidden()
+        score_drift(name, config, mode, model, c, weights)
         for layer in range(config.layers):
             got = ref.intermediates[f"layers.{layer}.hidden"].float().numpy()
             diff = got - want[layer]
