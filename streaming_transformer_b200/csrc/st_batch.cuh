@@ -111,9 +111,12 @@ __device__ __forceinline__ void btl(const StepArgs& a, BatchSmem& sm, int tag) {
     a.timeline[sm.tl_n++] = (long long)((clock64() << 8) | (long long)tag);
 }
 
-// Round barriers per launch step: one after P0, eight per layer, none after
-// the last R1 (the next round's P0 of a stream runs on the CTA that did its R1).
-__host__ __device__ inline int round_barriers(int layers) { return 8 * layers; }
+// Round barriers per launch step: one after P0, eight per layer (seven when
+// the gate/up epilogue computes SwiGLU), none after the last R1 (the next
+// round's P0 of a stream runs on the CTA that did its R1).
+__host__ __device__ inline int round_barriers(int layers, bool fused_swiglu) {
+  return (fused_swiglu ? 7 : 8) * layers;
+}
 
 // True when the batched round supports this model (host and device).
 __host__ __device__ inline bool batch_supported(int width, int heads, int ffn, int features) {
@@ -131,18 +134,22 @@ __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterp
 // run of N x 128 bytes. fp32 on the tensor cores: tf32 hi and lo planes of 32
 // columns per chunk, the lo plane spad x K floats after the hi plane.
 template <typename T, bool kTc>
-__device__ __forceinline__ void put_z(const StepArgs& a, int s, int k, int K, float v) {
+__device__ __forceinline__ void put_z_at(const StepArgs& a, void* dst, int s, int k, int K, float v) {
   if constexpr (kTc && std::is_same<T, float>::value) {
-    float* z = (float*)a.bz16;
-    const size_t at = umma_tile_offset32((size_t)s, (size_t)k, (size_t)a.spad, (size_t)K / kTileK32);
+    float* z = (float*)dst;
+    const unsigned at = z_tile_offset32((unsigned)s, (unsigned)k, (unsigned)a.spad);
     const float hi = to_tf32(v);
     z[at] = hi;
     z[(size_t)a.spad * K + at] = to_tf32(v - hi);
   } else if constexpr (kTc) {
-    Storage<T>::store((T*)a.bz16, umma_tile_offset((size_t)s, (size_t)k, (size_t)a.spad, (size_t)K / kTileK), v);
+    Storage<T>::store((T*)dst, z_tile_offset((unsigned)s, (unsigned)k, (unsigned)a.spad), v);
   } else {
     a.bz[(size_t)s * K + k] = v;
   }
+}
+template <typename T, bool kTc>
+__device__ __forceinline__ void put_z(const StepArgs& a, int s, int k, int K, float v) {
+  put_z_at<T, kTc>(a, a.bz16, s, k, K, v);
 }
 
 // Two consecutive cache elements (K/V rows are 16-byte aligned, dim even).
@@ -992,7 +999,7 @@ struct TcRoles {
 // oracle where the CUDA-core fp32 round stays within the policy.)
 template <typename T>
 __device__ void tc_gemm_phase(const StepArgs& a, BatchSmem& sm, unsigned char* stages, TcRoles& tr, const T* Wt,
-                              int M, int K, int ksplit, int nu, float* P) {
+                              int M, int K, int ksplit, int nu, float* P, const void* Bsrc, bool swiglu) {
   constexpr bool kX3 = std::is_same<T, float>::value;  // fp32 as three tf32 products
   constexpr int kK = kX3 ? kTileK32 : kTileK;           // K elements per 128-byte chunk row
   const int S = a.streams, spad = a.spad;
@@ -1000,7 +1007,7 @@ __device__ void tc_gemm_phase(const StepArgs& a, BatchSmem& sm, unsigned char* s
   const int sgroups = (spad + nu - 1) / nu;  // nu: streams per unit (MMA N), a multiple of 16
   const int units = mtiles * ksplit * sgroups;
   const int warp = (int)threadIdx.x >> 5, lane = (int)threadIdx.x & 31;
-  const T* Bt = (const T*)a.bz16;
+  const T* Bt = (const T*)Bsrc;
   // tf32 lo planes: weights after the padded hi matrix, inputs after the hi plane
   const size_t wlo = (size_t)mtiles * kUmmaM * K, blo = (size_t)spad * K;
   const unsigned long long tmo = a.bar_timeout_ns;
@@ -1095,10 +1102,31 @@ __device__ void tc_gemm_phase(const StepArgs& a, BatchSmem& sm, unsigned char* s
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] += w[j];
           }
-          if (m < M)
+          if (!kX3 && swiglu) {  // 16-bit only (fp32 keeps its K-split and the SwiGLU phase)
+            // rows 2i (gate) and 2i + 1 (up) are lanes 2i, 2i + 1 of this warp:
+            // act[s][i] = cast(silu(cast(g)) cast(u)) (reference src/cpu/Cpu.cpp:121-127);
+            // the even lane takes columns 0-7 of the 16, the odd lane 8-15
+            float o[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] = __shfl_xor_sync(0xffffffffu, v[j], 1);
+            const bool odd = (lane & 1) != 0;
+            if (m < M) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int jj = odd ? j + 8 : j;
+                const float gv = odd ? o[jj] : v[jj], uv = odd ? v[jj] : o[jj];
+                if (c + jj < live) {
+                  const float g = Storage<T>::round(gv), u = Storage<T>::round(uv);
+                  put_z_at<T, true>(a, a.bz16_act, s0 + c + jj, m >> 1, M >> 1,
+                                    Storage<T>::round((g / (1.0f + expf(-g))) * u));
+                }
+              }
+            }
+          } else if (m < M) {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
               if (c + j < live) out[(size_t)(c + j) * M + m] = v[j];
+          }
         }
         tc_fence_before();
       } else if (lane == 0 && !tr.failed) {
@@ -1158,8 +1186,10 @@ __device__ inline void tc_teardown(const StepArgs& a, BatchSmem& sm, const TcRol
 // One GEMM phase on the CUDA cores or the tensor cores.
 template <typename T, bool kTc, int kView>
 __device__ __forceinline__ void gemm_any(const StepArgs& a, BatchSmem& sm, unsigned char* stages, TcRoles& tr,
-                                         const void* W, const void* Wt, int M, int K, int ksplit, int nu) {
-  if constexpr (kTc) tc_gemm_phase<T>(a, sm, stages, tr, (const T*)Wt, M, K, ksplit, nu, a.bpart);
+                                         const void* W, const void* Wt, int M, int K, int ksplit, int nu,
+                                         const void* Bsrc = nullptr, bool swiglu = false) {
+  if constexpr (kTc)
+    tc_gemm_phase<T>(a, sm, stages, tr, (const T*)Wt, M, K, ksplit, nu, a.bpart, Bsrc ? Bsrc : a.bz16, swiglu);
   else gemm_phase<T, kView>(a, sm, (const T*)W, M, K, ksplit, a.bz, a.bpart);
 }
 
@@ -1190,11 +1220,17 @@ __device__ bool round_batched(const StepArgs& a, BatchSmem& sm, unsigned char* s
     for (int s = blockIdx.x; s < S; s += gridDim.x)
       row_residual<T, kTc>(a, sm, s, a.bx, a.bx2, a.bpart, a.bsplit[1], nullptr, (const T*)w.norm2, false, nullptr);
     if (!sync(kBtlResidual2)) return false;
-    gemm_any<T, kTc, kViewRows>(a, sm, stages, tr, w.gateup, a.tgateup[l], 2 * F, d, a.bsplit[2], a.tc_n[2]);
+    // SwiGLU in the 16-bit gate/up epilogue (no K-split there)
+    const bool fused = kTc && !std::is_same<T, float>::value && a.fuse_swiglu;
+    gemm_any<T, kTc, kViewRows>(a, sm, stages, tr, w.gateup, a.tgateup[l], 2 * F, d, a.bsplit[2], a.tc_n[2],
+                                nullptr, fused);
     if (!sync(kBtlGateUp)) return false;
-    swiglu_phase<T, kTc>(a, a.bsplit[2]);
-    if (!sync(kBtlSwiglu)) return false;
-    gemm_any<T, kTc, kViewColumns>(a, sm, stages, tr, w.down, a.tdown[l], d, F, a.bsplit[3], a.tc_n[3]);
+    if (!fused) {
+      swiglu_phase<T, kTc>(a, a.bsplit[2]);
+      if (!sync(kBtlSwiglu)) return false;
+    }
+    gemm_any<T, kTc, kViewColumns>(a, sm, stages, tr, w.down, a.tdown[l], d, F, a.bsplit[3], a.tc_n[3],
+                                   fused ? a.bz16_act : nullptr);
     if (!sync(kBtlDown)) return false;
     const bool last = l + 1 == L;
     for (int s = blockIdx.x; s < S; s += gridDim.x)

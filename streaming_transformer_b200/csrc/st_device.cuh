@@ -118,6 +118,8 @@ struct StepArgs {
   const void* tgateup[kMaxLayers];
   const void* tdown[kMaxLayers];
   void* bz16;                         // next GEMM input, storage type, tiled [K/64][spad/8][8][8][8]
+  void* bz16_act;                     // the down GEMM's input (SwiGLU output) when the gate/up epilogue makes it
+  int fuse_swiglu;                    // gate/up GEMM without K-split computes SwiGLU in its epilogue
   int spad;                           // streams rounded up to 16 (MMA N granularity)
   int tc_stages;                      // shared-memory stages of the MMA pipeline
   unsigned tc_stage_bytes;            // bytes per stage: A tile 16 KB + B tile (<= 256 streams x 128 B)

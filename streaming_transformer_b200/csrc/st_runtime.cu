@@ -401,7 +401,7 @@ int launch_rounds(st_runtime* rt, const StepArgs& a0, const float* inputs, unsig
   void* params[] = {&a, &inputs, &count, &scores, &base};
   ST_CUDA(rt, cudaLaunchKernel(rounds_fn(rt), dim3(rt->bgrid), dim3(kThreads), params, rt->tc_smem, rt->stream));
   rt->launches += 1;
-  rt->bar_base += count * (unsigned long long)round_barriers(rt->desc.layers) * (unsigned long long)rt->bgrid;
+  rt->bar_base += count * (unsigned long long)round_barriers(rt->desc.layers, rt->args.fuse_swiglu != 0) * (unsigned long long)rt->bgrid;
   return ST_OK;
 }
 
@@ -953,7 +953,14 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
             continue;
           }
           const size_t sg = (spad + n - 1) / n;
-          for (size_t ks = 1; ks <= std::min(K / 64, (size_t)16); ++ks) {
+          // 16-bit gate/up: no K-split, so its epilogue can compute SwiGLU (one
+          // phase and one grid barrier per layer less). fp32 (3xTF32): at most
+          // 512 columns, 64 MMAs, per accumulator: the tensor core's
+          // accumulation of longer runs missed the fp32 bound on B200
+          // (1.2e-5 on one key element at C5-A).
+          const size_t ks_min = planes == 2 ? std::max<size_t>(1, K / 512) : 1;
+          const size_t ks_max = which == 2 && planes == 1 ? 1 : std::min(K / 64, (size_t)16);
+          for (size_t ks = ks_min; ks <= ks_max; ++ks) {
             if (ks > 1 && ks * S * M * 4 > ((size_t)64 << 20)) break;
             const size_t units = mt * sg * ks, waves = (units + rt->bgrid - 1) / rt->bgrid;
             const size_t chunks = (kch + ks - 1) / ks;
@@ -989,6 +996,7 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
   const size_t bz_at = take(rt->batched && !rt->tc ? S * (size_t)std::max(d, F) * 4 : 0), bpart_at = take(bpart_floats * 4);
   // the tensor cores' tiled input: storage type, or tf32 hi and lo planes for fp32
   const size_t bz16_at = take(rt->tc ? spad * (size_t)std::max(d, F) * (m.mode == ST_MODE_FP32 ? 8 : 2) : 0);
+  const size_t bzact_at = take(rt->tc ? spad * (size_t)F * (m.mode == ST_MODE_FP32 ? 8 : 2) : 0);
   const size_t bar_at = take(sizeof(unsigned long long)), err_at = take(sizeof(int));
   const size_t rope_at = take((hd / 2) * sizeof(float)), ctl_at = take(sizeof(Control));
   // flow kernel: choose it and its cluster shape (largest cluster whose
@@ -1138,6 +1146,8 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
   if (rt->tc) {
     // The tensor-core copy of the layer matrices, rows padded to 128 (zeros).
     a.bz16 = rt->scratch + bz16_at;
+    a.bz16_act = rt->scratch + bzact_at;
+    a.fuse_swiglu = rt->bsplit[2] == 1 && m.mode != ST_MODE_FP32 ? 1 : 0;
     auto pad = [](size_t rows) { return (rows + kUmmaM - 1) / kUmmaM * kUmmaM; };
     size_t to = 0;
     const size_t tbytes = m.mode == ST_MODE_FP32 ? 8 : 2;  // fp32: tf32 hi and lo planes
@@ -1709,7 +1719,7 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     << ",\"batched_grid\":" << rt->bgrid << ",\"batched_splits\":[" << rt->bsplit[0] << "," << rt->bsplit[1] << ","
     << rt->bsplit[2] << "," << rt->bsplit[3] << "],\"batched_tc_streams_per_unit\":[" << rt->tcn[0] << ","
     << rt->tcn[1] << "," << rt->tcn[2] << "," << rt->tcn[3] << "],\"batched_barriers_per_round\":"
-    << (rt->batched ? round_barriers(rt->desc.layers) : 0) << ",\"weights_bytes\":" << rt->weights_bytes
+    << (rt->batched ? round_barriers(rt->desc.layers, rt->args.fuse_swiglu != 0) : 0) << ",\"weights_bytes\":" << rt->weights_bytes
     << ",\"state_bytes\":" << rt->state_bytes << ",\"scratch_bytes\":" << rt->scratch_bytes << "}";
   return copy_json(o.str(), json, capacity, needed);
 }

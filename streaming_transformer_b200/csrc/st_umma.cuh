@@ -46,6 +46,16 @@ __host__ __device__ inline size_t umma_tile_offset(size_t r, size_t k, size_t ti
   return tile * tile_rows * kTileK + (((rr >> 3) * 8 + ((k >> 3) & 7)) * 64) + (rr & 7) * 8 + (k & 7);
 }
 
+// Offset of (stream s, column k) in the tiled B operand (one tile of all
+// `spad` rows per 64-column chunk; s < spad): 32-bit arithmetic, no division.
+__host__ __device__ __forceinline__ unsigned z_tile_offset(unsigned s, unsigned k, unsigned spad) {
+  return (k >> 6) * (spad << 6) + ((((s >> 3) << 3) + ((k >> 3) & 7u)) << 6) + ((s & 7u) << 3) + (k & 7u);
+}
+// The same for 32-bit elements (32 columns per chunk).
+__host__ __device__ __forceinline__ unsigned z_tile_offset32(unsigned s, unsigned k, unsigned spad) {
+  return (k >> 5) * (spad << 5) + ((((s >> 3) << 3) + ((k >> 2) & 7u)) << 5) + ((s & 7u) << 2) + (k & 3u);
+}
+
 // The same layout for 32-bit elements (tf32 operands, 32 columns per tile).
 __host__ __device__ inline size_t umma_tile_offset32(size_t r, size_t k, size_t tile_rows, size_t kchunks) {
   const size_t tile = (r / tile_rows) * kchunks + k / kTileK32;
