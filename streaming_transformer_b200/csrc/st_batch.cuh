@@ -79,7 +79,7 @@ __host__ __device__ inline unsigned att_table_bytes(int units, int hd) {
 
 struct BatchSmem {
   float red[kWarps];                              // block reductions (16-byte aligned)
-  union {
+  union __align__(16) {
     AttSmem att[kAttGroups];                      // attention phase (direct loads)
     float zt[kWarps][kBatchStreams * 8];          // GEMM phases: each warp's stream-input tile
     float xs[kMaxCols];                           // row phases: per-stream input vector
@@ -767,13 +767,17 @@ __device__ void attention_phase_staged(const StepArgs& a, BatchSmem& sm, unsigne
 // Head dimension 64 (every benchmark shape): the same per-warp walk as
 // attention_phase_staged, with 16-byte shared-memory reads throughout.
 //  * A row is kNch 16-byte pieces (8 for 16-bit storage, 16 for fp32). A
-//    chunk holds kC = 32 / kG slots; kG lanes take each slot's key dot, two
+//    chunk (one stage, 4 KB of K and V) holds kC slots and is computed in two
+//    passes of kP = 32 / kG slots; kG lanes take each slot's key dot, two
 //    pieces per lane, with this lane's q pieces held in registers.
 //  * 16-bit rows are stored with piece p of row j at p ^ (4 (j & 1)), so the
 //    8 lanes of a quarter-warp (two slots, pieces 0-3 or 4-7) read 8 distinct
 //    bank groups; fp32 quarter-warps read one row's 8 consecutive pieces.
 //  * Value rows: lane (y, c) accumulates piece c of slots y, y + kY, ... into
 //    kVec partial sums; the kY slot groups are summed once per unit.
+//  * The q of the CTA's units (and their retained-slot counts) sit in the
+//    static shared-memory union, idle in this phase, so the dynamic shared
+//    memory holds only the stages (kWarps x a.att_stages x 4 KB).
 //  * The chunk copies start after the q/k/v inserts and a block barrier
 //    (cp.async reads are ordered after it), so the staged rows include the
 //    slot this step writes.
@@ -782,33 +786,39 @@ struct Att64 {
   static constexpr int kVec = Storage<T>::kVec;       // elements per 16-byte piece
   static constexpr int kNch = 64 / kVec;              // pieces per row
   static constexpr int kG = sizeof(T) == 2 ? 4 : 8;   // lanes per slot in the key dot
-  static constexpr int kC = 32 / kG;                  // slots per chunk
+  static constexpr int kP = 32 / kG;                  // slots per pass
+  static constexpr int kC = 2 * kP;                   // slots per chunk (stage)
   static constexpr int kY = 32 / kNch;                // slot groups in the value sums
   static constexpr unsigned kRowBytes = 64u * sizeof(T);
   __device__ static int swz(int row) { return sizeof(T) == 2 ? ((row & 1) << 2) : 0; }
 };
 
+// Bytes of the head-dim-64 phase's q table for `units` units (q in fp32, then
+// each unit's retained-slot count); it must fit the static union.
+__host__ __device__ inline unsigned att64_table_bytes(int units) {
+  return (unsigned)units * (64u * 4u + 4u);
+}
+
 template <typename T, bool kTc>
 __device__ void attention_phase_hd64(const StepArgs& a, BatchSmem& sm, unsigned char* dyn, int l,
                                      unsigned long long event) {
   using A = Att64<T>;
-  constexpr int E = A::kVec, NCH = A::kNch, G = A::kG, C = A::kC, Y = A::kY;
+  constexpr int E = A::kVec, NCH = A::kNch, G = A::kG, P = A::kP, C = A::kC, Y = A::kY;
   const int W = a.window, H = a.heads, S = a.streams, d = a.width, M = 3 * d;
   const int NB = a.att_stages, nch = (W + C - 1) / C;
   int lo, hi;
   split(S * H, (int)blockIdx.x, (int)gridDim.x, lo, hi);
   const int mine = hi - lo;
   if (mine <= 0) return;
-  if (att_table_bytes(mine, 64) > a.att_table_bytes || a.att_chunk != C) {  // the host sized both
+  if (att64_table_bytes(mine) > sizeof(sm.u) || a.att_chunk != C || a.att_buf_bytes != 4096u) {  // host-sized
     if (threadIdx.x == 0) set_error(a, kClusterShape);
     return;
   }
   const int warp = (int)threadIdx.x >> 5, lane = (int)threadIdx.x & 31;
-  constexpr int rowf = 3 * 64;
-  float* table = reinterpret_cast<float*>(dyn);
-  int2* meta = reinterpret_cast<int2*>(dyn + ((unsigned)mine * (unsigned)rowf * 4u + 15u) / 16u * 16u);
-  unsigned char* stages = dyn + a.att_table_bytes;
-  const unsigned sbytes = a.att_buf_bytes, half = sbytes / 2;
+  float* qtab = reinterpret_cast<float*>(&sm.u);                  // [mine][64]
+  int* vtab = reinterpret_cast<int*>(qtab + (size_t)mine * 64);  // [mine] retained slots
+  unsigned char* stages = dyn + (size_t)warp * NB * 4096u;        // this warp's stages
+  constexpr unsigned kHalf = (unsigned)C * A::kRowBytes;          // K, then V
   const int nu = mine > warp ? (mine - 1 - warp) / kWarps + 1 : 0;
   const int total = nu * nch;
   const size_t head_stride = (size_t)W * 64;  // elements per (stream, layer, head) ring
@@ -816,41 +826,47 @@ __device__ void attention_phase_hd64(const StepArgs& a, BatchSmem& sm, unsigned 
     const int u = lo + k, su = u / H, hu = u - su * H;
     return (((size_t)su * a.layers + l) * H + hu) * head_stride;
   };
-  // issue state: the next chunk to copy (unit k_i of this warp's list, chunk c_i)
-  int ik = warp, ic = 0, issued = 0;
-  size_t ibase = nu > 0 ? ring_base(warp) : 0;
-  auto issue = [&]() {  // every lane: its pieces of the next chunk into stage issued % NB, one group
+  // issue state: the next chunk to copy (unit k_i of this warp's list, chunk c_i, stage s_i)
+  int ik = warp, ic = 0, is = 0, issued = 0;
+  const T* ikeys = (const T*)a.keys + (nu > 0 ? ring_base(warp) : 0);
+  const T* ivals = (const T*)a.values + (ikeys - (const T*)a.keys);
+  auto issue = [&]() {  // every lane: its pieces of the next chunk into its stage, one group
     if (issued < total) {
-      unsigned char* dst = stages + (size_t)(warp * NB + issued % NB) * sbytes;
+      unsigned char* dst = stages + (unsigned)is * 4096u;
       const int c0 = ic * C, n = min(C, W - c0);
-      const unsigned char* ks = reinterpret_cast<const unsigned char*>((const T*)a.keys + ibase + (size_t)c0 * 64);
-      const unsigned char* vs = reinterpret_cast<const unsigned char*>((const T*)a.values + ibase + (size_t)c0 * 64);
+      const unsigned char* ks = reinterpret_cast<const unsigned char*>(ikeys + (size_t)c0 * 64);
+      const unsigned char* vs = reinterpret_cast<const unsigned char*>(ivals + (size_t)c0 * 64);
+#pragma unroll 4
       for (int q = lane; q < n * NCH; q += 32) {
         const int row = q / NCH, pc = q - row * NCH;
         const unsigned so = (unsigned)row * A::kRowBytes + (unsigned)pc * 16u;
         const unsigned dp = (unsigned)row * A::kRowBytes + (unsigned)(pc ^ A::swz(row)) * 16u;
         cp_async16(dst + dp, ks + so);
-        cp_async16(dst + half + dp, vs + so);
+        cp_async16(dst + kHalf + dp, vs + so);
       }
       ++issued;
+      is = is + 1 == NB ? 0 : is + 1;
       if (++ic == nch) {
         ic = 0;
         ik += kWarps;
-        if (ik < mine) ibase = ring_base(ik);
+        if (ik < mine) {
+          ikeys = (const T*)a.keys + ring_base(ik);
+          ivals = (const T*)a.values + (ikeys - (const T*)a.keys);
+        }
       }
     }
     cp_async_commit();  // empty past the last chunk: the group count stays uniform
   };
-  // every owned unit's final q, k, v (and the K/V insert), all units at once
+  // every owned unit's final q, k, v (the K/V insert into the ring, q into the table)
   constexpr int per_unit = 3 * 64 / 2;
   for (int x = threadIdx.x; x < mine * per_unit; x += kThreads) {
     const int k = x / per_unit, p = x - k * per_unit;
     const int u = lo + k, su = u / H, hu = u - su * H;
     const unsigned long long t = __ldcg(a.position + su) + event;
     const int row = 2 * p, which = row >> 6, dim = row & 63;
-    const float* P = a.bpart + (size_t)su * M + (size_t)hu * rowf + row;
-    float v0 = Storage<T>::round(sum_splits(P, a.bsplit[0], (size_t)S * M));
-    float v1 = Storage<T>::round(sum_splits(P + 1, a.bsplit[0], (size_t)S * M));
+    const float* Pp = a.bpart + (size_t)su * M + (size_t)hu * 192 + row;
+    float v0 = Storage<T>::round(sum_splits(Pp, a.bsplit[0], (size_t)S * M));
+    float v1 = Storage<T>::round(sum_splits(Pp + 1, a.bsplit[0], (size_t)S * M));
     if (which < 2) {
       const float angle = (float)t * a.rope_freq[dim >> 1];
       const float co = cosf(angle), sn = sinf(angle);
@@ -859,11 +875,12 @@ __device__ void attention_phase_hd64(const StepArgs& a, BatchSmem& sm, unsigned 
       v0 = Storage<T>::round(r0);
       v1 = Storage<T>::round(r1);
     }
-    table[(size_t)k * rowf + row] = v0;
-    table[(size_t)k * rowf + row + 1] = v1;
-    const int slot = (int)(t % (unsigned long long)W);
-    if (p == 0) meta[k] = make_int2(slot, valid_length(t, W));
-    if (which > 0) {
+    if (which == 0) {
+      qtab[(size_t)k * 64 + dim] = v0;
+      qtab[(size_t)k * 64 + dim + 1] = v1;
+      if (dim == 0) vtab[k] = valid_length(t, W);
+    } else {
+      const int slot = (int)(t % (unsigned long long)W);
       T* ring = (T*)(which == 1 ? a.keys : a.values) + ring_base(k);
       Storage<T>::store(ring, (size_t)slot * 64 + dim, v0);
       Storage<T>::store(ring, (size_t)slot * 64 + dim + 1, v1);
@@ -873,10 +890,9 @@ __device__ void attention_phase_hd64(const StepArgs& a, BatchSmem& sm, unsigned 
   btl(a, sm, kBtlAttPrepare);
   for (int i = 0; i < NB - 1; ++i) issue();
   const float rroot = 0.125f;                 // 1 / sqrt(64)
-  const int g = lane / G, r = lane - g * G;   // key dot: slot g of the chunk, pieces r and r + G
+  const int g = lane / G, r = lane - g * G;   // key dot: slot g of a pass, pieces r and r + G
   const int vy = lane / NCH, vc = lane - vy * NCH;  // value sums: slot group vy, piece vc
-  int k = warp, c = 0, s = 0, h = 0, valid = 0;
-  const float* qrow = table;
+  int k = warp, c = 0, cs = 0, s = 0, h = 0, valid = 0;
   float qv[2][E];
   float m = -INFINITY, lsum = 0.f;
   float acc[E];
@@ -885,8 +901,8 @@ __device__ void attention_phase_hd64(const StepArgs& a, BatchSmem& sm, unsigned 
       const int u = lo + k;
       s = u / H;
       h = u - s * H;
-      valid = meta[k].y;
-      qrow = table + (size_t)k * rowf;
+      valid = vtab[k];
+      const float* qrow = qtab + (size_t)k * 64;
 #pragma unroll
       for (int j = 0; j < 2; ++j)
 #pragma unroll
@@ -905,55 +921,62 @@ __device__ void attention_phase_hd64(const StepArgs& a, BatchSmem& sm, unsigned 
     issue();                        // into the stage chunk i - 1 used (read before the warp barrier below)
     cp_async_wait_pending(NB - 1);  // chunk i's group is complete
     __syncwarp();
-    const unsigned char* Kc = stages + (size_t)(warp * NB + i % NB) * sbytes;
-    const unsigned char* Vc = Kc + half;
+    const unsigned char* Kc = stages + (unsigned)cs * 4096u;
+    const unsigned char* Vc = Kc + kHalf;
     const int c0 = c * C, n = min(min(C, W - c0), valid - c0);  // retained slots of this chunk
-    if (n > 0) {
-      const bool ok = g < n;
-      float dot = 0.f;
-      if (ok) {
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int pc = r + G * j;
-          float kf[E];
-          const uint4 w = *reinterpret_cast<const uint4*>(Kc + (unsigned)g * A::kRowBytes +
-                                                          (unsigned)(pc ^ A::swz(g)) * 16u);
-          Storage<T>::unpack(w, kf);
+    for (int po = 0; po < C; po += P) {
+      const int np = n - po;  // retained slots from this pass on (warp-uniform)
+      if (np > 0) {
+        const bool ok = g < np;
+        float dot = 0.f;
+        if (ok) {
+          const int row = po + g;
 #pragma unroll
-          for (int e = 0; e < E; ++e) dot = fmaf(qv[j][e], kf[e], dot);
+          for (int j = 0; j < 2; ++j) {
+            const int pc = r + G * j;
+            float kf[E];
+            const uint4 w = *reinterpret_cast<const uint4*>(Kc + (unsigned)row * A::kRowBytes +
+                                                            (unsigned)(pc ^ A::swz(row)) * 16u);
+            Storage<T>::unpack(w, kf);
+#pragma unroll
+            for (int e = 0; e < E; ++e) dot = fmaf(qv[j][e], kf[e], dot);
+          }
         }
-      }
 #pragma unroll
-      for (int o = 1; o < G; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      const float lg = ok ? dot * rroot : -INFINITY;
-      float mx = lg;
+        for (int o = 1; o < G; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        const float lg = ok ? dot * rroot : -INFINITY;
+        float mx = lg;
 #pragma unroll
-      for (int o = G; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float mn = fmaxf(m, mx);  // finite: the chunk's first slot is retained
-      const float sc = expf(m - mn);
-      const float pj = ok ? expf(lg - mn) : 0.f;
-      float ps = pj;
+        for (int o = G; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float mn = fmaxf(m, mx);  // finite: the pass's first slot is retained
+        const float sc = expf(m - mn);
+        const float pj = ok ? expf(lg - mn) : 0.f;
+        float ps = pj;
 #pragma unroll
-      for (int o = G; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-      lsum = fmaf(lsum, sc, ps);
+        for (int o = G; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+        lsum = fmaf(lsum, sc, ps);
 #pragma unroll
-      for (int e = 0; e < E; ++e) acc[e] *= sc;
+        for (int e = 0; e < E; ++e) acc[e] *= sc;
 #pragma unroll
-      for (int x0 = 0; x0 < C; x0 += Y) {
-        const int x = x0 + vy;
-        const float px = __shfl_sync(0xffffffffu, pj, x * G);  // 0 past the retained slots
-        if (x < n) {
-          float vf[E];
-          const uint4 w = *reinterpret_cast<const uint4*>(Vc + (unsigned)x * A::kRowBytes +
-                                                          (unsigned)(vc ^ A::swz(x)) * 16u);
-          Storage<T>::unpack(w, vf);
+        for (int x0 = 0; x0 < P; x0 += Y) {
+          const int x = x0 + vy;
+          const float px = __shfl_sync(0xffffffffu, pj, x * G);  // 0 past the retained slots
+          if (x < np) {
+            const int row = po + x;
+            float vf[E];
+            const uint4 w = *reinterpret_cast<const uint4*>(Vc + (unsigned)row * A::kRowBytes +
+                                                            (unsigned)(vc ^ A::swz(row)) * 16u);
+            Storage<T>::unpack(w, vf);
 #pragma unroll
-          for (int e = 0; e < E; ++e) acc[e] = fmaf(px, vf[e], acc[e]);
+            for (int e = 0; e < E; ++e) acc[e] = fmaf(px, vf[e], acc[e]);
+          }
         }
+        m = mn;
       }
-      m = mn;
     }
     __syncwarp();  // the stage is read: the next issue may refill it
+    cs = cs + 1 == NB ? 0 : cs + 1;
     if (++c == nch) {
       // the unit's value sums over the slot groups, in a fixed order
 #pragma unroll
@@ -1211,7 +1234,7 @@ __device__ bool round_batched(const StepArgs& a, BatchSmem& sm, unsigned char* s
     const LayerPtrs& w = a.layer[l];
     gemm_any<T, kTc, kViewRows>(a, sm, stages, tr, w.qkv, a.tqkv[l], 3 * d, d, a.bsplit[0], a.tc_n[0]);
     if (!sync(kBtlQkv)) return false;
-    if (a.att_buf_bytes && a.head_dim == 64) attention_phase_hd64<T, kTc>(a, sm, stages, l, event);
+    if (a.att_hd64) attention_phase_hd64<T, kTc>(a, sm, stages, l, event);
     else if (a.att_buf_bytes) attention_phase_staged<T, kTc>(a, sm, stages, l, event);
     else attention_phase<T, kTc>(a, sm, l, event);
     if (!sync(kBtlAttention)) return false;

@@ -128,6 +128,7 @@ struct StepArgs {
   int att_chunk;                      // ring slots per stage (a power of two <= 16)
   int att_stages;                     // stages per warp
   unsigned att_table_bytes;           // the q/k/v table ahead of the stages in dynamic shared memory
+  int att_hd64;                       // staged attention by the head-dim-64 phase (q table in static memory)
 };
 
 // ---------------------------------------------------------------- storage types

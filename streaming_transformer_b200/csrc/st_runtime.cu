@@ -881,8 +881,10 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
     // (the tensor-core GEMM stages reuse the same bytes). C ring slots per
     // stage (a power of two <= 16): the largest C that leaves at least 4
     // stages per warp, else 2 (more stages keep more bytes in flight). At
-    // head_dim 64 the chunk is fixed by the storage type (8 slots of 16-bit
-    // rows, 4 of fp32). ST_ATT_STAGE=0 selects the direct-load attention phase.
+    // head_dim 64, when the CTA's q table fits the static union, the chunk is
+    // fixed by the storage type (16 slots of 16-bit rows, 8 of fp32: 4 KB) and
+    // the dynamic memory holds stages only. ST_ATT_STAGE=0 selects the
+    // direct-load attention phase.
     {
       const char* aenv = std::getenv("ST_ATT_STAGE");
       cudaFuncAttributes fa{};
@@ -893,18 +895,21 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
         return bail(ST_ERR_CUDA);
       const size_t dyn = (size_t)optin > fa.sharedSizeBytes ? ((size_t)optin - fa.sharedSizeBytes) / 1024 * 1024 : 0;
       const int mine = (int)((S * (size_t)m.heads + (size_t)rt->bgrid - 1) / (size_t)rt->bgrid);
-      const unsigned table = att_table_bytes(mine, hd);
+      unsigned table = att_table_bytes(mine, hd);
       int chunk = 0, nb = 0;
-      if (hd == 64) {  // the head-dim-64 phase: fixed chunks, 2 KB stages (as many as fit, >= 2)
-        const int c = rt->elem == 2 ? 8 : 4;
-        const size_t stage = 2ull * (size_t)c * 64u * (size_t)rt->elem;
-        const size_t fit = dyn > table ? (dyn - table) / ((size_t)kWarps * stage) : 0;
+      bool hd64 = false;
+      if (hd == 64 && att64_table_bytes(mine) <= sizeof(BatchSmem::u)) {
+        // the head-dim-64 phase: q table in the static union, 4 KB stages of 16
+        // 16-bit or 8 fp32 slots, as many as fit (>= 2)
+        const size_t fit = dyn / ((size_t)kWarps * 4096u);
         if (fit >= 2) {
-          chunk = c;
+          chunk = rt->elem == 2 ? 16 : 8;
           nb = (int)std::min<size_t>(fit, kAttMaxStages);
+          table = 0;
+          hd64 = true;
         }
       }
-      for (int want = 4; want >= 2 && !chunk && hd != 64; want -= 2)
+      for (int want = 4; want >= 2 && !chunk; want -= 2)
         for (int c = kAttMaxChunk; c >= 1 && !chunk; c /= 2) {
           const size_t stage = 2ull * (size_t)c * (size_t)hd * (size_t)rt->elem;
           const size_t fit = dyn > table ? (dyn - table) / ((size_t)kWarps * stage) : 0;
@@ -919,6 +924,7 @@ static int create_impl(const st_model_desc* model, const st_options* options, in
         rt->args.att_stages = nb;
         rt->args.att_buf_bytes = stage;
         rt->args.att_table_bytes = table;
+        rt->args.att_hd64 = hd64 ? 1 : 0;
         rt->tc_smem = std::max(rt->tc_smem, (size_t)table + (size_t)kWarps * nb * stage);
         if (rt->cuda(cudaFuncSetAttribute(rounds_fn(rt), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rt->tc_smem),
                      "cudaFuncSetAttribute rounds") != ST_OK)
@@ -1714,7 +1720,7 @@ int st_info(st_runtime* rt, char* json, size_t capacity, size_t* needed) {
     << ",\"streams\":" << rt->desc.streams << ",\"batched\":" << (rt->batched ? "true" : "false")
     << ",\"batched_tensor_cores\":" << (rt->tc ? "true" : "false") << ",\"tc_stages\":" << rt->args.tc_stages
     << ",\"tc_stage_bytes\":" << rt->args.tc_stage_bytes << ",\"tc_tmem_columns\":" << rt->args.tc_ncols
-    << ",\"attention_stage_bytes\":" << rt->args.att_buf_bytes << ",\"attention_stage_slots\":" << rt->args.att_chunk << ",\"attention_stages_per_warp\":" << rt->args.att_stages
+    << ",\"attention_stage_bytes\":" << rt->args.att_buf_bytes << ",\"attention_stage_slots\":" << rt->args.att_chunk << ",\"attention_stages_per_warp\":" << rt->args.att_stages << ",\"attention_hd64\":" << rt->args.att_hd64
     << ",\"tiled_weights_bytes\":" << rt->tweights_bytes
     << ",\"batched_grid\":" << rt->bgrid << ",\"batched_splits\":[" << rt->bsplit[0] << "," << rt->bsplit[1] << ","
     << rt->bsplit[2] << "," << rt->bsplit[3] << "],\"batched_tc_streams_per_unit\":[" << rt->tcn[0] << ","
