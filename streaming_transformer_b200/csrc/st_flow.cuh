@@ -169,6 +169,7 @@ enum FlowMark : int {
   kFmAcqWait = 24  // not a phase: cycles spent waiting for ring chunks, inside the phases above
 };
 constexpr int kFlowTags = 32;
+constexpr int kFlowFullGather2 = 16384;  // records per CTA up to which exchange 2 gathers the whole width
 
 struct FlowChunk {
   const char* src;
@@ -769,6 +770,7 @@ struct FlowCtx {
   unsigned long long steps;  // steps this launch has run
   unsigned k[kSites];        // exchanges so far per site (selects buffer and mbarrier phase)
   unsigned bx;               // buffer holding the current x
+  float xss;                 // sum(x^2) of the current x when this CTA computed it whole (-1: from the publish)
 };
 
 // Bounded wait for an exchange phase that had not completed at the first try.
@@ -882,7 +884,8 @@ __device__ __forceinline__ bool flow_head(const StepArgs& a, FlowRing& fr, FlowC
   }
   fmark<kDiag>(a, fr, kFmKvIssue);
   if (first_head) {
-    const float scale = flow_norm_scale(sm.ssx[cx.bx], cx.cs, cx.n, D, a.epsilon);
+    const float scale = cx.xss >= 0.f ? rsqrtf(cx.xss * (1.0f / (float)D) + a.epsilon)
+                                      : flow_norm_scale(sm.ssx[cx.bx], cx.cs, cx.n, D, a.epsilon);
     const float* x = sm.x[cx.bx];
     fmark<kDiag>(a, fr, kFmNormScale);
     flow_gain<T, kDiag>(a, fr, cur, [&](const T* g) {
@@ -1050,6 +1053,7 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
                                    [&](int r, const float (&v)[1]) { sm.seg[r] = Storage<T>::round(v[0]); });
     flow_bsync(fr);
     if (!flow_publish(a, fr, sm, cx, !fr.failed)) return false;
+    cx.xss = -1.f;
     fmark<kDiag>(a, fr, kFmIn);
   }
   for (int l = 0; l < a.layers; ++l) {
@@ -1147,8 +1151,28 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
       }
       fmark<kDiag>(a, fr, kFmDpub);
     }
-    // exchange 2: x[seg] = cast(x'[seg] + cast(sum_c D[c][seg]))
-    {
+    // exchange 2 on one GPU at the Main/Small widths (whole width, no cluster
+    // handoff): x = cast(x' + cast(sum_c D[c])) in every CTA, with its sum of
+    // squares. Measured on B200: C2 102.6 -> 95.6 us per step; at the Large width
+    // (33 clusters x 1024 columns of records per CTA) the segment gather and the
+    // cluster publish below stay faster (356 against 370 us).
+    if (a.tp_size == 1 && (int)cx.nc * D <= kFlowFullGather2) {
+      const unsigned long long* Dq = a.ll_clusters + (size_t)(tag & 1u) * cx.nc * D;
+      const unsigned nb = cx.bx ^ 1u;  // the previous layer's x buffer: free in this layer
+      float ssn = 0.f;
+      const bool ok = flow_gather_full<T, D>(Dq, (int)cx.nc, tag, sm.x2, sm.x[nb], sm.u.red, sm.warp_scratch, &ssn,
+                                             a.error, a.host_error, a.bar_timeout_ns) && dok && ok1 && !fr.failed;
+      fmark<kDiag>(a, fr, kFmGather2);
+      if (cx.score_cluster && (int)threadIdx.x < n) a.hidden[(size_t)l * D + seg0 + threadIdx.x] = sm.x[nb][seg0 + threadIdx.x];
+      cx.bx = nb;
+      cx.xss = ssn;
+      // A CTA whose wait ran out leaves the step here; its cluster peers find out
+      // at their next exchange with it (bounded) and every CTA meets at the
+      // cluster barrier before the kernel ends.
+      if (!ok) return false;
+      fmark<kDiag>(a, fr, kFmPub1);
+    } else {
+      // exchange 2 over several GPUs: x[seg] = cast(x'[seg] + cast(sum_c D[c][seg]))
       const unsigned long long* Dq = a.ll_clusters + (size_t)(tag & 1u) * cx.nc * D;
       bool ok = flow_gather<D>(a, fr, Dq, (int)cx.nc, seg0, n, tag, sm) && dok && ok1;
       if (a.tp_size > 1) {
@@ -1172,12 +1196,14 @@ __device__ __forceinline__ bool flow_step(const StepArgs& a, FlowRing& fr, FlowC
       }
       flow_bsync(fr);
       if (!flow_publish(a, fr, sm, cx, ok && !fr.failed)) return false;
+      cx.xss = -1.f;
       fmark<kDiag>(a, fr, kFmPub1);
     }
   }
   // final RMSNorm and score head (no cast), by the score CTA
   if (cx.score_cluster && cx.rank == 0) {
-    const float scale = flow_norm_scale(sm.ssx[cx.bx], cx.cs, n, D, a.epsilon);
+    const float scale = cx.xss >= 0.f ? rsqrtf(cx.xss * (1.0f / (float)D) + a.epsilon)
+                                      : flow_norm_scale(sm.ssx[cx.bx], cx.cs, n, D, a.epsilon);
     const float* x = sm.x[cx.bx];
     float acc = 0.f;
     for (int i = threadIdx.x; i < D; i += kThreads)
@@ -1225,6 +1251,7 @@ __device__ __forceinline__ void flow_run(const StepArgs& a, const FlowLaunch& f,
   cx.seg0 = (int)cx.rank * cx.n;
   cx.heads_here = (int)cx.id < a.heads / a.tp_size;
   cx.score_cluster = cx.id == cx.nc - 1;
+  cx.xss = -1.f;
   cx.epoch = ld_cg_u64(a.flow_epoch);
   cx.steps = 0;
   for (int i = 0; i < kSites; ++i) cx.k[i] = 0;
