@@ -729,7 +729,7 @@ __device__ __forceinline__ bool flow_gather_full(const unsigned long long* rec, 
 #pragma unroll
       for (int k = 0; k < 8; ++k) ready = ready && ll_tag(r[k][0]) == tag && ll_tag(r[k][1]) == tag;
       if (ready) break;
-      __nanosleep(64);
+
       if ((++polls & 31u) == 0) {
         if (ld_volatile_int(error) != 0) { ok = false; break; }
         const unsigned long long now = globaltimer();
