@@ -1334,14 +1334,20 @@ __device__ __forceinline__ void flow_run(const StepArgs& a, const FlowLaunch& f,
             if (globaltimer() - start >= p.idle_ns) { cmd = kFlowExit; break; }
             if (p.backoff) __nanosleep(128);
           }
-          if (cmd == 0) {
+        }
+        cmd = __shfl_sync(0xffffffffu, cmd, 0);
+        if (cmd == 0) {
+          // a request arrived: its input (one float per lane), command and
+          // argument are read together, one round trip over the host link
+          static_assert(kFlowFeatures == 32, "one input feature per lane");
+          const float v = __ldcv(f.mapped_input + lane);
+          if (lane == 0) {
             cmd = *reinterpret_cast<volatile int*>(&p.mailbox->command);
             carg = *reinterpret_cast<volatile int*>(&p.mailbox->arg);
           }
+          cmd = __shfl_sync(0xffffffffu, cmd, 0);
+          if (cmd == kRun) const_cast<float*>(a.input)[lane] = v;
         }
-        cmd = __shfl_sync(0xffffffffu, cmd, 0);
-        if (cmd == kRun)
-          for (int i = lane; i < kFlowFeatures; i += 32) const_cast<float*>(a.input)[i] = __ldcv(f.mapped_input + i);
         __syncwarp();
         if (lane == 0) {
           if (cmd != kFlowExit) {
