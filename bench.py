@@ -104,6 +104,17 @@ def streams_per_rank(total, world):
     return total // world
 
 
+def rank_streams(rank, S):
+    """Global ids of the streams rank `rank` steps when every rank steps S: rank * S + s.
+    Stream g's events come from seed seed_base + g, the same at any GPU count."""
+    return [rank * S + s for s in range(S)]
+
+
+def aggregate_rate(world, S, steps, max_elapsed):
+    """Whole-job rate: every rank's S streams x steps over the slowest rank's time."""
+    return world * S * steps / max_elapsed
+
+
 def config_json(args, config, mode, working_set, world=1):
     total = max(1, args.streams)
     s = streams_per_rank(total, world)
@@ -317,8 +328,8 @@ def run_rounds(model, config, S, rank, warm, timed, local, seed_base):
     windows), then `timed` rounds continuing from that state. Returns
     (us per round, kernels launched in the timed region, runtime info)."""
     import torch
-    events = np.stack([synthetic.make_events(warm + timed, config.features, seed=seed_base + rank * S + s)
-                       for s in range(S)], axis=1)
+    events = np.stack([synthetic.make_events(warm + timed, config.features, seed=seed_base + g)
+                       for g in rank_streams(rank, S)], axis=1)
     dev = torch.from_numpy(np.ascontiguousarray(events)).cuda()
     rt = Runtime(model, RuntimeOptions(backend=Backend.FUSED, blocks=0, device=local), streams=S)
     try:
@@ -396,7 +407,7 @@ def run_b200(args):
     # Untimed device steps before the timed region: at least a full window.
     Wd = max(W, config.window)
     # stream g = rank * S + s has its own seeded trace
-    events = np.stack([synthetic.make_events(K + Wd, config.features, seed=123 + rank * S + s) for s in range(S)],
+    events = np.stack([synthetic.make_events(K + Wd, config.features, seed=123 + g) for g in rank_streams(rank, S)],
                       axis=1)  # [K + Wd, S, features]
     e2e_lat = []
     with ClockSampler(local) as clocks:
@@ -455,7 +466,7 @@ def run_b200(args):
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    value = world * S * K / max_elapsed
+    value = aggregate_rate(world, S, K, max_elapsed)
     peak, peak_src = measured_peak()
     alg = metrics.trace_bytes(config, mode, K, start=Wd, streams=S)
     achieved = alg / K / (us * 1e-6) / 1e9
@@ -469,7 +480,7 @@ def run_b200(args):
         "config": config_json(args, config, mode, ws, world),
         "mean_us_per_step_device": us,
         "device_warmup_steps": Wd,
-        "e2e": {"value": world * S * K / max_e2e, "unit": "steps/s", "h2d_bytes_per_step": 4 * config.features * S,
+        "e2e": {"value": aggregate_rate(world, S, K, max_e2e), "unit": "steps/s", "h2d_bytes_per_step": 4 * config.features * S,
                 "d2h_bytes_per_step": 4 * S, "p50_us": metrics.nearest_rank(e2e_lat, 0.5),
                 "p99_us": metrics.nearest_rank(e2e_lat, 0.99),
                 "path": ("Runtime.step -> st_step, persistent mailbox, mapped pinned input/score, host clock"
@@ -489,7 +500,7 @@ def run_b200(args):
     }
     if c4:
         c4_us, c4_K, c4_S, c4_launches, c4_info, c4_config, c4_mode = c4
-        c4_value = world * c4_S * c4_K / maxed[2]
+        c4_value = aggregate_rate(world, c4_S, c4_K, maxed[2])
         roof, per_gpu_bytes = c4_roofline(world, peak)
         line["c4"] = {
             "workload": (f"c4-large-bf16: 256 streams in total, {c4_S} per GPU on {world} GPU(s), d1024 L12 H16 "
