@@ -453,10 +453,18 @@ def run_b200(args):
             barrier()
             c4 = (c4_us, c4_K, c4_S, c4_launches, c4_info, c4_config, c4_mode)
         c5b = None
+        c5b_error = None
         if world > 1 and not args.no_c5b:
             c5b_K = max(1, min(K, args.c5b_steps))
             barrier()
-            c5b = run_tp_stream(world, rank, local, c5b_K, host) + (c5b_K,)
+            try:
+                c5b = run_tp_stream(world, rank, local, c5b_K, host) + (c5b_K,)
+            except Exception as exc:  # the C5-B record must not take the bench line with it
+                c5b_error = f"{type(exc).__name__}: {exc}"[:400]
+            # every rank keeps the record only when every rank's run succeeded
+            if combine_ranks([0.0 if c5b else 1.0], dist, host)[0] > 0:
+                c5b = None
+                c5b_error = c5b_error or "the C5-B run failed on another rank"
             barrier()
     elapsed_s = us * K / 1e6
     times = [elapsed_s, e2e_wall] + ([c4[0] * c4[1] / 1e6] if c4 else []) + ([c5b[0]] if c5b else [])
@@ -528,6 +536,9 @@ def run_b200(args):
             "exchanges": "out-projection records and down sums stored into every GPU's buffers over NVLink, "
                          "polled locally (no collective library on the step path)",
         }
+    if c5b_error:
+        line["c5b"] = {"workload": f"c5-large-fp32 phase B: one stream tensor-parallel over {world} GPUs",
+                       "error": c5b_error}
     if world == 1 and not args.no_cpu_baseline:
         sps, n, dt = time_cpu_oracle(model, events[:, 0], 1, args.cpu_seconds, K)
         line["cpu_baseline"] = {
