@@ -302,6 +302,21 @@ def run_reference(args):
     return 0
 
 
+def guarded_on_all_ranks(run, dist=None, group=None):
+    """(result, error) of run() on every rank; the result is kept only when
+    every rank's run succeeded, so all ranks report the same outcome (a failed
+    record must not end the bench line, nor leave the ranks disagreeing)."""
+    result, error = None, None
+    try:
+        result = run()
+    except Exception as exc:
+        error = f"{type(exc).__name__}: {exc}"[:400]
+    if combine_ranks([0.0 if result else 1.0], dist, group)[0] > 0:
+        result = None
+        error = error or "the run failed on another rank"
+    return result, error
+
+
 def combine_ranks(values, dist=None, group=None):
     """Max over ranks of each host-side timing (a CPU tensor over the host
     group); identity on one process."""
@@ -457,14 +472,8 @@ def run_b200(args):
         if world > 1 and not args.no_c5b:
             c5b_K = max(1, min(K, args.c5b_steps))
             barrier()
-            try:
-                c5b = run_tp_stream(world, rank, local, c5b_K, host) + (c5b_K,)
-            except Exception as exc:  # the C5-B record must not take the bench line with it
-                c5b_error = f"{type(exc).__name__}: {exc}"[:400]
-            # every rank keeps the record only when every rank's run succeeded
-            if combine_ranks([0.0 if c5b else 1.0], dist, host)[0] > 0:
-                c5b = None
-                c5b_error = c5b_error or "the C5-B run failed on another rank"
+            c5b, c5b_error = guarded_on_all_ranks(
+                lambda: run_tp_stream(world, rank, local, c5b_K, host) + (c5b_K,), dist, host)
             barrier()
     elapsed_s = us * K / 1e6
     times = [elapsed_s, e2e_wall] + ([c4[0] * c4[1] / 1e6] if c4 else []) + ([c5b[0]] if c5b else [])

@@ -82,6 +82,43 @@ def test_stream_partition_over_two_gloo_ranks():
         assert v0 == v1 == 2 * 128 * 100 / 0.75
 
 
+def _guarded_rank(rank, world, port, fail_rank, out):
+    import torch.distributed as dist
+    import bench
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        def run():
+            if rank == fail_rank:
+                raise RuntimeError("device wait ran out")
+            return (1.0, rank)
+        out[rank] = bench.guarded_on_all_ranks(run, dist, None)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_rank", [-1, 1])
+def test_a_failed_record_is_dropped_on_every_rank(fail_rank):
+    """The C5-B record's guard: when one rank's run raises, every rank drops the
+    record and reports an error (the failing rank its own message); when none
+    fails, every rank keeps its result."""
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        out = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_guarded_rank, args=(r, 2, port, fail_rank, out)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+        assert all(p.exitcode == 0 for p in procs)
+        if fail_rank < 0:
+            assert out[0] == ((1.0, 0), None) and out[1] == ((1.0, 1), None)
+        else:
+            assert out[0] == (None, "the run failed on another rank")
+            assert out[1] == (None, "RuntimeError: device wait ran out")
+
+
 def test_partition_matches_one_gpu_and_rejects_uneven_splits():
     import bench
     assert bench.rank_streams(0, 256) == list(range(256))  # one GPU: the same stream ids
